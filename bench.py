@@ -1,0 +1,368 @@
+"""Benchmark of the batched environment step on B200, one JSON line per run.
+
+Workload: Acrobot batched step, N = 262,144 environments per
+GPU, 1,000 environment steps per bench step, actions uniform over {0, 1, 2} drawn once
+from a seeded generator and resident in HBM, initial state uniform in +-0.1.
+
+One bench step is one launch of the T-step Acrobot kernel over the whole batch: the state
+stays in registers for the 1,000 steps; every step reads one action byte per environment
+and writes the reward (float32) and done flag (byte) of every environment to (T, N)
+buffers, with the terminated environments reset from the in-kernel hash stream. Inputs
+and outputs (262 MB of actions, 1.3 GB of rewards and flags per step) are larger than
+the 126 MB L2, so nothing is served from L2 across steps.
+
+  value  env steps/s of the whole job: N x 1000 x K x world / max-over-ranks device time
+  e2e    the same metric through the public API (acrobot_metal.step_many) with host
+         buffers: each step copies the state and the actions from pinned host memory and
+         reads back the final state and the per-environment reward sum and done count
+  roofline  the step kernel against the FP32 issue roofline (algorithmic flops from
+         rlenv_flops.py over CUDA-event time; peak = cuBLAS SGEMM measured in this run,
+         TF32 off) with the HBM view beside it
+  cpu_baseline  the numpy oracle port of the reference's acrobot_np.step loop on the
+         host cores (rank 0, N = 1 only), a bounded sample
+
+`--impl reference` times the reference's CPU implementation of the path (the oracle
+port of acrobot_np.step, the reference's own numpy code restated) on all host cores
+and prints the same line with "impl": "reference".
+
+Multi-GPU (torchrun): every rank steps its own 262,144 environments (global indices
+offset by rank, so each rank draws its own resets); there is no collective on the data
+path, only barriers and one max-reduction of the elapsed time. Weak scaling.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+PKG = ROOT / "metal-rl-envs_b200"
+sys.path.insert(0, str(PKG))
+
+N_ENVS = 262_144
+T_STEPS = 1000
+METRIC = "env steps/s"
+WORKLOAD = "acrobot_batched_step"
+
+
+def parse():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--n", type=int, default=N_ENVS, help="environments per GPU")
+    p.add_argument("--t", type=int, default=T_STEPS, help="environment steps per bench step")
+    p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+# ---- the CPU arm: the oracle port of the reference's numpy step loop ------------------------------
+
+def _cpu_worker(args):
+    """Step n environments of the numpy Acrobot (physics, termination, numpy-RNG reset: the shape of
+    acrobot_np.step) for `steps` steps; returns the elapsed seconds."""
+    n, steps, seed = args
+    import os as _os
+
+    _os.environ.setdefault("OMP_NUM_THREADS", "1")
+    sys.path.insert(0, str(ROOT))
+    from oracle import classic
+
+    rng = np.random.default_rng(seed)
+    state = rng.uniform(-0.1, 0.1, size=(4, n)).astype(np.float32)
+    acts = rng.integers(0, 3, size=(steps, n))
+    t0 = time.perf_counter()
+    for t in range(steps):
+        stepped = classic.acrobot_physics(state, acts[t])
+        done = classic.acrobot_terminated(stepped)
+        fresh = rng.uniform(-0.1, 0.1, size=(4, n)).astype(np.float32)
+        state = np.where(done[None, :], fresh, stepped)
+        classic.acrobot_reward(done)
+    return time.perf_counter() - t0
+
+
+def cpu_throughput(n, budget_s, processes):
+    """(steps/s, sample description, cores) of the numpy step loop on `processes` host processes,
+    the batch sharded across them, sized to about budget_s seconds of wall time."""
+    import multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    per = max(1, n // processes)
+    # calibrate on one process with a short run
+    probe = _cpu_worker((per, 3, 0))
+    steps = max(3, min(T_STEPS, int(budget_s / max(probe / 3, 1e-6))))
+    with ctx.Pool(processes) as pool:
+        secs = pool.map(_cpu_worker, [(per, steps, r) for r in range(processes)])
+    total = per * processes * steps
+    sample = f"N={per * processes} environments ({processes} shards of {per}), {steps} steps, numpy {np.__version__}"
+    return total / max(secs), sample, processes
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cores = len(os.sched_getaffinity(0))
+    vals = []
+    for _ in range(args.warmup):
+        cpu_throughput(args.n, 2.0, cores)
+    sample = ""
+    for _ in range(args.steps if args.steps <= 5 else 3):
+        v, sample, _ = cpu_throughput(args.n, args.cpu_seconds / 3, cores)
+        vals.append(v)
+    value = statistics.median(vals)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "env steps/s", "n_gpus": args.gpus,
+            "steps": len(vals), "warmup": args.warmup, "ms_per_step": 1e3 * args.n * args.t / value,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded uniform states and actions)",
+            "config": {"workload": WORKLOAD, "n_envs": args.n, "env_steps_per_step": args.t,
+                       "note": "the reference's numpy step (acrobot_np.step) restated in oracle/; each step a "
+                               "bounded sample of the workload"},
+            "cpu_baseline": {"value": value, "unit": "env steps/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "env steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---- GPU helpers ---------------------------------------------------------------------------------
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.rows = []
+        self._stop = threading.Event()
+        self._thread = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+                for line in out.stdout.strip().splitlines():
+                    self.rows.append([x.strip() for x in line.split(",")])
+            except Exception:
+                return
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        self._thread.join(timeout=10)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if len(r) > 5 + i and "Active" in r[5 + i]
+                          and "Not" not in r[5 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(self.rows[0][2]) if self.rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def measured_sgemm_tflops(torch):
+    """cuBLAS fp32 GEMM throughput with TF32 off: the measured FP32 FMA ceiling used for the roofline."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        n = 8192
+        a = torch.randn(n, n, device="cuda")
+        b = torch.randn(n, n, device="cuda")
+        for _ in range(2):
+            a @ b
+        torch.cuda.synchronize()
+        best = float("inf")
+        for _ in range(5):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            a @ b
+            e.record()
+            e.synchronize()
+            best = min(best, s.elapsed_time(e) / 1e3)
+        return 2 * n ** 3 / best / 1e12
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+def hbm_peak_gbs():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return float(json.loads(path.read_text())["hbm_gbs"]), "measured (MEASURED_PEAKS.json)"
+    return 6650.0, "fallback"
+
+
+def profiled_traffic():
+    """DRAM bytes per launch of the step kernel from the committed ncu summary, if present."""
+    f = ROOT / "profiles" / "acrobot_step_many_n262144_t1000.md"
+    if f.exists():
+        for line in f.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].strip().split()[0])
+    return None
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    import acrobot_metal
+    import rlenv_flops
+    import rlenv_lib as rl
+
+    lib = rl.load()
+    n, T = args.n, args.t
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    actions = torch.randint(0, 3, (T, n), device=dev, generator=g, dtype=torch.int64).to(torch.uint8)
+    state0 = rl.reset_uniform(4, n, 0.1, seed=99, index_offset=rank * n, dev=dev)
+    state = torch.empty_like(state0)
+    rew = torch.empty((T, n), device=dev)
+    dn = torch.empty((T, n), device=dev, dtype=torch.bool)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    off = rank * n
+
+    def launch(seed0):
+        rl.check(lib.acrobot_step_many(state0.data_ptr(), actions.data_ptr(), rl.U8, seed0, T, n, off, state.data_ptr(),
+                                       rew.data_ptr(), dn.data_ptr(), 0, 0, sp))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for w in range(args.warmup):
+        launch(1 + w * T)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for k in range(args.steps):
+            launch(1 + (args.warmup + k) * T)
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    secs = start.elapsed_time(end) / 1e3
+    t = torch.tensor([secs], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    secs_max = float(t.item())
+    per_launch = secs / args.steps
+    value = world * n * T * args.steps / secs_max
+
+    # ---- e2e through the public API with host buffers --------------------------------------------
+    pin_state = state0.cpu().pin_memory()
+    pin_actions = actions.cpu().pin_memory()
+    out_state = torch.empty((4, n), pin_memory=True)
+    out_sum = torch.empty(n, pin_memory=True)
+    out_cnt = torch.empty(n, pin_memory=True)
+
+    def e2e_step():
+        s_dev = pin_state.to(dev, non_blocking=True)
+        a_dev = pin_actions.to(dev, non_blocking=True)
+        fin, _, _, rsum, dcnt = acrobot_metal.step_many(s_dev, a_dev, sums=True)
+        out_state.copy_(fin, non_blocking=True)
+        out_sum.copy_(rsum, non_blocking=True)
+        out_cnt.copy_(dcnt, non_blocking=True)
+
+    for _ in range(max(1, args.warmup // 2)):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_steps = max(3, args.steps // 10)
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    t2 = torch.tensor([s2.elapsed_time(e2) / 1e3], device=dev)
+    if world > 1:
+        dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+    e2e_value = world * n * T * e2e_steps / float(t2.item())
+
+    # ---- roofline of the step kernel -----------------------------------------------------------------
+    flops = rlenv_flops.ACROBOT["flops"] * n * T
+    sgemm = measured_sgemm_tflops(torch) if rank == 0 else None
+    bytes_per_launch = rlenv_flops.step_many_bytes(4, n, T, 1, True)
+    hbm, hbm_kind = hbm_peak_gbs()
+    traffic = profiled_traffic()
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        v, sample, cores = cpu_throughput(n, args.cpu_seconds, 1)
+        cpu = {"value": v, "unit": "env steps/s", "cores": cores, "kind": "port",
+               "sample": sample + " (single thread, as the reference reports numpy)"}
+    achieved = flops / per_launch / 1e12
+    line = {
+        "metric": METRIC, "value": value, "unit": "env steps/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * secs_max / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded uniform states, uniform actions in {0,1,2})",
+        "config": {"workload": WORKLOAD, "n_envs_per_gpu": n, "env_steps_per_step": T,
+                   "kernel": "rlenv_acrobot_step_many (state in registers, per-step rewards and dones to HBM)",
+                   "l2": "inputs and outputs larger than L2 (actions 262 MB, rewards+dones 1.3 GB per step)",
+                   "parallelism": f"env-sharded x{world}, no data-path collective"},
+        "roofline": {"bound": "fp32", "achieved": achieved, "peak": sgemm, "unit": "TFLOP/s",
+                     "frac": achieved / sgemm if sgemm else None,
+                     "peak_kind": "cuBLAS SGEMM (TF32 off) measured in this run; nominal FP32 FMA 74.4 TFLOP/s",
+                     "flops_per_env_step": rlenv_flops.ACROBOT["flops"],
+                     "transcendentals_per_env_step": rlenv_flops.ACROBOT["transcendentals"],
+                     "traffic": traffic, "algorithmic_bytes_per_launch": bytes_per_launch,
+                     "hbm": {"achieved": bytes_per_launch / per_launch / 1e9, "peak": hbm, "unit": "GB/s",
+                             "frac": bytes_per_launch / per_launch / 1e9 / hbm, "peak_kind": hbm_kind},
+                     "launch_ms": per_launch * 1e3},
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e_value, "unit": "env steps/s", "h2d_bytes_per_step": 4 * 4 * n + T * n,
+                "d2h_bytes_per_step": 4 * 4 * n + 8 * n, "api": "acrobot_metal.step_many", "steps": e2e_steps},
+        "gpu_launches": args.steps,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,217 @@
+/*
+ * rlenv.h — C ABI of librlenv.so, the sm_100a CUDA implementation of the batched
+ * environment step kernels and the fused Evolution Strategies rollouts of
+ * metal-rl-envs.
+ *
+ * Every entry point replaces one `mx.fast.metal_kernel` of the reference (its
+ * file:line is given beside each declaration). The conventions are the same for all:
+ *
+ *  - State is structure-of-arrays, row-major (D, N) float32: row r of
+ *    environment i is state[r * N + i]. Every pointer is a device pointer
+ *    unless its comment says otherwise.
+ *  - The caller allocates every buffer. The library never allocates or frees
+ *    memory and holds no state between calls.
+ *  - Work is enqueued asynchronously on `stream` (a cudaStream_t; NULL is the
+ *    legacy default stream). Calls are reentrant.
+ *  - Inputs are never written. Outputs must not alias inputs except where a
+ *    comment says so.
+ *  - The return value is 0 on success, a negative RLENV_E* code for an argument
+ *    that the library rejects before launching anything, or a positive
+ *    cudaError_t from the launch. Nothing aborts or traps.
+ *  - `seed` is the per-call counter of the reference (`_calls`, incremented
+ *    before every step call, cartpole_metal.py:106-125). A terminated
+ *    environment i is reset from pcg_hash(seed ^ ((i + index_offset) *
+ *    0x9E3779B9)) plus a per-row offset, so that a shard starting at global
+ *    environment `index_offset` draws exactly the resets the unsharded batch
+ *    would.
+ *  - Actions are integer arrays of N elements whose element type is given by
+ *    `action_dtype` (RLENV_I32, RLENV_I64 or RLENV_U8).
+ *  - `done` is one byte per environment, 0 or 1 (torch.bool layout).
+ */
+#ifndef RLENV_H
+#define RLENV_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define RLENV_API __attribute__((visibility("default")))
+#else
+#define RLENV_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes and dtypes ------------------------------------------- */
+#define RLENV_OK 0
+#define RLENV_EINVAL (-1)       /* a null pointer, a negative size, an unknown dtype        */
+#define RLENV_EUNSUPPORTED (-2) /* a (K, C, H, ...) for which no kernel instance is built  */
+
+#define RLENV_I32 0
+#define RLENV_I64 1
+#define RLENV_U8 2
+
+/* Human-readable message for a status code; the string is static. */
+RLENV_API const char* rlenv_strerror(int code);
+
+/* Version of this ABI: bumped whenever a signature below changes. */
+RLENV_API int rlenv_abi_version(void);
+
+/* ---- CartPole ------------------------------------------------------------
+ * Replaces `cartpole_step` (cartpole_metal.py:69-104, launched at :114-125).
+ * state (4, n) rows x, x_dot, theta, theta_dot; action 1 pushes right, anything
+ * else left; reward 1 for every environment; done when |x| > 2.4 or
+ * |theta| > 12 degrees, after which the column is reset uniformly in +-0.05.
+ */
+RLENV_API int rlenv_cartpole_step(const float* state, const void* action, int action_dtype,
+                        uint32_t seed, int64_t n, int64_t index_offset,
+                        float* next_state, float* reward, uint8_t* done, void* stream);
+
+/* T consecutive CartPole steps in one launch, the state held in registers.
+ * No reference counterpart: it is what a chain of T `step` calls computes
+ * (cartpole_metal.py:114-125 called T times), with step t using the per-call
+ * seed seed0 + t. actions (T, n); reward_seq (T, n) and done_seq (T, n) may be
+ * NULL; reward_sum and done_count (n) may be NULL and, when given, receive the
+ * per-environment sums over the T steps. state_out may equal state_in. */
+RLENV_API int rlenv_cartpole_step_many(const float* state_in, const void* actions, int action_dtype,
+                             uint32_t seed0, int64_t steps, int64_t n, int64_t index_offset,
+                             float* state_out, float* reward_seq, uint8_t* done_seq,
+                             float* reward_sum, float* done_count, void* stream);
+
+/* ---- Acrobot -------------------------------------------------------------
+ * Replaces `acrobot_step` (acrobot_metal.py:24-111). state (4, n) rows theta1,
+ * theta2, dtheta1, dtheta2; action in {0, 1, 2} is torque action - 1; RK4 with
+ * dt 0.2; reward -1, or 0 on the terminating step; reset uniform in +-0.1. */
+RLENV_API int rlenv_acrobot_step(const float* state, const void* action, int action_dtype,
+                       uint32_t seed, int64_t n, int64_t index_offset,
+                       float* next_state, float* reward, uint8_t* done, void* stream);
+
+/* T Acrobot steps per launch; same contract as rlenv_cartpole_step_many. */
+RLENV_API int rlenv_acrobot_step_many(const float* state_in, const void* actions, int action_dtype,
+                            uint32_t seed0, int64_t steps, int64_t n, int64_t index_offset,
+                            float* state_out, float* reward_seq, uint8_t* done_seq,
+                            float* reward_sum, float* done_count, void* stream);
+
+/* ---- K-link pendulum -----------------------------------------------------
+ * state (2k, n): k absolute angles then k angular velocities; action in
+ * {0, 1, 2} is a root torque of action - 1; RK4 with dt 0.02; reward -1, or 0 on
+ * the terminating step; reset uniform in +-0.1 on all 2k rows.
+ *
+ * Mass-matrix form, one thread per environment. Replaces `pendulum{K}_step`
+ * and its `_pairwise` variant (pendulum_metal.py:11-131). pairwise_trig != 0
+ * evaluates cos and sin of every angle difference directly instead of by the
+ * addition formulas. Built for k in 1..16. */
+RLENV_API int rlenv_pendulum_mm_step(int k, int pairwise_trig, const float* state, const void* action,
+                           int action_dtype, uint32_t seed, int64_t n, int64_t index_offset,
+                           float* next_state, float* reward, uint8_t* done, void* stream);
+
+/* Mass-matrix form with k lanes of a warp per environment, lane j owning row j
+ * of the mass matrix. Replaces `pendulum{K}_coop_step`
+ * (pendulum_metal_coop.py:28-149). k in {2, 4, 8, 16, 32}. */
+RLENV_API int rlenv_pendulum_coop_step(int k, const float* state, const void* action, int action_dtype,
+                             uint32_t seed, int64_t n, int64_t index_offset,
+                             float* next_state, float* reward, uint8_t* done, void* stream);
+
+/* Articulated-body (Featherstone) form, O(k) per stage, one thread per
+ * environment. Replaces `pendulum{K}_aba_step` (pendulum_aba_metal.py:14-144).
+ * Built for k in 1..16, 24, 32, 48, 64. */
+RLENV_API int rlenv_pendulum_aba_step(int k, const float* state, const void* action, int action_dtype,
+                            uint32_t seed, int64_t n, int64_t index_offset,
+                            float* next_state, float* reward, uint8_t* done, void* stream);
+
+/* ---- Hopper and legged bodies ---------------------------------------------
+ * Legged body with c legs and c hard contacts (legged_metal.py:13-185):
+ * state (2(3+c), n) = q then q_dot with q = (x, y, phi, psi_1..psi_c); action in
+ * [0, 3^c) decoded per leg to a torque ((a / 3^leg) % 3 - 1) * 2; 4 substeps of
+ * 0.01 with `iters` block projected Gauss-Seidel sweeps over the contacts;
+ * reward x_dot + 1, or 0 on the terminating step; done when y < 0.6 or
+ * |phi| > 1; reset to stand (2(3+c) floats, device) plus uniform +-0.05 on every
+ * row. assist_ptr (device, one float) overrides `assist` when not NULL: it is
+ * the stiffness of the torso-upright spring-damper of the curriculum.
+ * Built for c in 1..4; iters >= 1. */
+RLENV_API int rlenv_legged_step(int c, int iters, const float* state, const void* action, int action_dtype,
+                      uint32_t seed, const float* stand, float assist, const float* assist_ptr,
+                      int64_t n, int64_t index_offset,
+                      float* next_state, float* reward, uint8_t* done, void* stream);
+
+/* Hopper: the one-legged body with an exact single-contact solve, equal to the
+ * legged body with c = 1 and one sweep. Replaces `hopper_step` and
+ * `hopper_step_branchy` (hopper_metal.py:13-138): branchy != 0 skips the
+ * contact solve of airborne environments with a branch instead of a select.
+ * state (8, n); stand as for rlenv_legged_step. */
+RLENV_API int rlenv_hopper_step(int branchy, const float* state, const void* action, int action_dtype,
+                      uint32_t seed, const float* stand, int64_t n, int64_t index_offset,
+                      float* next_state, float* reward, uint8_t* done, void* stream);
+
+/* ---- Fused ES rollouts ------------------------------------------------------
+ * One launch runs a whole population: member i runs its own MLP policy from
+ * parameter row theta + i * theta_stride (theta_stride 0 shares one row) against
+ * its own environment from column i of state (D, p) until its first
+ * termination or `horizon` steps. Rows are es.unflatten's layout: w1 (obs, h)
+ * row-major, b1 (h), w2 (h, out) row-major, b2 (out). The policy acts greedily,
+ * the first index winning ties.
+ *
+ * CartPole (cartpole_rollout_metal.py:46-100), obs 4, out 2: fitness = steps
+ * survived (the terminating step excluded). hidden in {1, 2, 4, 8, 16, 32, 64}. */
+RLENV_API int rlenv_cartpole_rollout(const float* state, const float* theta, int64_t theta_stride,
+                           int64_t p, int hidden, int horizon, float* fitness, void* stream);
+
+/* Acrobot (acrobot_rollout_metal.py:21-81), obs (cos t1, sin t1, cos t2,
+ * sin t2, dt1, dt2), out 3: fitness = steps before the tip first clears height 1.
+ * hidden as for CartPole. */
+RLENV_API int rlenv_acrobot_rollout(const float* state, const float* theta, int64_t theta_stride,
+                          int64_t p, int hidden, int horizon, float* fitness, void* stream);
+
+/* Legged (legged_rollout_metal.py:19-83), obs = state without x (5 + 2c),
+ * out 3c (one three-way head per leg): fitness = sum over steps before the
+ * first fall of (y >= gate ? x_dot : 0) + alive, minus `fall` once at a fall;
+ * steps = steps taken including the falling one. c in 1..4, hidden in
+ * {1, 2, 4, 8, 16, 32}. */
+RLENV_API int rlenv_legged_rollout(int c, int hidden, int horizon, int iters, float alive, float fall,
+                         float gate, float assist, const float* state, const float* theta,
+                         int64_t theta_stride, int64_t p, float* fitness, float* steps,
+                         void* stream);
+
+/* ---- ES generation pieces (es.py:214-227) ------------------------------------
+ * Noise: half (rows, d) of standard normals for antithetic pairs
+ * [row_offset, row_offset + rows), element (pair, j) a function of
+ * (seed, gen, pair, j) only (Philox-4x32-10 and Box-Muller), so any shard of
+ * the pairs regenerates the same values. Replaces es.py:220's
+ * mx.random.normal((P/2, D)). */
+RLENV_API int rlenv_es_noise(float* half, int64_t rows, int64_t d, uint64_t seed, uint64_t gen,
+                   int64_t row_offset, void* stream);
+
+/* Perturbed population rows for members [member_offset, member_offset + rows)
+ * of a population of 2 * pairs: member m < pairs gets theta + sigma * half[m],
+ * member m >= pairs gets theta - sigma * half[m - pairs] (es.py:221-223). The
+ * noise is regenerated in the kernel from (seed, gen, pair), exactly as
+ * rlenv_es_noise computes it. theta_pop (rows, d). */
+RLENV_API int rlenv_es_perturb(const float* theta, int64_t d, float sigma, uint64_t seed, uint64_t gen,
+                     int64_t pairs, int64_t member_offset, int64_t rows, float* theta_pop,
+                     void* stream);
+
+/* Centred ranks (es.py:214-215): ranks[i] = r_i / (p - 1) - 0.5 with r_i the
+ * position of fitness[i] in ascending order, ties broken by index (a stable
+ * sort). p >= 2. */
+RLENV_API int rlenv_es_centered_ranks(const float* fitness, int64_t p, float* ranks, void* stream);
+
+/* Rank-weighted antithetic update (es.py:224-225):
+ * theta_out = theta + lr / (2 * pairs * sigma) * sum_j (ranks[j] - ranks[j + pairs]) * half[j],
+ * with half regenerated from (seed, gen) and a fixed summation order, so every
+ * rank of a multi-GPU job computes the same bits. theta_out may equal theta. */
+RLENV_API int rlenv_es_update(const float* theta, const float* ranks, int64_t d, int64_t pairs, float lr,
+                    float sigma, uint64_t seed, uint64_t gen, float* theta_out, void* stream);
+
+/* Fresh states for n environments: out (rows, n) = center[r] + uniform +-bound
+ * (center NULL means 0), drawn from pcg_hash(seed ^ ((i + index_offset) *
+ * 0x9E3779B9) + r * 0x85EBCA6B). Re-provides `reset(n)` of the MLX ports
+ * (cartpole_mlx.py:30-31, legged_mlx.py:21-22) on the device. */
+RLENV_API int rlenv_reset_uniform(float* out, int rows, int64_t n, const float* center, float bound,
+                        uint32_t seed, int64_t index_offset, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RLENV_H */

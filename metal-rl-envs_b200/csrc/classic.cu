@@ -1,0 +1,265 @@
+// CartPole and Acrobot: the single-step kernels that replace the reference's
+// `cartpole_step` / `acrobot_step` Metal kernels, and T-step kernels that keep
+// the state in registers across steps.
+//
+// Both are streaming kernels: per environment-step they read 16 B of state and
+// one action and write 16 B of state, a 4 B reward and a 1 B done flag. When
+// N is a multiple of 4 and every buffer is 16-byte aligned, each thread owns 4
+// consecutive environments and moves them with 16-byte vector accesses;
+// otherwise one environment per thread.
+#include "classic.cuh"
+
+namespace rlenv {
+namespace {
+
+struct CartPoleEnv {
+  using S = CartPole;
+  static constexpr float kBound = cp::RESET_BOUND;
+  RLENV_D static S from(const float (&r)[4]) { return S{r[0], r[1], r[2], r[3]}; }
+  RLENV_D static void to(const S& s, float (&r)[4]) {
+    r[0] = s.x; r[1] = s.xd; r[2] = s.th; r[3] = s.thd;
+  }
+  RLENV_D static S physics(const S& s, int a) { return cartpole_physics(s, cartpole_force(a)); }
+  RLENV_D static bool terminated(const S& s) { return cartpole_terminated(s); }
+  RLENV_D static float reward(bool) { return 1.0f; }
+};
+
+struct AcrobotEnv {
+  using S = Acrobot;
+  static constexpr float kBound = ac::RESET_BOUND;
+  RLENV_D static S from(const float (&r)[4]) { return S{r[0], r[1], r[2], r[3]}; }
+  RLENV_D static void to(const S& s, float (&r)[4]) {
+    r[0] = s.th1; r[1] = s.th2; r[2] = s.dth1; r[3] = s.dth2;
+  }
+  RLENV_D static S physics(const S& s, int a) { return acrobot_physics(s, float(a - 1)); }
+  RLENV_D static bool terminated(const S& s) { return acrobot_terminated(s); }
+  RLENV_D static float reward(bool d) { return d ? 0.0f : -1.0f; }
+};
+
+// Load V consecutive actions starting at element `i` (i is a multiple of V).
+template <typename A, int V>
+RLENV_D void load_actions(const A* __restrict__ a, int64_t i, int (&out)[V]) {
+#pragma unroll
+  for (int u = 0; u < V; ++u) out[u] = load_action(a, i + u);
+}
+template <>
+RLENV_D void load_actions<uint8_t, 4>(const uint8_t* __restrict__ a, int64_t i, int (&out)[4]) {
+  uchar4 v = __ldg(reinterpret_cast<const uchar4*>(a + i));
+  out[0] = v.x; out[1] = v.y; out[2] = v.z; out[3] = v.w;
+}
+template <>
+RLENV_D void load_actions<int32_t, 4>(const int32_t* __restrict__ a, int64_t i, int (&out)[4]) {
+  int4 v = __ldg(reinterpret_cast<const int4*>(a + i));
+  out[0] = v.x; out[1] = v.y; out[2] = v.z; out[3] = v.w;
+}
+
+// State rows of V consecutive environments: st[r][u] is row r of env i + u.
+template <int V>
+RLENV_D void load_rows(const float* __restrict__ s, int64_t n, int64_t i, float (&st)[4][V]) {
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    if (V == 4) {
+      float4 v = __ldg(reinterpret_cast<const float4*>(s + r * n + i));
+      st[r][0] = v.x; st[r][1] = v.y; st[r][2] = v.z; st[r][V > 3 ? 3 : 0] = v.w;
+    } else {
+#pragma unroll
+      for (int u = 0; u < V; ++u) st[r][u] = __ldg(s + r * n + i + u);
+    }
+  }
+}
+
+template <int V>
+RLENV_D void store_rows(float* __restrict__ s, int64_t n, int64_t i, const float (&st)[4][V]) {
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    if (V == 4) {
+      *reinterpret_cast<float4*>(s + r * n + i) =
+          make_float4(st[r][0], st[r][1], st[r][2], st[r][V > 3 ? 3 : 0]);
+    } else {
+#pragma unroll
+      for (int u = 0; u < V; ++u) s[r * n + i + u] = st[r][u];
+    }
+  }
+}
+
+template <int V>
+RLENV_D void store_vec(float* __restrict__ p, int64_t i, const float (&x)[V]) {
+  if (V == 4) *reinterpret_cast<float4*>(p + i) = make_float4(x[0], x[1], x[2], x[V > 3 ? 3 : 0]);
+  else
+#pragma unroll
+    for (int u = 0; u < V; ++u) p[i + u] = x[u];
+}
+
+template <int V>
+RLENV_D void store_flags(uint8_t* __restrict__ p, int64_t i, const bool (&d)[V]) {
+  if (V == 4) *reinterpret_cast<uchar4*>(p + i) = make_uchar4(d[0], d[1], d[2], d[V > 3 ? 3 : 0]);
+  else
+#pragma unroll
+    for (int u = 0; u < V; ++u) p[i + u] = d[u];
+}
+
+// Advance V environments one step in registers: physics, termination, masked
+// reset from the PCG stream. Returns the done flags and rewards.
+template <typename Env, int V>
+RLENV_D void advance(float (&st)[4][V], const int (&act)[V], uint32_t seed, int64_t gidx,
+                     bool (&d)[V], float (&rw)[V]) {
+#pragma unroll
+  for (int u = 0; u < V; ++u) {
+    float cur[4] = {st[0][u], st[1][u], st[2][u], st[3][u]};
+    typename Env::S nx = Env::physics(Env::from(cur), act[u]);
+    const bool dn = Env::terminated(nx);
+    float out[4];
+    Env::to(nx, out);
+    const uint32_t h = env_hash(seed, gidx + u);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const float fresh = uniform_pm(pcg_hash(h + classic_row_offset(r)), Env::kBound);
+      st[r][u] = dn ? fresh : out[r];
+    }
+    d[u] = dn;
+    rw[u] = Env::reward(dn);
+  }
+}
+
+template <typename Env, typename A, int V>
+__global__ void __launch_bounds__(kThreads)
+step_kernel(const float* __restrict__ state, const A* __restrict__ action, uint32_t seed, int64_t n,
+            int64_t off, float* __restrict__ next, float* __restrict__ reward,
+            uint8_t* __restrict__ done) {
+  const int64_t i = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) * V;
+  if (i >= n) return;
+  float st[4][V];
+  int act[V];
+  load_rows<V>(state, n, i, st);
+  load_actions<A, V>(action, i, act);
+  bool d[V];
+  float rw[V];
+  advance<Env, V>(st, act, seed, off + i, d, rw);
+  store_rows<V>(next, n, i, st);
+  store_vec<V>(reward, i, rw);
+  store_flags<V>(done, i, d);
+}
+
+template <typename Env, typename A, int V>
+__global__ void __launch_bounds__(kThreads)
+step_many_kernel(const float* __restrict__ state_in, const A* __restrict__ actions, uint32_t seed0,
+                 int64_t T, int64_t n, int64_t off, float* __restrict__ state_out,
+                 float* __restrict__ reward_seq, uint8_t* __restrict__ done_seq,
+                 float* __restrict__ reward_sum, float* __restrict__ done_count) {
+  const int64_t i = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) * V;
+  if (i >= n) return;
+  float st[4][V];
+  load_rows<V>(state_in, n, i, st);
+  float rsum[V], dcnt[V];
+#pragma unroll
+  for (int u = 0; u < V; ++u) rsum[u] = dcnt[u] = 0.0f;
+  for (int64_t t = 0; t < T; ++t) {
+    int act[V];
+    load_actions<A, V>(actions, t * n + i, act);
+    bool d[V];
+    float rw[V];
+    advance<Env, V>(st, act, seed0 + uint32_t(t), off + i, d, rw);
+    if (reward_seq) store_vec<V>(reward_seq, t * n + i, rw);
+    if (done_seq) store_flags<V>(done_seq, t * n + i, d);
+#pragma unroll
+    for (int u = 0; u < V; ++u) {
+      rsum[u] += rw[u];
+      dcnt[u] += d[u] ? 1.0f : 0.0f;
+    }
+  }
+  store_rows<V>(state_out, n, i, st);
+  if (reward_sum) store_vec<V>(reward_sum, i, rsum);
+  if (done_count) store_vec<V>(done_count, i, dcnt);
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <typename Env>
+int launch_step(const float* state, const void* action, int dtype, uint32_t seed, int64_t n,
+                int64_t off, float* next, float* reward, uint8_t* done, void* stream) {
+  if (n < 0 || !valid_dtype(dtype)) return RLENV_EINVAL;
+  if (n == 0) return RLENV_OK;
+  if (!state || !action || !next || !reward || !done) return RLENV_EINVAL;
+  const int esz = dtype == RLENV_I64 ? 8 : dtype == RLENV_I32 ? 4 : 1;
+  const bool vec = (n % 4 == 0) && aligned16(state) && aligned16(next) && aligned16(reward) &&
+                   (reinterpret_cast<uintptr_t>(done) & 3u) == 0 &&
+                   (reinterpret_cast<uintptr_t>(action) % (4 * esz)) == 0 && dtype != RLENV_I64;
+  cudaStream_t s = as_stream(stream);
+  return with_action_type(dtype, [&](auto tag) {
+    using A = std::remove_const_t<std::remove_pointer_t<decltype(tag)>>;
+    const A* a = static_cast<const A*>(action);
+    if (vec)
+      step_kernel<Env, A, 4><<<grid_for(n / 4), kThreads, 0, s>>>(state, a, seed, n, off, next,
+                                                                  reward, done);
+    else
+      step_kernel<Env, A, 1><<<grid_for(n), kThreads, 0, s>>>(state, a, seed, n, off, next, reward,
+                                                              done);
+    return launch_status();
+  });
+}
+
+template <typename Env>
+int launch_step_many(const float* state_in, const void* actions, int dtype, uint32_t seed0,
+                     int64_t T, int64_t n, int64_t off, float* state_out, float* reward_seq,
+                     uint8_t* done_seq, float* reward_sum, float* done_count, void* stream) {
+  if (n < 0 || T < 0 || !valid_dtype(dtype)) return RLENV_EINVAL;
+  if (n == 0) return RLENV_OK;
+  if (!state_in || !state_out || (T > 0 && !actions)) return RLENV_EINVAL;
+  const int esz = dtype == RLENV_I64 ? 8 : dtype == RLENV_I32 ? 4 : 1;
+  const bool vec = (n % 4 == 0) && aligned16(state_in) && aligned16(state_out) &&
+                   (!reward_seq || aligned16(reward_seq)) &&
+                   (!done_seq || (reinterpret_cast<uintptr_t>(done_seq) & 3u) == 0) &&
+                   (!reward_sum || aligned16(reward_sum)) && (!done_count || aligned16(done_count)) &&
+                   (reinterpret_cast<uintptr_t>(actions) % (4 * esz)) == 0 && dtype != RLENV_I64;
+  cudaStream_t s = as_stream(stream);
+  return with_action_type(dtype, [&](auto tag) {
+    using A = std::remove_const_t<std::remove_pointer_t<decltype(tag)>>;
+    const A* a = static_cast<const A*>(actions);
+    if (vec)
+      step_many_kernel<Env, A, 4><<<grid_for(n / 4), kThreads, 0, s>>>(
+          state_in, a, seed0, T, n, off, state_out, reward_seq, done_seq, reward_sum, done_count);
+    else
+      step_many_kernel<Env, A, 1><<<grid_for(n), kThreads, 0, s>>>(
+          state_in, a, seed0, T, n, off, state_out, reward_seq, done_seq, reward_sum, done_count);
+    return launch_status();
+  });
+}
+
+}  // namespace
+}  // namespace rlenv
+
+extern "C" {
+
+int rlenv_cartpole_step(const float* state, const void* action, int action_dtype, uint32_t seed,
+                        int64_t n, int64_t index_offset, float* next_state, float* reward,
+                        uint8_t* done, void* stream) {
+  return rlenv::launch_step<rlenv::CartPoleEnv>(state, action, action_dtype, seed, n, index_offset,
+                                                next_state, reward, done, stream);
+}
+
+int rlenv_cartpole_step_many(const float* state_in, const void* actions, int action_dtype,
+                             uint32_t seed0, int64_t steps, int64_t n, int64_t index_offset,
+                             float* state_out, float* reward_seq, uint8_t* done_seq,
+                             float* reward_sum, float* done_count, void* stream) {
+  return rlenv::launch_step_many<rlenv::CartPoleEnv>(state_in, actions, action_dtype, seed0, steps,
+                                                     n, index_offset, state_out, reward_seq,
+                                                     done_seq, reward_sum, done_count, stream);
+}
+
+int rlenv_acrobot_step(const float* state, const void* action, int action_dtype, uint32_t seed,
+                       int64_t n, int64_t index_offset, float* next_state, float* reward,
+                       uint8_t* done, void* stream) {
+  return rlenv::launch_step<rlenv::AcrobotEnv>(state, action, action_dtype, seed, n, index_offset,
+                                               next_state, reward, done, stream);
+}
+
+int rlenv_acrobot_step_many(const float* state_in, const void* actions, int action_dtype,
+                            uint32_t seed0, int64_t steps, int64_t n, int64_t index_offset,
+                            float* state_out, float* reward_seq, uint8_t* done_seq,
+                            float* reward_sum, float* done_count, void* stream) {
+  return rlenv::launch_step_many<rlenv::AcrobotEnv>(state_in, actions, action_dtype, seed0, steps,
+                                                    n, index_offset, state_out, reward_seq,
+                                                    done_seq, reward_sum, done_count, stream);
+}
+
+}  // extern "C"

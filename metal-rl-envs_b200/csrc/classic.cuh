@@ -1,0 +1,122 @@
+// CartPole and Acrobot dynamics as device functions, shared by the single-step
+// kernels, the T-step kernels and the fused ES rollouts so that all of them run
+// the same arithmetic.
+#pragma once
+
+#include "common.cuh"
+
+namespace rlenv {
+
+// ---- CartPole: Gym CartPole-v1, explicit Euler with tau = 0.02 -------------
+// Constants and formulas follow cartpole_np.py:20-31 and 58-77: the float32
+// values of the reference's Python constants.
+namespace cp {
+constexpr float G = 9.8f;
+constexpr float POLE_MASS = 0.1f;
+constexpr float TOTAL_MASS = 1.1f;         // 1.0 + 0.1
+constexpr float HALF_POLE = 0.5f;
+constexpr float POLE_MASS_LENGTH = 0.05f;  // 0.1 * 0.5
+constexpr float FORCE = 10.0f;
+constexpr float TAU = 0.02f;
+constexpr float X_LIMIT = 2.4f;
+constexpr float THETA_LIMIT = 0.20943951023931953f;  // 12 * 2 * pi / 360
+constexpr float FOUR_THIRDS = 1.3333333333333333f;
+constexpr float RESET_BOUND = 0.05f;
+}  // namespace cp
+
+struct CartPole {
+  float x, xd, th, thd;
+};
+
+// One Euler step for a push of `force` (cartpole_np.py:58-77).
+RLENV_D CartPole cartpole_physics(CartPole s, float force) {
+  float sn, c;
+  sincosf(s.th, &sn, &c);
+  float temp = (force + cp::POLE_MASS_LENGTH * (s.thd * s.thd) * sn) / cp::TOTAL_MASS;
+  float th_acc = (cp::G * sn - c * temp) /
+                 (cp::HALF_POLE * (cp::FOUR_THIRDS - cp::POLE_MASS * (c * c) / cp::TOTAL_MASS));
+  float x_acc = temp - cp::POLE_MASS_LENGTH * th_acc * c / cp::TOTAL_MASS;
+  CartPole n;
+  n.x = s.x + cp::TAU * s.xd;
+  n.xd = s.xd + cp::TAU * x_acc;
+  n.th = s.th + cp::TAU * s.thd;
+  n.thd = s.thd + cp::TAU * th_acc;
+  return n;
+}
+
+RLENV_D bool cartpole_terminated(const CartPole& s) {
+  return fabsf(s.x) > cp::X_LIMIT || fabsf(s.th) > cp::THETA_LIMIT;
+}
+
+RLENV_D float cartpole_force(int action) { return action == 1 ? cp::FORCE : -cp::FORCE; }
+
+// ---- Acrobot: Gym's book dynamics, RK4 with dt = 0.2 -----------------------
+// acrobot_np.py:19-30 and 47-93.
+namespace ac {
+constexpr float DT = 0.2f;
+constexpr float HALF_DT = 0.1f;
+constexpr float SIXTH_DT = 0.03333333333333333f;
+constexpr float MAX_VEL_1 = 12.566370614359172f;  // 4 pi
+constexpr float MAX_VEL_2 = 28.274333882308138f;  // 9 pi
+constexpr float PI = 3.141592653589793f;
+constexpr float TWO_PI = 6.283185307179586f;
+constexpr float HALF_PI = 1.5707963267948966f;
+constexpr float RESET_BOUND = 0.1f;
+// Products of the unit link constants, as the reference's Python evaluates them.
+constexpr float D1_CONST = 0.25f;   // m1 lc1^2
+constexpr float D1_INNER = 1.25f;   // l1^2 + lc2^2
+constexpr float D2_CONST = 0.25f;   // lc2^2
+constexpr float PHI2_K = 4.9f;      // m2 lc2 g
+constexpr float PHI1_K = 14.700000000000001f;  // (m1 lc1 + m2 l1) g
+constexpr float DENOM_CONST = 1.25f;  // m2 lc2^2 + I2
+}  // namespace ac
+
+struct Acrobot {
+  float th1, th2, dth1, dth2;
+};
+
+// Gym AcrobotEnv._dsdt with the torque passed alongside (acrobot_np.py:64-86).
+RLENV_D Acrobot acrobot_dsdt(const Acrobot& s, float torque) {
+  float s2, c2;
+  sincosf(s.th2, &s2, &c2);
+  float d1 = ac::D1_CONST + (ac::D1_INNER + c2) + 1.0f + 1.0f;  // m2 (l1^2 + lc2^2 + 2 l1 lc2 c2) + I1 + I2
+  float d2 = (ac::D2_CONST + 0.5f * c2) + 1.0f;                 // m2 (lc2^2 + l1 lc2 c2) + I2
+  float phi2 = ac::PHI2_K * cosf(s.th1 + s.th2 - ac::HALF_PI);
+  float phi1 = -0.5f * (s.dth2 * s.dth2) * s2 - s.dth2 * s.dth1 * s2 +
+               ac::PHI1_K * cosf(s.th1 - ac::HALF_PI) + phi2;
+  float dd2 = (torque + d2 / d1 * phi1 - 0.5f * (s.dth1 * s.dth1) * s2 - phi2) /
+              (ac::DENOM_CONST - (d2 * d2) / d1);
+  float dd1 = -(d2 * dd2 + phi1) / d1;
+  return Acrobot{s.dth1, s.dth2, dd1, dd2};
+}
+
+// Angle to [-pi, pi) without branches (acrobot_np.py:88-90).
+RLENV_D float wrap_angle(float x) { return x - ac::TWO_PI * floorf((x + ac::PI) / ac::TWO_PI); }
+
+RLENV_D Acrobot acrobot_physics(const Acrobot& s, float torque) {
+  Acrobot k1 = acrobot_dsdt(s, torque);
+  Acrobot s2{s.th1 + ac::HALF_DT * k1.th1, s.th2 + ac::HALF_DT * k1.th2,
+             s.dth1 + ac::HALF_DT * k1.dth1, s.dth2 + ac::HALF_DT * k1.dth2};
+  Acrobot k2 = acrobot_dsdt(s2, torque);
+  Acrobot s3{s.th1 + ac::HALF_DT * k2.th1, s.th2 + ac::HALF_DT * k2.th2,
+             s.dth1 + ac::HALF_DT * k2.dth1, s.dth2 + ac::HALF_DT * k2.dth2};
+  Acrobot k3 = acrobot_dsdt(s3, torque);
+  Acrobot s4{s.th1 + ac::DT * k3.th1, s.th2 + ac::DT * k3.th2, s.dth1 + ac::DT * k3.dth1,
+             s.dth2 + ac::DT * k3.dth2};
+  Acrobot k4 = acrobot_dsdt(s4, torque);
+  Acrobot n;
+  n.th1 = wrap_angle(s.th1 + ac::SIXTH_DT * (k1.th1 + 2.0f * k2.th1 + 2.0f * k3.th1 + k4.th1));
+  n.th2 = wrap_angle(s.th2 + ac::SIXTH_DT * (k1.th2 + 2.0f * k2.th2 + 2.0f * k3.th2 + k4.th2));
+  n.dth1 = fminf(fmaxf(s.dth1 + ac::SIXTH_DT * (k1.dth1 + 2.0f * k2.dth1 + 2.0f * k3.dth1 + k4.dth1),
+                       -ac::MAX_VEL_1), ac::MAX_VEL_1);
+  n.dth2 = fminf(fmaxf(s.dth2 + ac::SIXTH_DT * (k1.dth2 + 2.0f * k2.dth2 + 2.0f * k3.dth2 + k4.dth2),
+                       -ac::MAX_VEL_2), ac::MAX_VEL_2);
+  return n;
+}
+
+// The tip above height 1 (acrobot_np.py:92-93).
+RLENV_D bool acrobot_terminated(const Acrobot& s) {
+  return -cosf(s.th1) - cosf(s.th2 + s.th1) > 1.0f;
+}
+
+}  // namespace rlenv

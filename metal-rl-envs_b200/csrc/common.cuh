@@ -1,0 +1,142 @@
+// Shared device helpers for every kernel of librlenv: the reset hash, the
+// action loader, the Philox noise generator and the launch/status plumbing.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "rlenv.h"
+
+#define RLENV_HD __host__ __device__ __forceinline__
+#define RLENV_D __device__ __forceinline__
+
+namespace rlenv {
+
+constexpr int kThreads = 256;  // block size of the streaming step kernels
+
+// ---------------------------------------------------------------------------
+// Reset stream. The PCG hash of Jarzynski & Olano, "Hash Functions for GPU
+// Rendering" (JCGT 9(3), 2020), applied to seed ^ (i * 0x9E3779B9) plus a
+// per-row offset: the reference's in-kernel reset generator
+// (cartpole_metal.py:40-51, 89-93; pendulum_metal.py:86-90). Keeping the same
+// constants keeps the reset values of every environment equal to the
+// reference kernel's.
+RLENV_HD uint32_t pcg_hash(uint32_t v) {
+  uint32_t s = v * 747796405u + 2891336453u;
+  uint32_t w = ((s >> ((s >> 28u) + 4u)) ^ s) * 277803737u;
+  return (w >> 22u) ^ w;
+}
+
+// The top 24 bits of a hash as a float in [-bound, bound). Every step before
+// the final product is exact; the product is one correctly rounded multiply
+// (__fmul_rn is never fused into a neighbouring add).
+RLENV_D float uniform_pm(uint32_t h, float bound) {
+  float t = float(h >> 8) * (1.0f / 16777216.0f) * 2.0f - 1.0f;
+  return __fmul_rn(t, bound);
+}
+
+RLENV_D uint32_t env_hash(uint32_t seed, int64_t global_index) {
+  return seed ^ (uint32_t(global_index) * 0x9E3779B9u);
+}
+
+constexpr uint32_t kRowStride = 0x85EBCA6Bu;  // per-row offset for the K-link, hopper and legged resets
+// CartPole and Acrobot use four explicit offsets (cartpole_metal.py:90-93).
+RLENV_D uint32_t classic_row_offset(int r) {
+  return r == 0 ? 0u : r == 1 ? 0x85EBCA6Bu : r == 2 ? 0xC2B2AE35u : 0x27D4EB2Fu;
+}
+
+// ---------------------------------------------------------------------------
+// Actions arrive as int32 (MLX randint), int64 (numpy, torch) or uint8.
+template <typename A>
+RLENV_D int load_action(const A* __restrict__ a, int64_t i) {
+  return int(__ldg(a + i));
+}
+template <>
+RLENV_D int load_action<int64_t>(const int64_t* __restrict__ a, int64_t i) {
+  return int(__ldg(reinterpret_cast<const long long*>(a) + i));
+}
+
+// ---------------------------------------------------------------------------
+// Philox-4x32-10 (Salmon, Moraes, Dror & Shaw, "Parallel random numbers: as
+// easy as 1, 2, 3", SC 2011), written from the paper: ten rounds of two
+// 32x32->64 multiplies with the published multipliers and Weyl key increments.
+struct U4 {
+  uint32_t x, y, z, w;
+};
+
+RLENV_HD U4 philox4x32_10(U4 c, uint32_t k0, uint32_t k1) {
+  const uint32_t M0 = 0xD2511F53u, M1 = 0xCD9E8D57u;
+  const uint32_t W0 = 0x9E3779B9u, W1 = 0xBB67AE85u;
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    uint64_t p0 = uint64_t(M0) * c.x;
+    uint64_t p1 = uint64_t(M1) * c.z;
+    U4 n;
+    n.x = uint32_t(p1 >> 32) ^ c.y ^ k0;
+    n.y = uint32_t(p1);
+    n.z = uint32_t(p0 >> 32) ^ c.w ^ k1;
+    n.w = uint32_t(p0);
+    c = n;
+    k0 += W0;
+    k1 += W1;
+  }
+  return c;
+}
+
+// Four standard normals for block `blk` (parameters 4*blk .. 4*blk+3) of
+// antithetic pair `pair` in generation `gen`: two Box-Muller transforms
+// (Box & Muller 1958) of the four Philox words. u1 is in (0, 1], so the
+// logarithm is finite.
+RLENV_D void normal4(uint64_t seed, uint64_t gen, int64_t pair, int64_t blk, float out[4]) {
+  U4 c{uint32_t(blk), uint32_t(pair), uint32_t(gen), uint32_t(gen >> 32)};
+  U4 r = philox4x32_10(c, uint32_t(seed), uint32_t(seed >> 32) ^ uint32_t(uint64_t(pair) >> 32));
+  const float inv24 = 1.0f / 16777216.0f;
+  float u1a = float((r.x >> 8) + 1u) * inv24;  // (0, 1]
+  float u2a = float(r.y >> 8) * inv24;          // [0, 1)
+  float u1b = float((r.z >> 8) + 1u) * inv24;
+  float u2b = float(r.w >> 8) * inv24;
+  float ra = sqrtf(-2.0f * logf(u1a));
+  float rb = sqrtf(-2.0f * logf(u1b));
+  float sa, ca, sb, cb;
+  sincospif(2.0f * u2a, &sa, &ca);
+  sincospif(2.0f * u2b, &sb, &cb);
+  out[0] = ra * ca;
+  out[1] = ra * sa;
+  out[2] = rb * cb;
+  out[3] = rb * sb;
+}
+
+RLENV_D float noise_at(uint64_t seed, uint64_t gen, int64_t pair, int64_t j) {
+  float v[4];
+  normal4(seed, gen, pair, j >> 2, v);
+  return v[j & 3];
+}
+
+// ---------------------------------------------------------------------------
+inline int grid_for(int64_t threads, int block = kThreads) {
+  int64_t g = (threads + block - 1) / block;
+  return int(g < 1 ? 1 : g);
+}
+
+inline int launch_status() {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? RLENV_OK : int(e);
+}
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool valid_dtype(int dt) { return dt == RLENV_I32 || dt == RLENV_I64 || dt == RLENV_U8; }
+
+// Call f with the action pointer typed by dtype; f receives a typed null
+// pointer whose type selects the template instance.
+template <typename F>
+int with_action_type(int dtype, F&& f) {
+  switch (dtype) {
+    case RLENV_I32: return f(static_cast<const int32_t*>(nullptr));
+    case RLENV_I64: return f(static_cast<const int64_t*>(nullptr));
+    case RLENV_U8: return f(static_cast<const uint8_t*>(nullptr));
+    default: return RLENV_EINVAL;
+  }
+}
+
+}  // namespace rlenv

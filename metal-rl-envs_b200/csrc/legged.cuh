@@ -1,0 +1,266 @@
+// Planar legged bodies with hard ground contacts (hopper_np.py, legged_np.py):
+// a torso disk at the hip (x, y, phi) and C massless legs at relative angles
+// psi_k, each with a point mass at its foot. C = 1 with one sweep is the
+// hopper. One substep is semi-implicit Euler with exact single-contact
+// impulses combined by block projected Gauss-Seidel over the feet.
+#pragma once
+
+#include "common.cuh"
+#include "pendulum.cuh"  // tri()
+
+namespace rlenv {
+namespace lg {
+constexpr float M_T = 1.0f;
+constexpr float I_T = 0.1f;
+constexpr float M_F = 0.2f;
+constexpr float L = 1.0f;
+constexpr float G = 9.8f;
+constexpr float TORQUE = 2.0f;
+constexpr float MU = 0.7f;
+constexpr float H = 0.01f;
+constexpr int SUBSTEPS = 4;
+constexpr float BAUMGARTE_OVER_H = 20.0f;  // 0.2 / 0.01
+constexpr float FALL_HEIGHT = 0.6f;
+constexpr float FALL_ANGLE = 1.0f;
+constexpr float RESET_BOUND = 0.05f;
+constexpr float ASSIST_DAMPING = 0.1f;
+}  // namespace lg
+
+// Exact impulse (lt, ln) of one contact with Delassus block [[Att, Atn],
+// [Atn, Ann]], free relative velocity (wt, wn) and penetration depth
+// (hopper_np.py:80-109): inelastic normal with Baumgarte push-out, Coulomb
+// friction (stick inside the cone, else slide on its edge), nothing for a
+// contact above the floor, one that would pull, or one already separating.
+// inv_det, inv_dp and inv_dm are 1 / det, 1 / (Ann + mu Atn) and
+// 1 / (Ann - mu Atn), which depend on the block only and so are computed once
+// per substep. BRANCHY skips the solve of an airborne contact with a branch
+// (the variant of hopper_metal.py:110) instead of computing it and selecting
+// zero.
+template <bool BRANCHY>
+RLENV_D void contact_impulse(float Att, float Atn, float Ann, float inv_det, float den_p,
+                             float inv_dp, float den_m, float inv_dm, float wt, float wn,
+                             float depth, float& lt, float& ln) {
+  const bool touching = depth >= 0.0f;
+  if (BRANCHY && !touching) {
+    lt = 0.0f;
+    ln = 0.0f;
+    return;
+  }
+  const float target = lg::BAUMGARTE_OVER_H * fmaxf(depth, 0.0f);
+  const float gap = target - wn;
+  const float ln_stick = (Att * gap + Atn * wt) * inv_det;
+  const float lt_stick = (-Ann * wt - Atn * gap) * inv_det;
+  const bool sticks = fabsf(lt_stick) <= lg::MU * ln_stick;
+  const float ln_p = den_p > 0.0f ? fmaxf(gap * inv_dp, 0.0f) : 0.0f;
+  const float ln_m = den_m > 0.0f ? fmaxf(gap * inv_dm, 0.0f) : 0.0f;
+  const float slip_p = wt + (Att * lg::MU + Atn) * ln_p;
+  const float sgn = slip_p <= 0.0f ? 1.0f : -1.0f;
+  const float ln_slide = slip_p <= 0.0f ? ln_p : ln_m;
+  const float lt_slide = (lg::MU * sgn) * ln_slide;
+  const float l_n = sticks ? ln_stick : ln_slide;
+  const float l_t = sticks ? lt_stick : lt_slide;
+  const bool active = touching && l_n > 0.0f && wn < target;
+  ln = active ? l_n : 0.0f;
+  lt = active ? l_t : 0.0f;
+}
+
+// Non-zero pattern of foot k's Jacobian rows: the tangent row is
+// (1, 0, L cos a, 0.., L cos a at 3+k, 0..), the normal row
+// (0, 1, L sin a, 0.., L sin a at 3+k, 0..), a = phi + psi_k. After unrolling
+// these tests are compile-time, so zero entries are skipped; skipping an
+// exact zero leaves every product and sum unchanged.
+RLENV_HD constexpr bool jt_nz(int k, int i) { return i == 0 || i == 2 || i == 3 + k; }
+RLENV_HD constexpr bool jn_nz(int k, int i) { return i == 1 || i == 2 || i == 3 + k; }
+RLENV_D float jt_at(int i, float lca) { return i == 0 ? 1.0f : lca; }
+RLENV_D float jn_at(int i, float lsa) { return i == 1 ? 1.0f : lsa; }
+
+template <int n>
+RLENV_D void cholesky_packed(float (&Lm)[n * (n + 1) / 2], float (&inv_diag)[n]) {
+#pragma unroll
+  for (int i = 0; i < n; ++i) {
+#pragma unroll
+    for (int j = 0; j <= i; ++j) {
+      float v = Lm[tri(i, j)];
+#pragma unroll
+      for (int p = 0; p < j; ++p) v -= Lm[tri(i, p)] * Lm[tri(j, p)];
+      if (i == j) {
+        const float d = sqrtf(v);
+        Lm[tri(i, i)] = d;
+        inv_diag[i] = 1.0f / d;
+      } else {
+        Lm[tri(i, j)] = v * inv_diag[j];
+      }
+    }
+  }
+}
+
+template <int n>
+RLENV_D void cholesky_solve(const float (&Lm)[n * (n + 1) / 2], const float (&inv_diag)[n],
+                            float (&b)[n]) {
+#pragma unroll
+  for (int i = 0; i < n; ++i) {
+    float v = b[i];
+#pragma unroll
+    for (int p = 0; p < i; ++p) v -= Lm[tri(i, p)] * b[p];
+    b[i] = v * inv_diag[i];
+  }
+#pragma unroll
+  for (int i = n - 1; i >= 0; --i) {
+    float v = b[i];
+#pragma unroll
+    for (int p = i + 1; p < n; ++p) v -= Lm[tri(p, i)] * b[p];
+    b[i] = v * inv_diag[i];
+  }
+}
+
+// One substep of H for C legs (legged_np.py:57-97), in place on q and v.
+template <int C, bool BRANCHY>
+RLENV_D void legged_substep(float (&q)[3 + C], float (&v)[3 + C], const float (&tq)[C],
+                            float assist, int iters) {
+  constexpr int n = 3 + C;
+  float lca[C], lsa[C], dx[C], dy[C], depth[C];
+#pragma unroll
+  for (int k = 0; k < C; ++k) {
+    float sa, ca;
+    sincosf(q[2] + q[3 + k], &sa, &ca);
+    const float ad = v[2] + v[3 + k];
+    lca[k] = lg::L * ca;
+    lsa[k] = lg::L * sa;
+    dx[k] = -lg::L * sa * ad * ad;  // foot acceleration at zero joint acceleration
+    dy[k] = lg::L * ca * ad * ad;
+    depth[k] = -(q[1] - lg::L * ca);
+  }
+  // mass matrix M = M_T diag(1,1,0..) + I_T e_phi e_phi^T + M_F sum_k J_k^T J_k,
+  // lower triangle packed, and the generalised forces
+  float Lm[n * (n + 1) / 2];
+  float f[n];
+#pragma unroll
+  for (int i = 0; i < n; ++i) {
+#pragma unroll
+    for (int j = 0; j <= i; ++j) {
+      float s = 0.0f;
+#pragma unroll
+      for (int k = 0; k < C; ++k) {
+        const bool tt = jt_nz(k, i) && jt_nz(k, j);
+        const bool nn = jn_nz(k, i) && jn_nz(k, j);
+        if (tt && nn) s += jt_at(i, lca[k]) * jt_at(j, lca[k]) + jn_at(i, lsa[k]) * jn_at(j, lsa[k]);
+        else if (tt) s += jt_at(i, lca[k]) * jt_at(j, lca[k]);
+        else if (nn) s += jn_at(i, lsa[k]) * jn_at(j, lsa[k]);
+      }
+      const float base = (i == j) ? (i < 2 ? lg::M_T : (i == 2 ? lg::I_T : 0.0f)) : 0.0f;
+      Lm[tri(i, j)] = base + lg::M_F * s;
+    }
+    float drift = 0.0f, jn_sum = 0.0f;
+#pragma unroll
+    for (int k = 0; k < C; ++k) {
+      if (jt_nz(k, i) && jn_nz(k, i)) drift += jt_at(i, lca[k]) * dx[k] + jn_at(i, lsa[k]) * dy[k];
+      else if (jt_nz(k, i)) drift += jt_at(i, lca[k]) * dx[k];
+      else if (jn_nz(k, i)) drift += jn_at(i, lsa[k]) * dy[k];
+      if (jn_nz(k, i)) jn_sum += jn_at(i, lsa[k]);
+    }
+    f[i] = -lg::M_F * drift - lg::G * (lg::M_F * jn_sum + (i == 1 ? lg::M_T : 0.0f));
+    if (i >= 3) f[i] += tq[i - 3];
+  }
+  f[2] = f[2] - assist * q[2] - (lg::ASSIST_DAMPING * assist) * v[2];
+
+  float inv_diag[n];
+  cholesky_packed<n>(Lm, inv_diag);
+  cholesky_solve<n>(Lm, inv_diag, f);
+  float vf[n];
+#pragma unroll
+  for (int i = 0; i < n; ++i) vf[i] = v[i] + lg::H * f[i];
+
+  // M^-1 J_k^T for every foot, then the Delassus blocks J_k M^-1 J_l^T and the
+  // free relative velocities J_k v_free
+  float MiJt[C][n], MiJn[C][n];
+#pragma unroll
+  for (int k = 0; k < C; ++k) {
+#pragma unroll
+    for (int i = 0; i < n; ++i) {
+      MiJt[k][i] = jt_nz(k, i) ? jt_at(i, lca[k]) : 0.0f;
+      MiJn[k][i] = jn_nz(k, i) ? jn_at(i, lsa[k]) : 0.0f;
+    }
+    cholesky_solve<n>(Lm, inv_diag, MiJt[k]);
+    cholesky_solve<n>(Lm, inv_diag, MiJn[k]);
+  }
+  float Att[C][C], Atn[C][C], Ant[C][C], Ann[C][C], w0t[C], w0n[C];
+#pragma unroll
+  for (int k = 0; k < C; ++k) {
+    float wt = 0.0f, wn = 0.0f;
+#pragma unroll
+    for (int i = 0; i < n; ++i) {
+      if (jt_nz(k, i)) wt += jt_at(i, lca[k]) * vf[i];
+      if (jn_nz(k, i)) wn += jn_at(i, lsa[k]) * vf[i];
+    }
+    w0t[k] = wt;
+    w0n[k] = wn;
+#pragma unroll
+    for (int l = 0; l < C; ++l) {
+      float tt = 0.0f, tn = 0.0f, nt = 0.0f, nn = 0.0f;
+#pragma unroll
+      for (int i = 0; i < n; ++i) {
+        if (jt_nz(k, i)) {
+          tt += jt_at(i, lca[k]) * MiJt[l][i];
+          tn += jt_at(i, lca[k]) * MiJn[l][i];
+        }
+        if (jn_nz(k, i)) {
+          nt += jn_at(i, lsa[k]) * MiJt[l][i];
+          nn += jn_at(i, lsa[k]) * MiJn[l][i];
+        }
+      }
+      Att[k][l] = tt;
+      Atn[k][l] = tn;
+      Ant[k][l] = nt;
+      Ann[k][l] = nn;
+    }
+  }
+  // per-contact constants of the exact block solve
+  float inv_det[C], den_p[C], inv_dp[C], den_m[C], inv_dm[C];
+#pragma unroll
+  for (int k = 0; k < C; ++k) {
+    const float a = Att[k][k], b = Atn[k][k], d = Ann[k][k];
+    inv_det[k] = 1.0f / (a * d - b * b);
+    den_p[k] = d + lg::MU * b;
+    den_m[k] = d - lg::MU * b;
+    inv_dp[k] = 1.0f / (den_p[k] > 0.0f ? den_p[k] : 1.0f);
+    inv_dm[k] = 1.0f / (den_m[k] > 0.0f ? den_m[k] : 1.0f);
+  }
+  // block projected Gauss-Seidel: each contact solved exactly given the others
+  float lt[C], ln[C];
+#pragma unroll
+  for (int k = 0; k < C; ++k) {
+    lt[k] = 0.0f;
+    ln[k] = 0.0f;
+  }
+  for (int it = 0; it < iters; ++it) {
+#pragma unroll
+    for (int k = 0; k < C; ++k) {
+      // the other contacts' contribution first, then the free velocity (legged_np.py:91-94)
+      float st = 0.0f, sn = 0.0f;
+#pragma unroll
+      for (int l = 0; l < C; ++l) {
+        if (l == k) continue;
+        st += Att[k][l] * lt[l] + Atn[k][l] * ln[l];
+        sn += Ant[k][l] * lt[l] + Ann[k][l] * ln[l];
+      }
+      contact_impulse<BRANCHY>(Att[k][k], Atn[k][k], Ann[k][k], inv_det[k], den_p[k], inv_dp[k],
+                               den_m[k], inv_dm[k], w0t[k] + st, w0n[k] + sn, depth[k], lt[k],
+                               ln[k]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < n; ++i) {
+    float vi = 0.0f;
+#pragma unroll
+    for (int k = 0; k < C; ++k) vi += MiJt[k][i] * lt[k] + MiJn[k][i] * ln[k];
+    v[i] = vf[i] + vi;
+    q[i] += lg::H * v[i];
+  }
+}
+
+template <int C>
+RLENV_D bool legged_terminated(const float (&q)[3 + C]) {
+  return q[1] < lg::FALL_HEIGHT || fabsf(q[2]) > lg::FALL_ANGLE;
+}
+
+}  // namespace rlenv

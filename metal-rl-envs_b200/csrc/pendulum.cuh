@@ -1,0 +1,225 @@
+// K-link planar pendulum dynamics: the mass-matrix form (pendulum_np.py) and
+// Featherstone's articulated-body form (pendulum_aba_np.py), plus the shared
+// RK4 driver. Unit point masses on unit massless rods, absolute angles from
+// the downward vertical, torque at the root joint.
+#pragma once
+
+#include "common.cuh"
+
+namespace rlenv {
+namespace pd {
+constexpr float G = 9.8f;
+constexpr float DT = 0.02f;
+constexpr float HALF_DT = 0.01f;
+constexpr float SIXTH_DT = 0.0033333333333333335f;
+constexpr float TORQUE = 1.0f;
+constexpr float MAX_VEL = 31.41592653589793f;  // 10 pi
+constexpr float PI = 3.141592653589793f;
+constexpr float TWO_PI = 6.283185307179586f;
+constexpr float RESET_BOUND = 0.1f;
+}  // namespace pd
+
+RLENV_HD constexpr int tri(int i, int j) { return i * (i + 1) / 2 + j; }
+
+RLENV_D float pd_wrap(float x) { return x - pd::TWO_PI * floorf((x + pd::PI) / pd::TWO_PI); }
+
+// ---- mass-matrix accelerations (pendulum_np.py:68-111) ---------------------
+// M_ij = mu_ij cos(t_i - t_j), mu_ij = K - max(i, j); rhs_i = -sum_j mu_ij
+// sin(t_i - t_j) w_j^2 - G mu_ii sin t_i (+ torque at the root); M acc = rhs by
+// Cholesky. The lower triangle is stored packed. The angle-difference
+// cosines and sines come from K cosines and sines by the addition formulas,
+// or, with PAIRWISE, are evaluated directly (the v9 variant,
+// pendulum_metal.py:96-103).
+template <int K, bool PAIRWISE>
+RLENV_D void mm_accel(const float (&th)[K], const float (&om)[K], float torque, float (&acc)[K]) {
+  float c[K], s[K];
+#pragma unroll
+  for (int i = 0; i < K; ++i) sincosf(th[i], &s[i], &c[i]);
+  float L[K * (K + 1) / 2];
+  float rhs[K];
+#pragma unroll
+  for (int i = 0; i < K; ++i) {
+    float r = 0.0f;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      const float mu = float(K - (i > j ? i : j));
+      float cd, sd;
+      if (PAIRWISE) {
+        sincosf(th[i] - th[j], &sd, &cd);
+      } else {
+        cd = c[i] * c[j] + s[i] * s[j];
+        sd = s[i] * c[j] - c[i] * s[j];
+      }
+      if (j <= i) L[tri(i, j)] = mu * cd;
+      r += mu * sd * (om[j] * om[j]);
+    }
+    rhs[i] = -r - (pd::G * float(K - i)) * s[i];
+  }
+  rhs[0] += torque;
+  // Cholesky in place, then forward and back substitution.
+#pragma unroll
+  for (int i = 0; i < K; ++i) {
+#pragma unroll
+    for (int j = 0; j <= i; ++j) {
+      float v = L[tri(i, j)];
+#pragma unroll
+      for (int p = 0; p < j; ++p) v -= L[tri(i, p)] * L[tri(j, p)];
+      L[tri(i, j)] = (i == j) ? sqrtf(v) : v / L[tri(j, j)];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < K; ++i) {
+    float v = rhs[i];
+#pragma unroll
+    for (int p = 0; p < i; ++p) v -= L[tri(i, p)] * acc[p];
+    acc[i] = v / L[tri(i, i)];
+  }
+#pragma unroll
+  for (int i = K - 1; i >= 0; --i) {
+    float v = acc[i];
+#pragma unroll
+    for (int p = i + 1; p < K; ++p) v -= L[tri(p, i)] * acc[p];
+    acc[i] = v / L[tri(i, i)];
+  }
+}
+
+// ---- articulated-body accelerations (pendulum_aba_np.py:30-99) -------------
+// Planar spatial algebra: motion vectors (w, vx, vy), force vectors (n, fx,
+// fy), symmetric 3x3 inertias stored as (00, 01, 02, 11, 12, 22). Link i's
+// frame is rotated by its absolute angle; the joint coordinate is
+// q_i = t_i - t_{i-1}; each unit mass sits at (1, 0) of its link frame and
+// the next joint at (1, 0) too. Gravity enters as a base acceleration of -G.
+// Per link only the link velocity, U = I^A S and u are kept; the bias force
+// and the transform are recomputed.
+template <int K>
+RLENV_D void aba_accel(const float* th, const float* om, float torque, float* acc) {
+  float vw[K], vx[K], vy[K], U0[K], U1[K], U2[K], uu[K];
+  // outward: link velocities v_i = X_i v_{i-1} + S qd_i
+  float pw = 0.0f, px = 0.0f, py = 0.0f;
+#pragma unroll 4
+  for (int i = 0; i < K; ++i) {
+    const float q = (i == 0) ? th[0] : th[i] - th[i - 1];
+    const float qd = (i == 0) ? om[0] : om[i] - om[i - 1];
+    float sn, cs;
+    sincosf(q, &sn, &cs);
+    const float xy = (i == 0) ? py : py + pw;  // joint at (r, 0), r = 0 at the root and 1 elsewhere
+    vw[i] = pw + qd;
+    vx[i] = cs * px + sn * xy;
+    vy[i] = -sn * px + cs * xy;
+    pw = vw[i];
+    px = vx[i];
+    py = vy[i];
+  }
+  // inward: articulated inertia and bias force of the subtree, carried to the
+  // parent as the child's contribution (cA, cp)
+  float cA00 = 0.0f, cA01 = 0.0f, cA02 = 0.0f, cA11 = 0.0f, cA12 = 0.0f, cA22 = 0.0f;
+  float cp0 = 0.0f, cp1 = 0.0f, cp2 = 0.0f;
+#pragma unroll 4
+  for (int i = K - 1; i >= 0; --i) {
+    const float w = vw[i], x = vx[i], y = vy[i];
+    const float qd = (i == 0) ? om[0] : om[i] - om[i - 1];
+    // own bias p = v x* (I v), I of a unit mass at (1, 0) = [[1,0,1],[0,1,0],[1,0,1]]
+    const float fy = w + y;
+    const float p0 = (x * fy - y * x) + cp0;
+    const float p1 = (-w * fy) + cp1;
+    const float p2 = (w * x) + cp2;
+    const float a00 = 1.0f + cA00, a01 = cA01, a02 = 1.0f + cA02;
+    const float a11 = 1.0f + cA11, a12 = cA12, a22 = 1.0f + cA22;
+    U0[i] = a00;
+    U1[i] = a01;
+    U2[i] = a02;
+    uu[i] = ((i == 0) ? torque : 0.0f) - p0;
+    if (i == 0) break;
+    const float D = a00;
+    const float Ia00 = a00 - a00 * a00 / D, Ia01 = a01 - a00 * a01 / D, Ia02 = a02 - a00 * a02 / D;
+    const float Ia11 = a11 - a01 * a01 / D, Ia12 = a12 - a01 * a02 / D, Ia22 = a22 - a02 * a02 / D;
+    const float c1 = qd * y, c2 = -qd * x;  // c_i = v_i x S qd
+    const float g = uu[i] / D;
+    const float pa0 = p0 + (Ia01 * c1 + Ia02 * c2) + a00 * g;
+    const float pa1 = p1 + (Ia11 * c1 + Ia12 * c2) + a01 * g;
+    const float pa2 = p2 + (Ia12 * c1 + Ia22 * c2) + a02 * g;
+    float sn, cs;
+    sincosf(th[i] - th[i - 1], &sn, &cs);
+    // B = Ia X with X = [[1,0,0],[s,c,s],[c,-s,c]] (r = 1); parent gets X^T B and X^T pa
+    const float B00 = Ia00 + Ia01 * sn + Ia02 * cs, B01 = Ia01 * cs - Ia02 * sn, B02 = Ia01 * sn + Ia02 * cs;
+    const float B10 = Ia01 + Ia11 * sn + Ia12 * cs, B11 = Ia11 * cs - Ia12 * sn, B12 = Ia11 * sn + Ia12 * cs;
+    const float B20 = Ia02 + Ia12 * sn + Ia22 * cs, B21 = Ia12 * cs - Ia22 * sn, B22 = Ia12 * sn + Ia22 * cs;
+    cA00 = B00 + sn * B10 + cs * B20;
+    cA01 = B01 + sn * B11 + cs * B21;
+    cA02 = B02 + sn * B12 + cs * B22;
+    cA11 = cs * B11 - sn * B21;
+    cA12 = cs * B12 - sn * B22;
+    cA22 = sn * B12 + cs * B22;
+    cp0 = pa0 + sn * pa1 + cs * pa2;
+    cp1 = cs * pa1 - sn * pa2;
+    cp2 = sn * pa1 + cs * pa2;
+  }
+  // outward: accelerations, the base accelerating at -G; absolute angular
+  // accelerations are the running sum of the joint accelerations
+  float aw = 0.0f, ax = -pd::G, ay = 0.0f, run = 0.0f;
+#pragma unroll 4
+  for (int i = 0; i < K; ++i) {
+    const float q = (i == 0) ? th[0] : th[i] - th[i - 1];
+    const float qd = (i == 0) ? om[0] : om[i] - om[i - 1];
+    float sn, cs;
+    sincosf(q, &sn, &cs);
+    const float xy = (i == 0) ? ay : ay + aw;
+    const float ap1 = cs * ax + sn * xy + qd * vy[i];
+    const float ap2 = -sn * ax + cs * xy - qd * vx[i];
+    const float qdd = (uu[i] - (U0[i] * aw + U1[i] * ap1 + U2[i] * ap2)) / U0[i];
+    aw = aw + qdd;
+    ax = ap1;
+    ay = ap2;
+    run += qdd;
+    acc[i] = run;
+  }
+}
+
+// ---- RK4 step on (theta, omega) (pendulum_np.py:60-66) -----------------------
+// The angle derivative is omega itself, so only the accelerations need the
+// dynamics. Returns wrapped angles and clipped velocities in th, om.
+template <int K, typename Accel>
+RLENV_D void pendulum_rk4(float (&th)[K], float (&om)[K], float torque, Accel accel) {
+  float ts[K], os[K], a[K], dth[K], dom[K];
+  accel(th, om, torque, a);  // k1 = (om, a1)
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    dth[j] = om[j];
+    dom[j] = a[j];
+    ts[j] = th[j] + pd::HALF_DT * om[j];
+    os[j] = om[j] + pd::HALF_DT * a[j];
+  }
+  accel(ts, os, torque, a);  // k2 = (os, a2)
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    dth[j] += 2.0f * os[j];
+    dom[j] += 2.0f * a[j];
+    ts[j] = th[j] + pd::HALF_DT * os[j];
+    os[j] = om[j] + pd::HALF_DT * a[j];
+  }
+  accel(ts, os, torque, a);  // k3
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    dth[j] += 2.0f * os[j];
+    dom[j] += 2.0f * a[j];
+    ts[j] = th[j] + pd::DT * os[j];
+    os[j] = om[j] + pd::DT * a[j];
+  }
+  accel(ts, os, torque, a);  // k4
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    th[j] = pd_wrap(th[j] + pd::SIXTH_DT * (dth[j] + os[j]));
+    om[j] = fminf(fmaxf(om[j] + pd::SIXTH_DT * (dom[j] + a[j]), -pd::MAX_VEL), pd::MAX_VEL);
+  }
+}
+
+// The tip above half the chain's length: -sum_j cos t_j > K / 2.
+template <int K>
+RLENV_D bool pendulum_terminated(const float (&th)[K]) {
+  float h = 0.0f;
+#pragma unroll
+  for (int j = 0; j < K; ++j) h += cosf(th[j]);
+  return -h > float(K) * 0.5f;
+}
+
+}  // namespace rlenv

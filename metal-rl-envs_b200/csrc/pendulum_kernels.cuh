@@ -1,0 +1,173 @@
+// K-link pendulum step kernels as templates: the mass-matrix form with one
+// thread per environment, the same form with K warp lanes per environment, and
+// the O(K) articulated-body form. Each pendulum_*.cu instantiates a range of K
+// so that the translation units compile in parallel; pendulum.cu holds the
+// C ABI entry points and dispatches to them.
+#pragma once
+
+#include "pendulum.cuh"
+
+namespace rlenv {
+namespace pend {
+
+
+// Actions are read through a runtime dtype switch, uniform across the grid,
+// so each body needs one kernel instance per K rather than three.
+RLENV_D int action_at(const void* a, int dtype, int64_t i) {
+  switch (dtype) {
+    case RLENV_I64: return load_action(static_cast<const int64_t*>(a), i);
+    case RLENV_I32: return load_action(static_cast<const int32_t*>(a), i);
+    default: return load_action(static_cast<const uint8_t*>(a), i);
+  }
+}
+
+enum Form { MASS_MATRIX = 0, MASS_MATRIX_PAIRWISE = 1, ARTICULATED = 2 };
+
+template <int K, int FORM>
+__global__ void __launch_bounds__(128)
+pendulum_kernel(const float* __restrict__ state, const void* __restrict__ action, int dtype,
+                uint32_t seed, int64_t n, int64_t off, float* __restrict__ next,
+                float* __restrict__ reward, uint8_t* __restrict__ done) {
+  const int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (e >= n) return;
+  float th[K], om[K];
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    th[j] = __ldg(state + j * n + e);
+    om[j] = __ldg(state + (K + j) * n + e);
+  }
+  const float torque = float(action_at(action, dtype, e) - 1) * pd::TORQUE;
+  if (FORM == ARTICULATED) {
+    pendulum_rk4<K>(th, om, torque, [](const float* t, const float* o, float tq, float* a) {
+      aba_accel<K>(t, o, tq, a);
+    });
+  } else {
+    pendulum_rk4<K>(th, om, torque,
+                    [](const float (&t)[K], const float (&o)[K], float tq, float (&a)[K]) {
+                      mm_accel<K, FORM == MASS_MATRIX_PAIRWISE>(t, o, tq, a);
+                    });
+  }
+  const bool d = pendulum_terminated<K>(th);
+  const uint32_t h = env_hash(seed, off + e);
+#pragma unroll
+  for (int j = 0; j < 2 * K; ++j) {
+    const float fresh = uniform_pm(pcg_hash(h + uint32_t(j) * kRowStride), pd::RESET_BOUND);
+    next[j * n + e] = d ? fresh : (j < K ? th[j] : om[j - K]);
+  }
+  reward[e] = d ? 0.0f : -1.0f;
+  done[e] = d;
+}
+
+// ---- K lanes per environment (pendulum_metal_coop.py:28-149) -----------------
+// Lane j of a K-lane segment owns component j: its angle, its velocity, row j
+// of the mass matrix and row j of the Cholesky factor. Column c of the factor
+// is formed after the diagonal lane c broadcasts its row; forward
+// substitution broadcasts each y_i as it is produced; back substitution sums
+// the lanes' contributions with a butterfly over the segment. K is a power of
+// two no larger than 32, so a segment never straddles a warp.
+template <int K>
+RLENV_D float seg_sum(float v) {
+#pragma unroll
+  for (int m = 1; m < K; m <<= 1) v += __shfl_xor_sync(0xffffffffu, v, m, K);
+  return v;
+}
+
+template <int K>
+RLENV_D float coop_accel(float th_j, float om_j, float torque, int j) {
+  float sj, cj;
+  sincosf(th_j, &sj, &cj);
+  float Lr[K];
+  float r = 0.0f;
+#pragma unroll
+  for (int p = 0; p < K; ++p) {
+    const float cp = __shfl_sync(0xffffffffu, cj, p, K);
+    const float sp = __shfl_sync(0xffffffffu, sj, p, K);
+    const float op = __shfl_sync(0xffffffffu, om_j, p, K);
+    const float mu = float(K - (j > p ? j : p));
+    Lr[p] = mu * (cj * cp + sj * sp);
+    r += mu * (sj * cp - cj * sp) * (op * op);
+  }
+  float rhs = -r - (pd::G * float(K - j)) * sj;
+  if (j == 0) rhs += torque;
+#pragma unroll
+  for (int c = 0; c < K; ++c) {
+    float s = Lr[c];
+#pragma unroll
+    for (int p = 0; p < c; ++p) s -= Lr[p] * __shfl_sync(0xffffffffu, Lr[p], c, K);
+    const float dgn = sqrtf(__shfl_sync(0xffffffffu, s, c, K));
+    if (j == c) Lr[c] = dgn;
+    else if (j > c) Lr[c] = s / dgn;
+  }
+  float y[K];
+#pragma unroll
+  for (int i = 0; i < K; ++i) {
+    float yi = 0.0f;
+    if (j == i) {
+      float s = rhs;
+#pragma unroll
+      for (int p = 0; p < i; ++p) s -= Lr[p] * y[p];
+      yi = s / Lr[i];
+    }
+    y[i] = __shfl_sync(0xffffffffu, yi, i, K);
+  }
+  float x = 0.0f;
+#pragma unroll
+  for (int i = K - 1; i >= 0; --i) {
+    const float s = seg_sum<K>(j > i ? Lr[i] * x : 0.0f);
+    if (j == i) x = (y[i] - s) / Lr[i];
+  }
+  return x;
+}
+
+template <int K>
+__global__ void __launch_bounds__(256)
+pendulum_coop_kernel(const float* __restrict__ state, const void* __restrict__ action, int dtype,
+                     uint32_t seed, int64_t n, int64_t off, float* __restrict__ next,
+                     float* __restrict__ reward, uint8_t* __restrict__ done) {
+  const int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int j = int(threadIdx.x) & (K - 1);
+  const int64_t e_raw = t / K;
+  const bool valid = e_raw < n;
+  const int64_t e = valid ? e_raw : n - 1;  // idle lanes mirror the last env to keep shuffles full
+  const float th = __ldg(state + j * n + e);
+  const float om = __ldg(state + (K + j) * n + e);
+  const float torque = float(action_at(action, dtype, e) - 1) * pd::TORQUE;
+  const float a1 = coop_accel<K>(th, om, torque, j);
+  float dth = om, dom = a1;
+  float ts = th + pd::HALF_DT * om, os = om + pd::HALF_DT * a1;
+  const float a2 = coop_accel<K>(ts, os, torque, j);
+  dth += 2.0f * os;
+  dom += 2.0f * a2;
+  ts = th + pd::HALF_DT * os;
+  os = om + pd::HALF_DT * a2;
+  const float a3 = coop_accel<K>(ts, os, torque, j);
+  dth += 2.0f * os;
+  dom += 2.0f * a3;
+  ts = th + pd::DT * os;
+  os = om + pd::DT * a3;
+  const float a4 = coop_accel<K>(ts, os, torque, j);
+  const float nth = pd_wrap(th + pd::SIXTH_DT * (dth + os));
+  const float nom = fminf(fmaxf(om + pd::SIXTH_DT * (dom + a4), -pd::MAX_VEL), pd::MAX_VEL);
+  const bool d = -seg_sum<K>(cosf(nth)) > float(K) * 0.5f;
+  if (!valid) return;
+  const uint32_t h = env_hash(seed, off + e);
+  next[j * n + e] = d ? uniform_pm(pcg_hash(h + uint32_t(j) * kRowStride), pd::RESET_BOUND) : nth;
+  next[(K + j) * n + e] =
+      d ? uniform_pm(pcg_hash(h + uint32_t(K + j) * kRowStride), pd::RESET_BOUND) : nom;
+  if (j == 0) {
+    reward[e] = d ? 0.0f : -1.0f;
+    done[e] = d;
+  }
+}
+
+using StepFn = void (*)(const float*, const void*, int, uint32_t, int64_t, int64_t, float*, float*,
+                        uint8_t*);
+
+// Per-translation-unit pickers: nullptr when the unit does not build this K.
+StepFn pick_mm_lo(int k, bool pairwise);    // k in 1..8
+StepFn pick_mm_hi(int k, bool pairwise);    // k in 9..16
+StepFn pick_aba(int k);                     // k in 1..16, 24, 32, 48, 64
+StepFn pick_coop(int k);                    // k in 2, 4, 8, 16, 32
+
+}  // namespace pend
+}  // namespace rlenv

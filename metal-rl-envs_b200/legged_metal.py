@@ -1,0 +1,91 @@
+"""Planar legged bodies with C hard ground contacts, stepped by an sm_100a CUDA kernel.
+
+Drop-in for the reference module of the same name (legged_metal.py:1-185):
+`Legged(c, iters=8)` with `.step(state, action, assist=None)`, `.reseed(seed)`,
+`.reset(n)`, `.stand`, `.n_actions`. State (2(3+C), N) float32: q = (x, y, phi,
+psi_1..psi_C) then q_dot. The action is an index in [0, 3^C): leg k's torque is
+((a // 3^k) % 3 - 1) * 2. One thread per environment runs four substeps of 0.01:
+the (3+C) x (3+C) mass matrix and its Cholesky factor, 2C + 1 solves, the
+Delassus blocks, and `iters` sweeps of block projected Gauss-Seidel over the
+feet, each foot's exact stick/slide/separate impulse given the others. Then the
+fall test (torso below 0.6 or tilted past 1 rad), the reset to the standing
+pose plus uniform +-0.05 on every row, and the reward x_dot + 1.
+`assist` (a float or a one-element CUDA tensor) is the stiffness of the
+curriculum's torso-upright spring-damper. Built for C = 1..4.
+"""
+
+import numpy as np
+import torch
+
+import rlenv_lib as _rl
+
+M_T, I_T, M_F, L = 1.0, 0.1, 0.2, 1.0
+GRAVITY = 9.8
+TORQUE = 2.0
+MU = 0.7
+H, SUBSTEPS = 0.01, 4
+BAUMGARTE = 0.2
+FALL_HEIGHT, FALL_ANGLE = 0.6, 1.0
+RESET_BOUND = 0.05
+ITERS = 8
+
+
+def leg_angles(c):
+    """Resting leg angles, spread symmetrically so the inner feet touch the floor."""
+    return np.linspace(-0.25 * (c - 1), 0.25 * (c - 1), c) if c > 1 else np.zeros(1)
+
+
+def stand_pose(c):
+    """The reset pose (2(3+C),): hip at the height of the innermost feet, at rest."""
+    a = leg_angles(c)
+    q = np.concatenate([[0.0, L * np.cos(np.abs(a).min()), 0.0], a])
+    return np.concatenate([q, np.zeros_like(q)]).astype(np.float32)
+
+
+def static_pose(c):
+    """A true equilibrium with every foot on the floor, legs at +-0.25 rad."""
+    a = np.array([-0.25, 0.25] * (c // 2)) if c > 1 else np.zeros(1)
+    q = np.concatenate([[0.0, L * np.cos(np.abs(a).min()), 0.0], np.sort(a)])
+    return np.concatenate([q, np.zeros_like(q)]).astype(np.float32)
+
+
+class _OnDevice:
+    """A small constant array uploaded once per device."""
+
+    def __init__(self, host):
+        self.host = np.ascontiguousarray(host, dtype=np.float32)
+        self._dev = {}
+
+    def on(self, dev):
+        t = self._dev.get(dev)
+        if t is None:
+            t = self._dev[dev] = torch.from_numpy(self.host).to(dev)
+        return t
+
+
+class Legged(_rl.StepBody):
+    def __init__(self, c, iters=ITERS):
+        if c not in (1, 2, 3, 4):
+            raise ValueError("legged bodies are built for c in 1..4")
+        super().__init__()
+        self.c, self.iters = c, int(iters)
+        self.rows = 2 * (3 + c)
+        self.n_actions = 3**c
+        self._stand = _OnDevice(stand_pose(c))
+
+    @property
+    def stand(self):
+        return self._stand.on(_rl.device())
+
+    def reset(self, n):
+        return _rl.reset_uniform(self.rows, n, RESET_BOUND, center=self._stand.host)
+
+    def step(self, state, action, assist=None):
+        state = _rl.as_state(state, self.rows)
+        stand = self._stand.on(state.device)
+        if isinstance(assist, torch.Tensor) and assist.device.type == "cuda":
+            a_val, a_ptr = 0.0, assist.reshape(-1)[:1].float().contiguous()
+        else:
+            a_val, a_ptr = (0.0 if assist is None else _rl.float_scalar(assist)), None
+        return self._launch(_rl.lib().legged_step, (self.c, self.iters), state, action,
+                            tail=(stand.data_ptr(), a_val, _rl.ptr(a_ptr)))

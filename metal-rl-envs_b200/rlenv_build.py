@@ -1,0 +1,84 @@
+"""Build librlenv.so in place from csrc/*.cu for sm_100a.
+
+Each translation unit is compiled by nvcc in parallel; the objects are linked
+into librlenv.so next to this file, where rlenv_lib.py loads it. The build is
+incremental: a unit is recompiled only when it or a header it may include is
+newer than its object.
+
+Run as a script (`python rlenv_build.py [-v]`) or call build().
+"""
+
+import concurrent.futures
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+CSRC = HERE / "csrc"
+INCLUDE = HERE.parent / "include"
+OBJ = HERE / "_build"
+LIB = HERE / "librlenv.so"
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC",
+         "-Xcompiler", "-fvisibility=hidden"]
+
+
+def nvcc():
+    exe = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not Path(exe).exists():
+        raise RuntimeError("nvcc not found: the CUDA toolkit is required to build librlenv.so")
+    return exe
+
+
+def _stale(src, obj, headers):
+    if not obj.exists():
+        return True
+    t = obj.stat().st_mtime
+    return src.stat().st_mtime > t or any(h.stat().st_mtime > t for h in headers)
+
+
+def _compile(src, obj, extra, verbose):
+    cmd = [nvcc(), *ARCH, *FLAGS, *extra, f"-I{INCLUDE}", f"-I{CSRC}", "-c", str(src), "-o", str(obj)]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"nvcc failed on {src.name}:\n{r.stdout}\n{r.stderr}")
+    return r.stdout + r.stderr
+
+
+def build(verbose=False, ptxas_verbose=False, jobs=None):
+    """Compile every csrc/*.cu for sm_100a and link librlenv.so. Returns its path."""
+    OBJ.mkdir(exist_ok=True)
+    sources = sorted(CSRC.glob("*.cu"))
+    headers = sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h"))
+    extra = ["-Xptxas", "-v"] if ptxas_verbose else []
+    todo = [s for s in sources if ptxas_verbose or _stale(s, OBJ / (s.stem + ".o"), headers)]
+    logs = {}
+    if todo:
+        with concurrent.futures.ThreadPoolExecutor(max_workers=jobs or min(len(todo), os.cpu_count() or 4)) as ex:
+            futs = {ex.submit(_compile, s, OBJ / (s.stem + ".o"), extra, verbose): s for s in todo}
+            for f in concurrent.futures.as_completed(futs):
+                logs[futs[f].name] = f.result()
+    objs = [OBJ / (s.stem + ".o") for s in sources]
+    if todo or not LIB.exists() or any(o.stat().st_mtime > LIB.stat().st_mtime for o in objs):
+        tmp = LIB.with_suffix(".so.tmp")
+        cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-lcudart"]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+        os.replace(tmp, LIB)
+    if ptxas_verbose:
+        for name in sorted(logs):
+            print(f"==== {name}\n{logs[name]}")
+    return LIB
+
+
+if __name__ == "__main__":
+    build(verbose="-v" in sys.argv, ptxas_verbose="--ptxas" in sys.argv)
+    print(LIB)

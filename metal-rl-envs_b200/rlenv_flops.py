@@ -1,0 +1,58 @@
+"""Algorithmic work per environment step, for the roofline figures.
+
+Counting rule: a fused multiply-add is 2 flops; an add, multiply, divide, floor,
+min or max is 1; square roots and transcendentals (sin, cos, tanh, log) are
+counted separately, since on sm_100a the precise versions are instruction
+sequences rather than single operations. Integer work (the reset hash, index
+arithmetic) is not counted. The counts follow the formulas of the kernels in
+csrc/*.cuh term by term; they are the denominators' numerators, not profiler
+readings.
+"""
+
+# Acrobot (classic.cuh): one derivative evaluation is 36 flops, 4 divides included,
+# and 4 transcendentals (sin and cos of theta2, two cosines for the potential terms).
+# RK4: 4 derivatives (144) + three stage states (4 x 2 x 3 = 24) + the weighted sum and
+# update (4 x 7 = 28) + two wraps (2 x 5) + two clips (2 x 2) + termination (3): 213 flops;
+# transcendentals 4 x 4 + 2 (termination) = 18.
+ACROBOT = dict(flops=213, transcendentals=18)
+
+# CartPole (classic.cuh): temp 5, theta_acc 9 (one divide each side), x_acc 5, four Euler
+# updates as FMAs (8), termination 2 compares: 29 flops; sin and cos: 2.
+CARTPOLE = dict(flops=29, transcendentals=2)
+
+# Bytes moved per environment step by the single-step kernel: state in and out
+# (2 x 16), one action, a 4-byte reward and a 1-byte done. The T-step kernel
+# moves the state once per launch and per step only the action, reward and done.
+def step_bytes(rows=4, action_bytes=1):
+    return 2 * 4 * rows + action_bytes + 4 + 1
+
+
+def step_many_bytes(rows, n, T, action_bytes=1, write_seq=True):
+    per_step = action_bytes + (5 if write_seq else 0)
+    return n * (2 * 4 * rows + T * per_step)
+
+
+def mass_matrix_flops(k):
+    """Per step of the K-link mass-matrix form, 4 RK4 stages: matrix and right-hand side
+    (addition formulas: 6K^2 for cos/sin differences and products, 3K^2 for the Coriolis sum,
+    2K for gravity), Cholesky K^3/3 + K^2/2, two substitutions 2K^2, plus the RK4
+    combination (12K). The reference's own count (bench_pendulum.py:29-33) is of the same form."""
+    stage = 6 * k * k + 3 * k * k + 2 * k + k ** 3 / 3 + k * k / 2 + 2 * k * k
+    return dict(flops=round(4 * stage + 12 * k), transcendentals=4 * 2 * k + k)
+
+
+def aba_flops(k):
+    """Per step of the articulated-body form: about 140 flops per link per stage over the three
+    passes plus the RK4 combination, as the reference counts (bench_aba.py:53-55)."""
+    return dict(flops=4 * 140 * k + 12 * k, transcendentals=4 * 6 * k + k)
+
+
+def legged_flops(c, iters=8):
+    """Per step of the legged body, 4 substeps. Per substep with n = 3 + C: Jacobians and drift
+    10C; mass matrix and forces ~ (n(n+1)/2)(2C) + 8nC; Cholesky n^3/3; 2C + 1 solves of 2n^2;
+    Delassus blocks 4C^2 x 6 and free velocities 12C; per sweep and contact the other contacts'
+    contribution 8(C - 1) and the exact impulse ~40; the velocity update 4nC + 4n."""
+    n = 3 + c
+    sub = (10 * c + (n * (n + 1) // 2) * 2 * c + 8 * n * c + n ** 3 / 3 + (2 * c + 1) * 2 * n * n
+           + 24 * c * c + 12 * c + iters * c * (8 * (c - 1) + 40) + 4 * n * c + 4 * n)
+    return dict(flops=round(4 * sub), transcendentals=4 * (2 * c + n))

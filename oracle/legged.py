@@ -1,0 +1,149 @@
+"""Hopper and legged-body contact dynamics in float32 numpy.
+
+TEST INFRASTRUCTURE ONLY (see oracle/__init__.py).
+
+A torso disk (mass 1, inertia 0.1) at the hip (x, y, phi) and C massless legs
+of length 1 at relative angles psi_k, each with a 0.2 point mass at its foot.
+q = (x, y, phi, psi_1..psi_C), state (2(3+C), N) = q then q_dot. Each foot is a
+hard inelastic contact with Coulomb friction 0.7 and Baumgarte 0.2; four
+semi-implicit Euler substeps of 0.01 per step; multiple contacts are combined
+by block projected Gauss-Seidel (hopper_np.py:24-35, legged_np.py:24-97).
+C = 1 with one sweep is the hopper.
+"""
+
+import numpy as np
+
+from oracle.pendulum import chol_solve
+
+LG_M_T, LG_I_T, LG_M_F, LG_L = 1.0, 0.1, 0.2, 1.0
+LG_GRAVITY = 9.8
+LG_TORQUE = 2.0
+LG_MU = 0.7
+LG_H, LG_SUBSTEPS = 0.01, 4
+LG_BAUMGARTE = 0.2
+LG_FALL_HEIGHT, LG_FALL_ANGLE = 0.6, 1.0
+LG_RESET_BOUND = 0.05
+LG_ITERS = 8
+HOPPER_STAND = np.array([0.0, LG_L, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0], dtype=np.float32)
+
+
+def leg_angles(c):
+    """Resting leg angles, spread symmetrically (legged_np.py:28-30)."""
+    return np.linspace(-0.25 * (c - 1), 0.25 * (c - 1), c) if c > 1 else np.zeros(1)
+
+
+def stand_pose(c):
+    """Reset pose: hip at the height where the innermost feet touch the floor (legged_np.py:43-46)."""
+    a = leg_angles(c)
+    q = np.concatenate([[0.0, LG_L * np.cos(np.abs(a).min()), 0.0], a])
+    return np.concatenate([q, np.zeros_like(q)]).astype(np.float32)
+
+
+def static_pose(c):
+    """Every foot on the floor with legs at +-0.25 rad: a true equilibrium (legged_np.py:33-40)."""
+    a = np.array([-0.25, 0.25] * (c // 2)) if c > 1 else np.zeros(1)
+    q = np.concatenate([[0.0, LG_L * np.cos(np.abs(a).min()), 0.0], np.sort(a)])
+    return np.concatenate([q, np.zeros_like(q)]).astype(np.float32)
+
+
+def torques(action, c):
+    """Action index in [0, 3^C) to per-leg torques ((a // 3^k) % 3 - 1) * 2 (legged_np.py:49-54)."""
+    a = np.asarray(action)
+    return [((a // 3**k) % 3 - 1).astype(np.float32) * LG_TORQUE for k in range(c)]
+
+
+def contact_impulse(att, atn, ann, wt, wn, depth, mu=LG_MU):
+    """Exact single-contact impulse (lt, ln), branch-free (hopper_np.py:80-109): stick when
+    the sticking impulse lies in the friction cone, else slide on the cone's edge in the
+    direction that opposes the residual slip; nothing above the floor, when pulling, or when
+    the free motion already separates. A sliding direction with a non-positive denominator
+    (the Painleve regime) contributes nothing. As in the reference, the sliding sign is a
+    float64 array, so lt (and every state it touches afterwards) is float64."""
+    touching = depth >= 0.0
+    target = LG_BAUMGARTE / LG_H * np.maximum(depth, 0.0)
+    det = att * ann - atn * atn
+    ln_st = (att * (target - wn) + atn * wt) / det
+    lt_st = (-ann * wt - atn * (target - wn)) / det
+    stick = np.abs(lt_st) <= mu * ln_st
+    dp, dm = ann + mu * atn, ann - mu * atn
+    ln_p = np.where(dp > 0.0, np.maximum((target - wn) / np.where(dp > 0.0, dp, 1.0), 0.0), 0.0)
+    ln_m = np.where(dm > 0.0, np.maximum((target - wn) / np.where(dm > 0.0, dm, 1.0), 0.0), 0.0)
+    slip = wt + (att * mu + atn) * ln_p
+    direction = np.where(slip <= 0.0, 1.0, -1.0)
+    ln_sl = np.where(slip <= 0.0, ln_p, ln_m)
+    lt_sl = mu * direction * ln_sl
+    ln = np.where(stick, ln_st, ln_sl)
+    lt = np.where(stick, lt_st, lt_sl)
+    on = touching & (ln > 0.0) & (wn < target)
+    return np.where(on, lt, 0.0), np.where(on, ln, 0.0)
+
+
+def substep(q, v, tq, c, iters=LG_ITERS, mu=LG_MU, assist=0.0, return_impulses=False):
+    """One substep of 0.01 for C legs (legged_np.py:57-97). q, v: (3+C, N); tq: C arrays."""
+    n = 3 + c
+    z = np.zeros_like(q[0])
+    one = z + 1.0
+    Jt, Jn, drift, depth = [], [], [], []
+    for k in range(c):
+        a = q[2] + q[3 + k]
+        ca, sa = np.cos(a), np.sin(a)
+        ad = v[2] + v[3 + k]
+        Jt.append([one, z, LG_L * ca] + [LG_L * ca if j == k else z for j in range(c)])
+        Jn.append([z, one, LG_L * sa] + [LG_L * sa if j == k else z for j in range(c)])
+        drift.append((-LG_L * sa * ad * ad, LG_L * ca * ad * ad))
+        depth.append(-(q[1] - LG_L * ca))
+    base = [[0.0] * n for _ in range(n)]  # Python floats: weak scalars in float32 expressions
+    base[0][0] = base[1][1] = LG_M_T
+    base[2][2] = LG_I_T
+    M = np.stack([np.stack([base[i][j] + LG_M_F * sum(Jt[k][i] * Jt[k][j] + Jn[k][i] * Jn[k][j] for k in range(c))
+                            for j in range(n)]) for i in range(n)])
+    f = [-LG_M_F * sum(Jt[k][i] * drift[k][0] + Jn[k][i] * drift[k][1] for k in range(c))
+         - LG_GRAVITY * (LG_M_F * sum(Jn[k][i] for k in range(c)) + (LG_M_T if i == 1 else 0.0)) for i in range(n)]
+    for k in range(c):
+        f[3 + k] = f[3 + k] + tq[k]
+    f[2] = f[2] - assist * q[2] - 0.1 * assist * v[2]
+    vfree = [v[i] + LG_H * a for i, a in enumerate(chol_solve(M, np.stack(f), n))]
+    MiJt = [chol_solve(M, np.stack(Jt[k]), n) for k in range(c)]
+    MiJn = [chol_solve(M, np.stack(Jn[k]), n) for k in range(c)]
+
+    def dot(a, b):
+        return sum(a[i] * b[i] for i in range(n))
+
+    A = [[(dot(Jt[k], MiJt[l]), dot(Jt[k], MiJn[l]), dot(Jn[k], MiJt[l]), dot(Jn[k], MiJn[l])) for l in range(c)]
+         for k in range(c)]
+    w0 = [(dot(Jt[k], vfree), dot(Jn[k], vfree)) for k in range(c)]
+    lt, ln = [z] * c, [z] * c
+    for _ in range(iters):
+        for k in range(c):
+            wt = w0[k][0] + sum(A[k][l][0] * lt[l] + A[k][l][1] * ln[l] for l in range(c) if l != k)
+            wn = w0[k][1] + sum(A[k][l][2] * lt[l] + A[k][l][3] * ln[l] for l in range(c) if l != k)
+            lt[k], ln[k] = contact_impulse(A[k][k][0], A[k][k][1], A[k][k][3], wt, wn, depth[k], mu)
+    vnew = np.stack([vfree[i] + sum(MiJt[k][i] * lt[k] + MiJn[k][i] * ln[k] for k in range(c)) for i in range(n)])
+    out = q + LG_H * vnew, vnew
+    return out + (np.stack(lt), np.stack(ln)) if return_impulses else out
+
+
+def physics(state, action, c, iters=LG_ITERS, assist=0.0):
+    """Four substeps from state (2(3+C), N) under the decoded per-leg torques (legged_np.py:121-128)."""
+    s = np.asarray(state)
+    d = 3 + c
+    q, v = s[:d], s[d:]
+    tq = torques(action, c)
+    for _ in range(LG_SUBSTEPS):
+        q, v = substep(q, v, tq, c, iters, assist=assist)
+    return np.concatenate([q, v])
+
+
+def terminated(state):
+    """Torso below 0.6 or tilted past 1 rad (legged_np.py:130-132)."""
+    return (state[1] < LG_FALL_HEIGHT) | (np.abs(state[2]) > LG_FALL_ANGLE)
+
+
+def reward(stepped, done, c):
+    """Forward velocity plus one, zero on the terminating step (legged_np.py:115-119)."""
+    return np.where(done, np.float32(0.0), stepped[3 + c] + np.float32(1.0)).astype(np.float32)
+
+
+def foot_heights(state, c):
+    """Height of every foot above the floor (C, N)."""
+    return state[1] - LG_L * np.cos(state[2] + state[3:3 + c])

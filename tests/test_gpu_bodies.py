@@ -1,0 +1,206 @@
+"""K-link pendulum (mass matrix, pairwise trig, warp-cooperative, articulated body), hopper and
+legged step kernels against the reference (golden) and the oracle, on a B200.
+
+Mirrors test_pendulum.py, test_pendulum_aba.py, test_hopper.py and test_legged.py of the
+reference: parity of live columns to tolerance with exact done flags on seeded random states,
+resets (here bit-exact against the oracle's hash stream) and chained steps."""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+from oracle import kernels, legged, pendulum
+from parity import check_step, record, to_np
+
+pytestmark = pytest.mark.gpu
+
+# The reference's own Metal gate is rtol = atol = 1e-3 (test_pendulum.py:76, test_legged.py:107).
+# These bodies are checked tighter; each test states its tolerance.
+
+
+def _pend_tol(k):
+    return (1e-5, 1e-5) if k <= 4 else (1e-4, 1e-4)
+
+
+@pytest.mark.parametrize("k", [2, 3, 4, 8, 16])
+@pytest.mark.parametrize("pairwise", [False, True])
+def test_mass_matrix_matches_reference(cuda, k, pairwise):
+    import pendulum_metal
+
+    g = golden("pendulum")
+    st, ac = g[f"state_k{k}"], g[f"action_k{k}"]
+    p = pendulum_metal.Pendulum(k, pairwise_trig=pairwise)
+    p.reseed(10)
+    out = p.step(torch.from_numpy(st).to(cuda), torch.from_numpy(ac).to(cuda))
+    onext, orew, _, _ = kernels.pendulum_step(st, ac, 11, k)
+    rtol, atol = _pend_tol(k)
+    check_step(f"pendulum_mm{'_pairwise' if pairwise else ''}_k{k}", out, g[f"mm_stepped_k{k}"], g[f"mm_done_k{k}"],
+               onext, rtol, atol, ref_reward=orew)
+
+
+@pytest.mark.parametrize("k", [2, 4, 8, 16])
+def test_cooperative_matches_reference(cuda, k):
+    import pendulum_metal_coop
+
+    g = golden("pendulum")
+    st, ac = g[f"state_k{k}"], g[f"action_k{k}"]
+    p = pendulum_metal_coop.Pendulum(k)
+    p.reseed(20)
+    out = p.step(torch.from_numpy(st).to(cuda), torch.from_numpy(ac).to(cuda))
+    onext, orew, _, _ = kernels.pendulum_step(st, ac, 21, k)
+    rtol, atol = _pend_tol(k)
+    check_step(f"pendulum_coop_k{k}", out, g[f"mm_stepped_k{k}"], g[f"mm_done_k{k}"], onext, rtol, atol,
+               ref_reward=orew)
+
+
+def test_cooperative_k32_matches_articulated_oracle(cuda):
+    """K = 32 has no mass-matrix golden (the reference's own numpy stops at 16 there); the
+    articulated-body reference is the same dynamics."""
+    import pendulum_metal_coop
+
+    g = golden("pendulum")
+    st, ac = g["state_k32"], g["action_k32"]
+    p = pendulum_metal_coop.Pendulum(32)
+    p.reseed(30)
+    out = p.step(torch.from_numpy(st).to(cuda), torch.from_numpy(ac).to(cuda))
+    onext, _, _, _ = kernels.pendulum_step(st, ac, 31, 32)
+    check_step("pendulum_coop_k32", out, g["aba_stepped_k32"], g["aba_done_k32"], onext, 1e-3, 1e-3)
+
+
+@pytest.mark.parametrize("k", [2, 3, 4, 8, 16, 32, 64])
+def test_articulated_body_matches_reference(cuda, k):
+    import pendulum_aba_metal
+
+    g = golden("pendulum")
+    st, ac = g[f"state_k{k}"], g[f"action_k{k}"]
+    p = pendulum_aba_metal.Pendulum(k)
+    p.reseed(40)
+    out = p.step(torch.from_numpy(st).to(cuda), torch.from_numpy(ac).to(cuda))
+    onext, _, _, _ = kernels.pendulum_step(st, ac, 41, k, form="aba")
+    rtol, atol = _pend_tol(k) if k <= 16 else (1e-3, 1e-3)
+    check_step(f"pendulum_aba_k{k}", out, g[f"aba_stepped_k{k}"], g[f"aba_done_k{k}"], onext, rtol, atol)
+
+
+def test_unsupported_k_raises(cuda):
+    import pendulum_aba_metal
+    import pendulum_metal
+
+    with pytest.raises(ValueError):
+        pendulum_metal.Pendulum(17).step(torch.zeros((34, 4), device=cuda), torch.ones(4, dtype=torch.int64, device=cuda))
+    with pytest.raises(ValueError):
+        pendulum_aba_metal.Pendulum(65).step(torch.zeros((130, 4), device=cuda), torch.ones(4, dtype=torch.int64, device=cuda))
+
+
+@pytest.mark.parametrize("cls_name", ["pendulum_metal", "pendulum_metal_coop", "pendulum_aba_metal"])
+def test_pendulum_resets_and_chain(cuda, cls_name):
+    mod = __import__(cls_name)
+    p = mod.Pendulum(4)
+    n = 4096
+    up = np.zeros((8, n), dtype=np.float32)
+    up[:4] = np.pi
+    a = torch.ones(n, dtype=torch.int32, device=cuda)
+    first = to_np(p.step(torch.from_numpy(up).to(cuda), a)[0])
+    second = to_np(p.step(torch.from_numpy(up).to(cuda), a)[0])
+    assert np.all(np.abs(first) <= 0.1) and not np.allclose(first, second)
+    assert abs(first.std() - 0.1 / np.sqrt(3)) < 0.002
+    state = p.reset(n)
+    gen = torch.Generator(device=cuda).manual_seed(0)
+    for _ in range(100):
+        state, _, _ = p.step(state, torch.randint(0, 3, (n,), device=cuda, generator=gen))
+    out = to_np(state)
+    assert np.isfinite(out).all() and np.all(np.abs(out[:4]) <= np.pi)
+
+
+# ---- hopper and legged ----------------------------------------------------------------------
+
+@pytest.mark.parametrize("branchy", [False, True])
+def test_hopper_matches_reference(cuda, branchy):
+    import hopper_metal
+
+    g = golden("hopper")
+    h = hopper_metal.Hopper(branchy=branchy)
+    h.reseed(50)
+    out = h.step(torch.from_numpy(g["state"]).to(cuda), torch.from_numpy(g["action"]).to(cuda))
+    onext, orew, _, _ = kernels.hopper_step(g["state"], g["action"], 51)
+    check_step(f"hopper{'_branchy' if branchy else ''}", out, g["stepped"], g["done"], onext, 1e-4, 1e-4,
+               ref_reward=orew)
+    contacts = (legged.foot_heights(g["state"], 1) <= 0).mean()
+    assert 0.2 < contacts < 0.8
+
+
+@pytest.mark.parametrize("c", [1, 2, 4])
+@pytest.mark.parametrize("iters", [1, 4, 8, 16])
+def test_legged_matches_reference(cuda, c, iters):
+    import legged_metal
+
+    g = golden("legged")
+    st, ac = g[f"state_c{c}"], g[f"action_c{c}"]
+    body = legged_metal.Legged(c, iters)
+    body.reseed(60)
+    out = body.step(torch.from_numpy(st).to(cuda), torch.from_numpy(ac).to(cuda))
+    onext, orew, _, _ = kernels.legged_step(st, ac, 61, c, iters)
+    check_step(f"legged_c{c}_i{iters}", out, g[f"stepped_c{c}_i{iters}"], g[f"done_c{c}_i{iters}"], onext, 1e-4, 1e-4,
+               ref_reward=orew)
+    touching = (legged.foot_heights(st, c) <= 0).mean()
+    assert 0.2 < touching < 0.8
+
+
+@pytest.mark.parametrize("as_tensor", [False, True])
+def test_legged_assist(cuda, as_tensor):
+    import legged_metal
+
+    g = golden("legged")
+    st, ac = g["state_c2"], g["action_c2"]
+    body = legged_metal.Legged(2)
+    body.reseed(70)
+    assist = torch.tensor([20.0], device=cuda) if as_tensor else 20.0
+    out = body.step(torch.from_numpy(st).to(cuda), torch.from_numpy(ac).to(cuda), assist)
+    ref = g["assist_stepped_c2"]
+    done = legged.terminated(ref)
+    onext, _, _, _ = kernels.legged_step(st, ac, 71, 2, assist=20.0)
+    check_step(f"legged_c2_assist_{'tensor' if as_tensor else 'float'}", out, ref, done, onext, 1e-4, 1e-4)
+
+
+def test_legged_resets_and_chain(cuda):
+    import legged_metal
+
+    p = legged_metal.Legged(4)
+    n = 2048
+    tilted = np.tile(legged.stand_pose(4)[:, None], (1, n))
+    tilted[2] = 2.0
+    a = torch.zeros(n, dtype=torch.int32, device=cuda)
+    first = to_np(p.step(torch.from_numpy(tilted).to(cuda), a)[0])
+    second = to_np(p.step(torch.from_numpy(tilted).to(cuda), a)[0])
+    assert np.all(np.abs(first - legged.stand_pose(4)[:, None]) <= 0.05 + 1e-7) and not np.allclose(first, second)
+    state = p.reset(n)
+    gen = torch.Generator(device=cuda).manual_seed(0)
+    worst = 0.0
+    for _ in range(100):
+        state, _, _ = p.step(state, torch.randint(0, 81, (n,), device=cuda, generator=gen))
+        worst = min(worst, float(legged.foot_heights(to_np(state), 4).min()))
+    assert np.isfinite(to_np(state)).all() and worst > -0.08
+    record("legged4_chain100", min_foot=worst)
+
+
+@pytest.mark.parametrize("c", [2, 4])
+def test_legged_trajectory_matches_oracle(cuda, c):
+    """50 chained steps from the reset pose against the oracle's chain with the same resets."""
+    import legged_metal
+
+    body = legged_metal.Legged(c)
+    n = 512
+    r = np.random.default_rng(c)
+    s_np = legged.stand_pose(c)[:, None] + r.uniform(-0.05, 0.05, (2 * (3 + c), n)).astype(np.float32)
+    acts = r.integers(0, 3**c, (50, n))
+    body.reseed(900)
+    s_gpu = torch.from_numpy(s_np).to(cuda)
+    flips, worst = 0, 0.0
+    for t in range(acts.shape[0]):
+        s_gpu, _, d_gpu = body.step(s_gpu, torch.from_numpy(acts[t]).to(cuda))
+        s_np, _, d_np, _ = kernels.legged_step(s_np, acts[t], 901 + t, c)
+        flips += int((to_np(d_gpu) != d_np).sum())
+        both_live = ~to_np(d_gpu) & ~d_np
+        worst = max(worst, float(np.abs(to_np(s_gpu)[:, both_live] - s_np[:, both_live]).max()))
+    record(f"legged{c}_traj50", done_flips=flips, max_abs=worst, n=n)
+    assert flips <= n // 100, flips

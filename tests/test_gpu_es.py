@@ -1,0 +1,171 @@
+"""ES generation kernels and the GPU es.py on a B200 (mirrors test_es.py of the reference)."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import es as oes
+from oracle import rng
+from parity import record, to_np
+
+pytestmark = pytest.mark.gpu
+
+
+def test_noise_matches_oracle(cuda):
+    import rlenv_lib as rl
+
+    rows, d = 300, 226
+    out = torch.empty((rows, d), device=cuda)
+    rl.check(rl.lib().es_noise(out.data_ptr(), rows, d, 12345, 7, 100, rl.stream_ptr()))
+    want = rng.noise(12345, 7, np.arange(100, 100 + rows), d)
+    got = to_np(out)
+    record("es_noise", max_abs=float(np.abs(got - want).max()))
+    np.testing.assert_allclose(got, want, rtol=1e-5, atol=2e-6)
+    assert abs(got.mean()) < 0.02 and abs(got.std() - 1) < 0.02
+
+
+def test_perturb_is_antithetic_and_matches_noise(cuda):
+    import rlenv_lib as rl
+
+    pairs, d, sigma = 64, 50, 0.1
+    theta = torch.from_numpy(np.random.default_rng(0).normal(size=d).astype(np.float32)).to(cuda)
+    pop = torch.empty((2 * pairs, d), device=cuda)
+    rl.check(rl.lib().es_perturb(theta.data_ptr(), d, sigma, 9, 3, pairs, 0, 2 * pairs, pop.data_ptr(), rl.stream_ptr()))
+    half = torch.empty((pairs, d), device=cuda)
+    rl.check(rl.lib().es_noise(half.data_ptr(), pairs, d, 9, 3, 0, rl.stream_ptr()))
+    th, p, h = to_np(theta), to_np(pop), to_np(half)
+    np.testing.assert_array_equal(p[:pairs], (th + (np.float32(sigma) * h)).astype(np.float32))
+    np.testing.assert_array_equal(p[pairs:], (th + (np.float32(sigma) * -h)).astype(np.float32))
+    shard = torch.empty((40, d), device=cuda)
+    rl.check(rl.lib().es_perturb(theta.data_ptr(), d, sigma, 9, 3, pairs, 50, 40, shard.data_ptr(), rl.stream_ptr()))
+    np.testing.assert_array_equal(to_np(shard), p[50:90])
+
+
+@pytest.mark.parametrize("p", [2, 3, 1000, 4096, 16384])
+def test_centered_ranks_stable(cuda, p):
+    import es
+
+    r = np.random.default_rng(p)
+    vals = r.integers(0, max(2, p // 8), p).astype(np.float32)  # many ties
+    got = to_np(es.centered_ranks(torch, torch.from_numpy(vals).to(cuda)))
+    np.testing.assert_allclose(got, oes.centered_ranks(vals, stable=True), atol=1e-7)
+    known = to_np(es.centered_ranks(torch, torch.tensor([3.0, 1.0, 2.0, 10.0], device=cuda)))
+    np.testing.assert_allclose(known, [1 / 6, -0.5, -1 / 6, 0.5], atol=1e-6)
+
+
+def test_update_matches_float64(cuda):
+    import rlenv_lib as rl
+
+    pairs, d, lr, sigma = 2048, 428, 0.03, 0.1
+    theta = torch.from_numpy(np.random.default_rng(1).normal(size=d).astype(np.float32) * 0.1).to(cuda)
+    ranks = torch.from_numpy(oes.centered_ranks(np.random.default_rng(2).normal(size=2 * pairs).astype(np.float32))).to(cuda)
+    out = torch.empty_like(theta)
+    rl.check(rl.lib().es_update(theta.data_ptr(), ranks.data_ptr(), d, pairs, lr, sigma, 5, 11, out.data_ptr(), rl.stream_ptr()))
+    half = torch.empty((pairs, d), device=cuda)
+    rl.check(rl.lib().es_noise(half.data_ptr(), pairs, d, 5, 11, 0, rl.stream_ptr()))
+    h = to_np(half).astype(np.float64)
+    rk = to_np(ranks).astype(np.float64)
+    eps = np.concatenate([h, -h])
+    want = to_np(theta) + lr * (rk[:, None] * eps).sum(0) / (2 * pairs * sigma)
+    got = to_np(out)
+    record("es_update", max_abs=float(np.abs(got - want).max()))
+    np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-6)
+    # fixed summation order: the same bits every call
+    out2 = torch.empty_like(theta)
+    rl.check(rl.lib().es_update(theta.data_ptr(), ranks.data_ptr(), d, pairs, lr, sigma, 5, 11, out2.data_ptr(), rl.stream_ptr()))
+    assert torch.equal(out, out2)
+
+
+def test_generation_uses_antithetic_pairs_and_moves_theta(cuda):
+    import es
+
+    cfg = es.Config(pop=8, horizon=5)
+    backend = es.MetalBackend(es.TASKS["cartpole"], 0)
+    theta = torch.zeros(es.n_params(4, es.TASKS["cartpole"]), device=cuda)
+    new, fit, steps = es.generation(backend, theta, cfg, 4)
+    assert fit.shape == (8,) and float(steps.max()) <= 5
+    assert not torch.allclose(new, torch.zeros_like(new))
+
+
+def test_generation_is_deterministic(cuda):
+    import es
+
+    task = es.TASKS["legged2"]
+    cfg = es.Config(task="legged2", pop=256, horizon=50)
+    outs = []
+    for _ in range(2):
+        backend = es.MetalBackend(task, 3)
+        theta = backend.normal((es.n_params(task.hidden, task),)) * 0.1
+        for gen in range(1, 4):
+            theta, fit, steps = es.generation(backend, theta, cfg, task.hidden, gen)
+        outs.append(theta)
+    assert torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("name,scale", [("cartpole", 0.5), ("acrobot", 0.5), ("legged2", 0.3), ("legged2_alive10_fall", 0.3)])
+def test_fused_kernel_matches_step_loop(cuda, name, scale):
+    """Same population, same initial states: the fused rollout and the step-by-step loop (torch
+    policy + CUDA step kernel) agree on reward sum and step count for almost every member."""
+    import es
+
+    task = es.TASKS[name]
+    pop, horizon = 1024, 200
+    theta = torch.from_numpy((np.random.default_rng(0).normal(size=(pop, es.n_params(task.hidden, task))) * scale)
+                             .astype(np.float32)).to(cuda)
+    backend = es.MLXBackend(task, 0)
+    state = backend.reset(pop, gen=5)
+    fk, sk = task.rollout(state, theta, task.hidden, horizon)
+    fl, sl = es.loop_fitness(backend, es.unflatten(theta, task.hidden, task), horizon, state=state)
+    fk, fl, sk, sl = to_np(fk), to_np(fl), to_np(sk), to_np(sl)
+    close = np.abs(fk - fl) <= 1e-3 * np.maximum(np.abs(fl), 1.0) + 1e-2
+    record(f"es_kernel_vs_loop_{name}", fitness_agree=float(close.mean()), steps_agree=float((sk == sl).mean()))
+    assert close.mean() > 0.95 and (sk == sl).mean() > 0.95, (close.mean(), (sk == sl).mean())
+    if name.startswith("legged"):
+        assert 5 < sl.mean() < 200
+
+
+def test_evaluate_theta_equals_actor_loop(cuda):
+    import es
+
+    for name in ("cartpole", "acrobot", "legged2"):
+        task = es.TASKS[name]
+        theta = torch.from_numpy((np.random.default_rng(4).normal(size=es.n_params(task.hidden, task)) * 0.3)
+                                 .astype(np.float32)).to(cuda)
+        state = es.MetalBackend(task, 0).reset(512, gen=9)
+        fused = es.evaluate_theta(task, theta, task.hidden, n=512, steps=200, state=state)
+        actor = es.mean_policy(theta, task.hidden, task)
+        # the loop from the same states: reuse evaluate's arithmetic with a fixed initial state
+        alive = torch.ones(512, dtype=torch.bool, device=cuda)
+        fit = torch.zeros(512, device=cuda)
+        s = state
+        for _ in range(200):
+            s, r, d = task.metal.step(s, task.action(torch, actor(task.obs(torch, s))))
+            alive = alive & ~d
+            fit = fit + (r - 1.0 + task.eval_bonus) * alive.float()
+        assert abs(fused - fit.mean().item()) <= 0.05 * max(1.0, abs(fused)), (name, fused, fit.mean().item())
+
+
+def test_es_learns_cartpole(cuda):
+    import es
+
+    r = es.train(es.Config(pop=256, time_budget=60.0, solved_at=150.0), "metal", seed=0)
+    record("es_cartpole_p256", solved=r.solved, generations=r.generations, score=r.score, seconds=r.train_seconds)
+    assert r.score >= 150.0, r
+
+
+def test_es_learns_acrobot(cuda):
+    import es
+
+    r = es.train(es.Config(task="acrobot", pop=4096, time_budget=60.0, solved_at=-250.0), "metal", seed=0)
+    record("es_acrobot_p4096", solved=r.solved, generations=r.generations, score=r.score, seconds=r.train_seconds)
+    assert r.score >= -250.0, r
+
+
+def test_es_biped_learns_to_stay_up(cuda):
+    import es
+
+    last = []
+    es.train(es.Config(task="legged2", pop=1024, time_budget=30.0, max_generations=60), "metal", seed=0,
+             log=lambda gen, steps, secs, fit, score: last.append(fit))
+    record("es_legged2_p1024_60gens", final_fitness=last[-1], generations=len(last))
+    assert last[-1] >= 300.0, last[-1]
