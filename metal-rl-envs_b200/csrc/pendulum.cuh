@@ -90,34 +90,46 @@ RLENV_D void mm_accel(const float (&th)[K], const float (&om)[K], float torque, 
 // q_i = t_i - t_{i-1}; each unit mass sits at (1, 0) of its link frame and
 // the next joint at (1, 0) too. Gravity enters as a base acceleration of -G.
 // Per link only the link velocity, U = I^A S and u are kept; the bias force
-// and the transform are recomputed.
+// and the transform are recomputed. The root link (joint at the base origin,
+// r = 0) is peeled out of every pass, so the loops over links 1..K-1 have no
+// special cases; they are fully unrolled up to K = 16 and left as loops above.
+
+// Calls f(i) for i = lo, lo+1, .., hi-1 (UP) or hi-1 down to lo; fully
+// unrolled when the range is short, a plain loop otherwise.
+template <int LO, int HI, bool UP, typename F>
+RLENV_D void for_links(F&& f) {
+  if constexpr (HI - LO <= 16) {
+#pragma unroll
+    for (int t = 0; t < HI - LO; ++t) f(UP ? LO + t : HI - 1 - t);
+  } else {
+#pragma unroll 1
+    for (int t = 0; t < HI - LO; ++t) f(UP ? LO + t : HI - 1 - t);
+  }
+}
+
 template <int K>
 RLENV_D void aba_accel(const float* th, const float* om, float torque, float* acc) {
   float vw[K], vx[K], vy[K], U0[K], U1[K], U2[K], uu[K];
-  // outward: link velocities v_i = X_i v_{i-1} + S qd_i
-  float pw = 0.0f, px = 0.0f, py = 0.0f;
-#pragma unroll 4
-  for (int i = 0; i < K; ++i) {
-    const float q = (i == 0) ? th[0] : th[i] - th[i - 1];
-    const float qd = (i == 0) ? om[0] : om[i] - om[i - 1];
+  // outward: link velocities v_i = X_i v_{i-1} + S qd_i; the root has v_0 = (qd_0, 0, 0)
+  vw[0] = om[0];
+  vx[0] = 0.0f;
+  vy[0] = 0.0f;
+  for_links<1, K, true>([&](int i) {
+    const float qd = om[i] - om[i - 1];
     float sn, cs;
-    sincosf(q, &sn, &cs);
-    const float xy = (i == 0) ? py : py + pw;  // joint at (r, 0), r = 0 at the root and 1 elsewhere
+    sincosf(th[i] - th[i - 1], &sn, &cs);
+    const float pw = vw[i - 1], px = vx[i - 1], xy = vy[i - 1] + pw;  // joint at (1, 0)
     vw[i] = pw + qd;
     vx[i] = cs * px + sn * xy;
     vy[i] = -sn * px + cs * xy;
-    pw = vw[i];
-    px = vx[i];
-    py = vy[i];
-  }
+  });
   // inward: articulated inertia and bias force of the subtree, carried to the
   // parent as the child's contribution (cA, cp)
   float cA00 = 0.0f, cA01 = 0.0f, cA02 = 0.0f, cA11 = 0.0f, cA12 = 0.0f, cA22 = 0.0f;
   float cp0 = 0.0f, cp1 = 0.0f, cp2 = 0.0f;
-#pragma unroll 4
-  for (int i = K - 1; i >= 0; --i) {
+  for_links<1, K, false>([&](int i) {
     const float w = vw[i], x = vx[i], y = vy[i];
-    const float qd = (i == 0) ? om[0] : om[i] - om[i - 1];
+    const float qd = om[i] - om[i - 1];
     // own bias p = v x* (I v), I of a unit mass at (1, 0) = [[1,0,1],[0,1,0],[1,0,1]]
     const float fy = w + y;
     const float p0 = (x * fy - y * x) + cp0;
@@ -128,8 +140,7 @@ RLENV_D void aba_accel(const float* th, const float* om, float torque, float* ac
     U0[i] = a00;
     U1[i] = a01;
     U2[i] = a02;
-    uu[i] = ((i == 0) ? torque : 0.0f) - p0;
-    if (i == 0) break;
+    uu[i] = -p0;
     const float D = a00;
     const float Ia00 = a00 - a00 * a00 / D, Ia01 = a01 - a00 * a01 / D, Ia02 = a02 - a00 * a02 / D;
     const float Ia11 = a11 - a01 * a01 / D, Ia12 = a12 - a01 * a02 / D, Ia22 = a22 - a02 * a02 / D;
@@ -153,26 +164,41 @@ RLENV_D void aba_accel(const float* th, const float* om, float torque, float* ac
     cp0 = pa0 + sn * pa1 + cs * pa2;
     cp1 = cs * pa1 - sn * pa2;
     cp2 = sn * pa1 + cs * pa2;
+  });
+  {  // root link: its inertia and bias with the whole chain's contribution
+    const float w = vw[0], x = vx[0], y = vy[0];
+    const float fy = w + y;
+    U0[0] = 1.0f + cA00;
+    U1[0] = cA01;
+    U2[0] = 1.0f + cA02;
+    uu[0] = torque - ((x * fy - y * x) + cp0);
   }
-  // outward: accelerations, the base accelerating at -G; absolute angular
+  // outward: accelerations, the base accelerating at -G; the absolute angular
   // accelerations are the running sum of the joint accelerations
-  float aw = 0.0f, ax = -pd::G, ay = 0.0f, run = 0.0f;
-#pragma unroll 4
-  for (int i = 0; i < K; ++i) {
-    const float q = (i == 0) ? th[0] : th[i] - th[i - 1];
-    const float qd = (i == 0) ? om[0] : om[i] - om[i - 1];
+  float sn0, cs0;
+  sincosf(th[0], &sn0, &cs0);
+  const float qd0 = om[0];
+  // root: X_0 maps the base acceleration (0, -G, 0); r = 0
+  float ax = cs0 * -pd::G + qd0 * vy[0];
+  float ay = -sn0 * -pd::G - qd0 * vx[0];
+  float qdd = (uu[0] - (U0[0] * 0.0f + U1[0] * ax + U2[0] * ay)) / U0[0];
+  float aw = 0.0f + qdd;
+  float run = qdd;
+  acc[0] = run;
+  for_links<1, K, true>([&](int i) {
+    const float qd = om[i] - om[i - 1];
     float sn, cs;
-    sincosf(q, &sn, &cs);
-    const float xy = (i == 0) ? ay : ay + aw;
+    sincosf(th[i] - th[i - 1], &sn, &cs);
+    const float xy = ay + aw;
     const float ap1 = cs * ax + sn * xy + qd * vy[i];
     const float ap2 = -sn * ax + cs * xy - qd * vx[i];
-    const float qdd = (uu[i] - (U0[i] * aw + U1[i] * ap1 + U2[i] * ap2)) / U0[i];
-    aw = aw + qdd;
+    const float q2 = (uu[i] - (U0[i] * aw + U1[i] * ap1 + U2[i] * ap2)) / U0[i];
+    aw = aw + q2;
     ax = ap1;
     ay = ap2;
-    run += qdd;
+    run += q2;
     acc[i] = run;
-  }
+  });
 }
 
 // ---- RK4 step on (theta, omega) (pendulum_np.py:60-66) -----------------------

@@ -33,11 +33,25 @@ def nvcc():
     return exe
 
 
-def _stale(src, obj, headers):
+def _includes(path, seen=None):
+    """Every local header a source reaches through #include "..." (recursively)."""
+    import re
+
+    seen = set() if seen is None else seen
+    for name in re.findall(r'^#include "([^"]+)"', path.read_text(), flags=re.M):
+        for d in (CSRC, INCLUDE):
+            h = d / name
+            if h.exists() and h not in seen:
+                seen.add(h)
+                _includes(h, seen)
+    return seen
+
+
+def _stale(src, obj):
     if not obj.exists():
         return True
     t = obj.stat().st_mtime
-    return src.stat().st_mtime > t or any(h.stat().st_mtime > t for h in headers)
+    return src.stat().st_mtime > t or any(h.stat().st_mtime > t for h in _includes(src))
 
 
 def _compile(src, obj, extra, verbose):
@@ -54,9 +68,8 @@ def build(verbose=False, ptxas_verbose=False, jobs=None):
     """Compile every csrc/*.cu for sm_100a and link librlenv.so. Returns its path."""
     OBJ.mkdir(exist_ok=True)
     sources = sorted(CSRC.glob("*.cu"))
-    headers = sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h"))
     extra = ["-Xptxas", "-v"] if ptxas_verbose else []
-    todo = [s for s in sources if ptxas_verbose or _stale(s, OBJ / (s.stem + ".o"), headers)]
+    todo = [s for s in sources if ptxas_verbose or _stale(s, OBJ / (s.stem + ".o"))]
     logs = {}
     if todo:
         with concurrent.futures.ThreadPoolExecutor(max_workers=jobs or min(len(todo), os.cpu_count() or 4)) as ex:
