@@ -2,38 +2,72 @@
 // `cartpole_step` / `acrobot_step` Metal kernels, and T-step kernels that keep
 // the state in registers across steps.
 //
-// Both are streaming kernels: per environment-step they read 16 B of state and
-// one action and write 16 B of state, a 4 B reward and a 1 B done flag. When
-// N is a multiple of 4 and every buffer is 16-byte aligned, each thread owns 4
-// consecutive environments and moves them with 16-byte vector accesses;
-// otherwise one environment per thread.
+// Per environment-step the single-step kernels read 16 B of state and one
+// action and write 16 B of state, a 4 B reward and a 1 B done flag; the T-step
+// kernels move the state once per launch and per step only the action, reward
+// and flag. CartPole threads own 4 consecutive environments (16-byte vector
+// accesses) when N is a multiple of 4 and every buffer is 16-byte aligned;
+// Acrobot, whose RK4 step is bound by instruction issue, owns one per thread.
 #include "classic.cuh"
 
 namespace rlenv {
 namespace {
 
+// Each environment advances one state in place by one step: physics,
+// termination, the masked reset from the hash stream, the reward. `Aux` is
+// whatever the next step can reuse from this one (Acrobot: the sines and
+// cosines of the stepped state, which its termination test computes and its
+// next first RK4 stage needs). kVec is the number of consecutive environments
+// a thread owns: 4 (16-byte accesses) where the step is light enough to be
+// bound by memory, 1 where it is bound by instruction issue and the
+// occupancy of one environment per thread hides latency better.
 struct CartPoleEnv {
   using S = CartPole;
-  static constexpr float kBound = cp::RESET_BOUND;
+  struct Aux {};
+  static constexpr int kVec = 4;
   RLENV_D static S from(const float (&r)[4]) { return S{r[0], r[1], r[2], r[3]}; }
   RLENV_D static void to(const S& s, float (&r)[4]) {
     r[0] = s.x; r[1] = s.xd; r[2] = s.th; r[3] = s.thd;
   }
-  RLENV_D static S physics(const S& s, int a) { return cartpole_physics(s, cartpole_force(a)); }
-  RLENV_D static bool terminated(const S& s) { return cartpole_terminated(s); }
-  RLENV_D static float reward(bool) { return 1.0f; }
+  RLENV_D static Aux aux(const S&) { return Aux{}; }
+  RLENV_D static bool step(S& s, Aux&, int a, uint32_t h, float& reward) {
+    const S nx = cartpole_physics(s, cartpole_force(a));
+    const bool d = cartpole_terminated(nx);
+    s.x = d ? uniform_pm(pcg_hash(h + classic_row_offset(0)), cp::RESET_BOUND) : nx.x;
+    s.xd = d ? uniform_pm(pcg_hash(h + classic_row_offset(1)), cp::RESET_BOUND) : nx.xd;
+    s.th = d ? uniform_pm(pcg_hash(h + classic_row_offset(2)), cp::RESET_BOUND) : nx.th;
+    s.thd = d ? uniform_pm(pcg_hash(h + classic_row_offset(3)), cp::RESET_BOUND) : nx.thd;
+    reward = 1.0f;
+    return d;
+  }
 };
 
 struct AcrobotEnv {
   using S = Acrobot;
-  static constexpr float kBound = ac::RESET_BOUND;
+  using Aux = AcrobotTrig;
+  static constexpr int kVec = 1;
   RLENV_D static S from(const float (&r)[4]) { return S{r[0], r[1], r[2], r[3]}; }
   RLENV_D static void to(const S& s, float (&r)[4]) {
     r[0] = s.th1; r[1] = s.th2; r[2] = s.dth1; r[3] = s.dth2;
   }
-  RLENV_D static S physics(const S& s, int a) { return acrobot_physics(s, float(a - 1)); }
-  RLENV_D static bool terminated(const S& s) { return acrobot_terminated(s); }
-  RLENV_D static float reward(bool d) { return d ? 0.0f : -1.0f; }
+  RLENV_D static Aux aux(const S& s) { return acrobot_trig(s); }
+  RLENV_D static bool step(S& s, Aux& t, int a, uint32_t h, float& reward) {
+    const S nx = acrobot_physics(s, t, float(a - 1));
+    const Aux tn = acrobot_trig(nx);
+    const bool d = acrobot_terminated(tn);
+    if (d) {  // rare under random actions: the fresh state's trig only on this branch
+      s = S{uniform_pm(pcg_hash(h + classic_row_offset(0)), ac::RESET_BOUND),
+            uniform_pm(pcg_hash(h + classic_row_offset(1)), ac::RESET_BOUND),
+            uniform_pm(pcg_hash(h + classic_row_offset(2)), ac::RESET_BOUND),
+            uniform_pm(pcg_hash(h + classic_row_offset(3)), ac::RESET_BOUND)};
+      t = acrobot_trig(s);
+    } else {
+      s = nx;
+      t = tn;
+    }
+    reward = d ? 0.0f : -1.0f;
+    return d;
+  }
 };
 
 // Load V consecutive actions starting at element `i` (i is a multiple of V).
@@ -98,46 +132,28 @@ RLENV_D void store_flags(uint8_t* __restrict__ p, int64_t i, const bool (&d)[V])
     for (int u = 0; u < V; ++u) p[i + u] = d[u];
 }
 
-// Advance V environments one step in registers: physics, termination, masked
-// reset from the PCG stream. Returns the done flags and rewards.
 template <typename Env, int V>
-RLENV_D void advance(float (&st)[4][V], const int (&act)[V], uint32_t seed, int64_t gidx,
-                     bool (&d)[V], float (&rw)[V]) {
+RLENV_D void load_states(const float* __restrict__ s, int64_t n, int64_t i, typename Env::S (&st)[V]) {
+  float rows[4][V];
+  load_rows<V>(s, n, i, rows);
 #pragma unroll
   for (int u = 0; u < V; ++u) {
-    float cur[4] = {st[0][u], st[1][u], st[2][u], st[3][u]};
-    typename Env::S nx = Env::physics(Env::from(cur), act[u]);
-    const bool dn = Env::terminated(nx);
-    float out[4];
-    Env::to(nx, out);
-    const uint32_t h = env_hash(seed, gidx + u);
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const float fresh = uniform_pm(pcg_hash(h + classic_row_offset(r)), Env::kBound);
-      st[r][u] = dn ? fresh : out[r];
-    }
-    d[u] = dn;
-    rw[u] = Env::reward(dn);
+    const float r[4] = {rows[0][u], rows[1][u], rows[2][u], rows[3][u]};
+    st[u] = Env::from(r);
   }
 }
 
-template <typename Env, typename A, int V>
-__global__ void __launch_bounds__(kThreads)
-step_kernel(const float* __restrict__ state, const A* __restrict__ action, uint32_t seed, int64_t n,
-            int64_t off, float* __restrict__ next, float* __restrict__ reward,
-            uint8_t* __restrict__ done) {
-  const int64_t i = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) * V;
-  if (i >= n) return;
-  float st[4][V];
-  int act[V];
-  load_rows<V>(state, n, i, st);
-  load_actions<A, V>(action, i, act);
-  bool d[V];
-  float rw[V];
-  advance<Env, V>(st, act, seed, off + i, d, rw);
-  store_rows<V>(next, n, i, st);
-  store_vec<V>(reward, i, rw);
-  store_flags<V>(done, i, d);
+template <typename Env, int V>
+RLENV_D void store_states(float* __restrict__ s, int64_t n, int64_t i, const typename Env::S (&st)[V]) {
+  float rows[4][V];
+#pragma unroll
+  for (int u = 0; u < V; ++u) {
+    float r[4];
+    Env::to(st[u], r);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) rows[k][u] = r[k];
+  }
+  store_rows<V>(s, n, i, rows);
 }
 
 template <typename Env, typename A, int V>
@@ -148,17 +164,23 @@ step_many_kernel(const float* __restrict__ state_in, const A* __restrict__ actio
                  float* __restrict__ reward_sum, float* __restrict__ done_count) {
   const int64_t i = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) * V;
   if (i >= n) return;
-  float st[4][V];
-  load_rows<V>(state_in, n, i, st);
+  typename Env::S st[V];
+  typename Env::Aux aux[V];
+  load_states<Env, V>(state_in, n, i, st);
   float rsum[V], dcnt[V];
 #pragma unroll
-  for (int u = 0; u < V; ++u) rsum[u] = dcnt[u] = 0.0f;
+  for (int u = 0; u < V; ++u) {
+    aux[u] = Env::aux(st[u]);
+    rsum[u] = dcnt[u] = 0.0f;
+  }
   for (int64_t t = 0; t < T; ++t) {
     int act[V];
     load_actions<A, V>(actions, t * n + i, act);
     bool d[V];
     float rw[V];
-    advance<Env, V>(st, act, seed0 + uint32_t(t), off + i, d, rw);
+#pragma unroll
+    for (int u = 0; u < V; ++u)
+      d[u] = Env::step(st[u], aux[u], act[u], env_hash(seed0 + uint32_t(t), off + i + u), rw[u]);
     if (reward_seq) store_vec<V>(reward_seq, t * n + i, rw);
     if (done_seq) store_flags<V>(done_seq, t * n + i, d);
 #pragma unroll
@@ -167,36 +189,12 @@ step_many_kernel(const float* __restrict__ state_in, const A* __restrict__ actio
       dcnt[u] += d[u] ? 1.0f : 0.0f;
     }
   }
-  store_rows<V>(state_out, n, i, st);
+  store_states<Env, V>(state_out, n, i, st);
   if (reward_sum) store_vec<V>(reward_sum, i, rsum);
   if (done_count) store_vec<V>(done_count, i, dcnt);
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-
-template <typename Env>
-int launch_step(const float* state, const void* action, int dtype, uint32_t seed, int64_t n,
-                int64_t off, float* next, float* reward, uint8_t* done, void* stream) {
-  if (n < 0 || !valid_dtype(dtype)) return RLENV_EINVAL;
-  if (n == 0) return RLENV_OK;
-  if (!state || !action || !next || !reward || !done) return RLENV_EINVAL;
-  const int esz = dtype == RLENV_I64 ? 8 : dtype == RLENV_I32 ? 4 : 1;
-  const bool vec = (n % 4 == 0) && aligned16(state) && aligned16(next) && aligned16(reward) &&
-                   (reinterpret_cast<uintptr_t>(done) & 3u) == 0 &&
-                   (reinterpret_cast<uintptr_t>(action) % (4 * esz)) == 0 && dtype != RLENV_I64;
-  cudaStream_t s = as_stream(stream);
-  return with_action_type(dtype, [&](auto tag) {
-    using A = std::remove_const_t<std::remove_pointer_t<decltype(tag)>>;
-    const A* a = static_cast<const A*>(action);
-    if (vec)
-      step_kernel<Env, A, 4><<<grid_for(n / 4), kThreads, 0, s>>>(state, a, seed, n, off, next,
-                                                                  reward, done);
-    else
-      step_kernel<Env, A, 1><<<grid_for(n), kThreads, 0, s>>>(state, a, seed, n, off, next, reward,
-                                                              done);
-    return launch_status();
-  });
-}
 
 template <typename Env>
 int launch_step_many(const float* state_in, const void* actions, int dtype, uint32_t seed0,
@@ -206,23 +204,37 @@ int launch_step_many(const float* state_in, const void* actions, int dtype, uint
   if (n == 0) return RLENV_OK;
   if (!state_in || !state_out || (T > 0 && !actions)) return RLENV_EINVAL;
   const int esz = dtype == RLENV_I64 ? 8 : dtype == RLENV_I32 ? 4 : 1;
-  const bool vec = (n % 4 == 0) && aligned16(state_in) && aligned16(state_out) &&
+  const bool vec = Env::kVec == 4 && (n % 4 == 0) && aligned16(state_in) && aligned16(state_out) &&
                    (!reward_seq || aligned16(reward_seq)) &&
                    (!done_seq || (reinterpret_cast<uintptr_t>(done_seq) & 3u) == 0) &&
                    (!reward_sum || aligned16(reward_sum)) && (!done_count || aligned16(done_count)) &&
-                   (reinterpret_cast<uintptr_t>(actions) % (4 * esz)) == 0 && dtype != RLENV_I64;
+                   (dtype == RLENV_I64 || (reinterpret_cast<uintptr_t>(actions) % (4 * esz)) == 0);
   cudaStream_t s = as_stream(stream);
   return with_action_type(dtype, [&](auto tag) {
     using A = std::remove_const_t<std::remove_pointer_t<decltype(tag)>>;
     const A* a = static_cast<const A*>(actions);
-    if (vec)
-      step_many_kernel<Env, A, 4><<<grid_for(n / 4), kThreads, 0, s>>>(
-          state_in, a, seed0, T, n, off, state_out, reward_seq, done_seq, reward_sum, done_count);
-    else
-      step_many_kernel<Env, A, 1><<<grid_for(n), kThreads, 0, s>>>(
-          state_in, a, seed0, T, n, off, state_out, reward_seq, done_seq, reward_sum, done_count);
+    if constexpr (Env::kVec == 4) {
+      if (vec) {
+        step_many_kernel<Env, A, 4><<<grid_for(n / 4), kThreads, 0, s>>>(
+            state_in, a, seed0, T, n, off, state_out, reward_seq, done_seq, reward_sum, done_count);
+        return launch_status();
+      }
+    }
+    step_many_kernel<Env, A, 1><<<grid_for(n), kThreads, 0, s>>>(
+        state_in, a, seed0, T, n, off, state_out, reward_seq, done_seq, reward_sum, done_count);
     return launch_status();
   });
+}
+
+// One step is the T-step kernel with T = 1, writing the step's reward and done
+// flag as its one-row sequences: a chain of single-step calls and one T-step
+// call then run the same machine code and agree bit for bit.
+template <typename Env>
+int launch_step(const float* state, const void* action, int dtype, uint32_t seed, int64_t n,
+                int64_t off, float* next, float* reward, uint8_t* done, void* stream) {
+  if (n > 0 && (!state || !action || !next || !reward || !done)) return RLENV_EINVAL;
+  return launch_step_many<Env>(state, action, dtype, seed, 1, n, off, next, reward, done, nullptr,
+                               nullptr, stream);
 }
 
 }  // namespace

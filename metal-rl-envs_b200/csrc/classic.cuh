@@ -75,35 +75,55 @@ struct Acrobot {
   float th1, th2, dth1, dth2;
 };
 
-// Gym AcrobotEnv._dsdt with the torque passed alongside (acrobot_np.py:64-86).
-RLENV_D Acrobot acrobot_dsdt(const Acrobot& s, float torque) {
-  float s2, c2;
-  sincosf(s.th2, &s2, &c2);
-  float d1 = ac::D1_CONST + (ac::D1_INNER + c2) + 1.0f + 1.0f;  // m2 (l1^2 + lc2^2 + 2 l1 lc2 c2) + I1 + I2
-  float d2 = (ac::D2_CONST + 0.5f * c2) + 1.0f;                 // m2 (lc2^2 + l1 lc2 c2) + I2
-  float phi2 = ac::PHI2_K * cosf(s.th1 + s.th2 - ac::HALF_PI);
-  float phi1 = -0.5f * (s.dth2 * s.dth2) * s2 - s.dth2 * s.dth1 * s2 +
-               ac::PHI1_K * cosf(s.th1 - ac::HALF_PI) + phi2;
-  float dd2 = (torque + d2 / d1 * phi1 - 0.5f * (s.dth1 * s.dth1) * s2 - phi2) /
-              (ac::DENOM_CONST - (d2 * d2) / d1);
-  float dd1 = -(d2 * dd2 + phi1) / d1;
+// Sines and cosines of both angles of an Acrobot state. Every derivative
+// evaluation needs exactly these: the reference's cos(theta1 + theta2 - pi/2)
+// and cos(theta1 - pi/2) are sin(theta1 + theta2) and sin(theta1), and the
+// former comes from the addition formula. The termination test of a stepped
+// state needs them too, and they are then the first RK4 stage's of the next
+// step, so a chain of steps evaluates them once per state.
+struct AcrobotTrig {
+  float s1, c1, s2, c2;
+};
+
+RLENV_D AcrobotTrig acrobot_trig(const Acrobot& s) {
+  AcrobotTrig t;
+  sincosf(s.th1, &t.s1, &t.c1);
+  sincosf(s.th2, &t.s2, &t.c2);
+  return t;
+}
+
+// Gym AcrobotEnv._dsdt with the torque passed alongside (acrobot_np.py:64-86),
+// rearranged to two divides: dd2 = (torque + d2/d1 phi1 - 0.5 w1^2 s2 - phi2) /
+// (1.25 - d2^2/d1) multiplied through by d1.
+RLENV_D Acrobot acrobot_dsdt(const Acrobot& s, const AcrobotTrig& t, float torque) {
+  const float s12 = t.s1 * t.c2 + t.c1 * t.s2;
+  const float d1 = ac::D1_CONST + (ac::D1_INNER + t.c2) + 1.0f + 1.0f;  // m1 lc1^2 + m2 (l1^2 + lc2^2 + 2 l1 lc2 c2) + I1 + I2
+  const float d2 = (ac::D2_CONST + 0.5f * t.c2) + 1.0f;                 // m2 (lc2^2 + l1 lc2 c2) + I2
+  const float phi2 = ac::PHI2_K * s12;
+  const float phi1 = -0.5f * (s.dth2 * s.dth2) * t.s2 - s.dth2 * s.dth1 * t.s2 + ac::PHI1_K * t.s1 + phi2;
+  const float num = d1 * (torque - 0.5f * (s.dth1 * s.dth1) * t.s2 - phi2) + d2 * phi1;
+  const float dd2 = num / (ac::DENOM_CONST * d1 - d2 * d2);
+  const float dd1 = -(d2 * dd2 + phi1) / d1;
   return Acrobot{s.dth1, s.dth2, dd1, dd2};
 }
 
 // Angle to [-pi, pi) without branches (acrobot_np.py:88-90).
 RLENV_D float wrap_angle(float x) { return x - ac::TWO_PI * floorf((x + ac::PI) / ac::TWO_PI); }
 
-RLENV_D Acrobot acrobot_physics(const Acrobot& s, float torque) {
-  Acrobot k1 = acrobot_dsdt(s, torque);
-  Acrobot s2{s.th1 + ac::HALF_DT * k1.th1, s.th2 + ac::HALF_DT * k1.th2,
-             s.dth1 + ac::HALF_DT * k1.dth1, s.dth2 + ac::HALF_DT * k1.dth2};
-  Acrobot k2 = acrobot_dsdt(s2, torque);
-  Acrobot s3{s.th1 + ac::HALF_DT * k2.th1, s.th2 + ac::HALF_DT * k2.th2,
-             s.dth1 + ac::HALF_DT * k2.dth1, s.dth2 + ac::HALF_DT * k2.dth2};
-  Acrobot k3 = acrobot_dsdt(s3, torque);
-  Acrobot s4{s.th1 + ac::DT * k3.th1, s.th2 + ac::DT * k3.th2, s.dth1 + ac::DT * k3.dth1,
-             s.dth2 + ac::DT * k3.dth2};
-  Acrobot k4 = acrobot_dsdt(s4, torque);
+RLENV_D Acrobot acrobot_stage(const Acrobot& s, const Acrobot& k, float h) {
+  return Acrobot{s.th1 + h * k.th1, s.th2 + h * k.th2, s.dth1 + h * k.dth1, s.dth2 + h * k.dth2};
+}
+
+// One RK4 step of dt 0.2, then wrap and clip (acrobot_np.py:47-61). t0 is the
+// trig of s.
+RLENV_D Acrobot acrobot_physics(const Acrobot& s, const AcrobotTrig& t0, float torque) {
+  const Acrobot k1 = acrobot_dsdt(s, t0, torque);
+  const Acrobot s2 = acrobot_stage(s, k1, ac::HALF_DT);
+  const Acrobot k2 = acrobot_dsdt(s2, acrobot_trig(s2), torque);
+  const Acrobot s3 = acrobot_stage(s, k2, ac::HALF_DT);
+  const Acrobot k3 = acrobot_dsdt(s3, acrobot_trig(s3), torque);
+  const Acrobot s4 = acrobot_stage(s, k3, ac::DT);
+  const Acrobot k4 = acrobot_dsdt(s4, acrobot_trig(s4), torque);
   Acrobot n;
   n.th1 = wrap_angle(s.th1 + ac::SIXTH_DT * (k1.th1 + 2.0f * k2.th1 + 2.0f * k3.th1 + k4.th1));
   n.th2 = wrap_angle(s.th2 + ac::SIXTH_DT * (k1.th2 + 2.0f * k2.th2 + 2.0f * k3.th2 + k4.th2));
@@ -114,9 +134,10 @@ RLENV_D Acrobot acrobot_physics(const Acrobot& s, float torque) {
   return n;
 }
 
-// The tip above height 1 (acrobot_np.py:92-93).
-RLENV_D bool acrobot_terminated(const Acrobot& s) {
-  return -cosf(s.th1) - cosf(s.th2 + s.th1) > 1.0f;
+// The tip above height 1: -cos t1 - cos(t1 + t2) > 1 (acrobot_np.py:92-93),
+// from the state's trig.
+RLENV_D bool acrobot_terminated(const AcrobotTrig& t) {
+  return -t.c1 - (t.c1 * t.c2 - t.s1 * t.s2) > 1.0f;
 }
 
 }  // namespace rlenv

@@ -112,6 +112,9 @@ RLENV_D float noise_at(uint64_t seed, uint64_t gen, int64_t pair, int64_t j) {
   return v[j & 3];
 }
 
+// Index of element (i, j), j <= i, of a lower triangle stored row by row.
+RLENV_HD constexpr int tri(int i, int j) { return i * (i + 1) / 2 + j; }
+
 // ---------------------------------------------------------------------------
 inline int grid_for(int64_t threads, int block = kThreads) {
   int64_t g = (threads + block - 1) / block;

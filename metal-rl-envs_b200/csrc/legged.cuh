@@ -6,7 +6,6 @@
 #pragma once
 
 #include "common.cuh"
-#include "pendulum.cuh"  // tri()
 
 namespace rlenv {
 namespace lg {

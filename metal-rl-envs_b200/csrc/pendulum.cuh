@@ -19,9 +19,26 @@ constexpr float TWO_PI = 6.283185307179586f;
 constexpr float RESET_BOUND = 0.1f;
 }  // namespace pd
 
-RLENV_HD constexpr int tri(int i, int j) { return i * (i + 1) / 2 + j; }
-
 RLENV_D float pd_wrap(float x) { return x - pd::TWO_PI * floorf((x + pd::PI) / pd::TWO_PI); }
+
+// Calls f(i) for i = 0 .. N-1, fully unrolled when UNROLL, as a plain loop
+// otherwise. A per-environment array is either always indexed by constants
+// (unrolled: it lives in registers) or always by the loop variable (local
+// memory): every loop that touches the arrays of one K uses the same UNROLL,
+// never a mix of the two.
+template <int N, bool UNROLL, typename F>
+RLENV_D void for_range(F&& f) {
+  if constexpr (UNROLL) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) f(i);
+  } else {
+#pragma unroll 1
+    for (int i = 0; i < N; ++i) f(i);
+  }
+}
+
+// K-link arrays stay in registers (fully unrolled loops) up to this size.
+constexpr int kUnrollLinks = 16;
 
 // ---- mass-matrix accelerations (pendulum_np.py:68-111) ---------------------
 // M_ij = mu_ij cos(t_i - t_j), mu_ij = K - max(i, j); rhs_i = -sum_j mu_ij
@@ -94,27 +111,113 @@ RLENV_D void mm_accel(const float (&th)[K], const float (&om)[K], float torque, 
 // r = 0) is peeled out of every pass, so the loops over links 1..K-1 have no
 // special cases; they are fully unrolled up to K = 16 and left as loops above.
 
-// Calls f(i) for i = lo, lo+1, .., hi-1 (UP) or hi-1 down to lo; fully
-// unrolled when the range is short, a plain loop otherwise.
-template <int LO, int HI, bool UP, typename F>
+// Calls f(i) for i = LO .. HI-1 (UP) or HI-1 down to LO, unrolled as for_range.
+template <int LO, int HI, bool UP, bool UNROLL, typename F>
 RLENV_D void for_links(F&& f) {
-  if constexpr (HI - LO <= 16) {
-#pragma unroll
-    for (int t = 0; t < HI - LO; ++t) f(UP ? LO + t : HI - 1 - t);
-  } else {
-#pragma unroll 1
-    for (int t = 0; t < HI - LO; ++t) f(UP ? LO + t : HI - 1 - t);
+  for_range<HI - LO, UNROLL>([&](int t) { f(UP ? LO + t : HI - 1 - t); });
+}
+
+// The same three passes as plain loops over per-link arrays in local memory,
+// for chains too long to unroll (K > kUnrollLinks). It is kept out of line: when
+// nvcc inlined these loops into the RK4 driver, whose stage arrays they index
+// by the loop variable, the optimised device code returned wrong accelerations
+// for K >= 24 although every single evaluation was right; the same source is
+// correct out of line, without NVVM optimisation (-Xcicc -O0), under -G, and
+// compiled for the host.
+template <int K>
+__device__ __noinline__ void aba_accel_loops(const float* th, const float* om, float torque,
+                                             float* acc) {
+  float vw[K], vx[K], vy[K], U0[K], U1[K], U2[K], uu[K];
+  vw[0] = om[0];
+  vx[0] = 0.0f;
+  vy[0] = 0.0f;
+  for (int i = 1; i < K; ++i) {
+    const float qd = om[i] - om[i - 1];
+    float sn, cs;
+    sincosf(th[i] - th[i - 1], &sn, &cs);
+    const float pw = vw[i - 1], px = vx[i - 1], xy = vy[i - 1] + pw;
+    vw[i] = pw + qd;
+    vx[i] = cs * px + sn * xy;
+    vy[i] = -sn * px + cs * xy;
+  }
+  float cA00 = 0.0f, cA01 = 0.0f, cA02 = 0.0f, cA11 = 0.0f, cA12 = 0.0f, cA22 = 0.0f;
+  float cp0 = 0.0f, cp1 = 0.0f, cp2 = 0.0f;
+  for (int i = K - 1; i >= 1; --i) {
+    const float w = vw[i], x = vx[i], y = vy[i];
+    const float qd = om[i] - om[i - 1];
+    const float fy = w + y;
+    const float p0 = (x * fy - y * x) + cp0, p1 = (-w * fy) + cp1, p2 = (w * x) + cp2;
+    const float a00 = 1.0f + cA00, a01 = cA01, a02 = 1.0f + cA02;
+    const float a11 = 1.0f + cA11, a12 = cA12, a22 = 1.0f + cA22;
+    U0[i] = a00;
+    U1[i] = a01;
+    U2[i] = a02;
+    uu[i] = -p0;
+    const float D = a00;
+    const float Ia00 = a00 - a00 * a00 / D, Ia01 = a01 - a00 * a01 / D, Ia02 = a02 - a00 * a02 / D;
+    const float Ia11 = a11 - a01 * a01 / D, Ia12 = a12 - a01 * a02 / D, Ia22 = a22 - a02 * a02 / D;
+    const float c1 = qd * y, c2 = -qd * x;
+    const float g = uu[i] / D;
+    const float pa0 = p0 + (Ia01 * c1 + Ia02 * c2) + a00 * g;
+    const float pa1 = p1 + (Ia11 * c1 + Ia12 * c2) + a01 * g;
+    const float pa2 = p2 + (Ia12 * c1 + Ia22 * c2) + a02 * g;
+    float sn, cs;
+    sincosf(th[i] - th[i - 1], &sn, &cs);
+    const float B00 = Ia00 + Ia01 * sn + Ia02 * cs, B01 = Ia01 * cs - Ia02 * sn, B02 = Ia01 * sn + Ia02 * cs;
+    const float B10 = Ia01 + Ia11 * sn + Ia12 * cs, B11 = Ia11 * cs - Ia12 * sn, B12 = Ia11 * sn + Ia12 * cs;
+    const float B20 = Ia02 + Ia12 * sn + Ia22 * cs, B21 = Ia12 * cs - Ia22 * sn, B22 = Ia12 * sn + Ia22 * cs;
+    cA00 = B00 + sn * B10 + cs * B20;
+    cA01 = B01 + sn * B11 + cs * B21;
+    cA02 = B02 + sn * B12 + cs * B22;
+    cA11 = cs * B11 - sn * B21;
+    cA12 = cs * B12 - sn * B22;
+    cA22 = sn * B12 + cs * B22;
+    cp0 = pa0 + sn * pa1 + cs * pa2;
+    cp1 = cs * pa1 - sn * pa2;
+    cp2 = sn * pa1 + cs * pa2;
+  }
+  {
+    const float w = vw[0], x = vx[0], y = vy[0], fy = w + y;
+    U0[0] = 1.0f + cA00;
+    U1[0] = cA01;
+    U2[0] = 1.0f + cA02;
+    uu[0] = torque - ((x * fy - y * x) + cp0);
+  }
+  float sn0, cs0;
+  sincosf(th[0], &sn0, &cs0);
+  float ax = cs0 * -pd::G + om[0] * vy[0];
+  float ay = -sn0 * -pd::G - om[0] * vx[0];
+  const float qdd = (uu[0] - (U0[0] * 0.0f + U1[0] * ax + U2[0] * ay)) / U0[0];
+  float aw = 0.0f + qdd, run = qdd;
+  acc[0] = run;
+  for (int i = 1; i < K; ++i) {
+    const float qd = om[i] - om[i - 1];
+    float sn, cs;
+    sincosf(th[i] - th[i - 1], &sn, &cs);
+    const float xy = ay + aw;
+    const float ap1 = cs * ax + sn * xy + qd * vy[i];
+    const float ap2 = -sn * ax + cs * xy - qd * vx[i];
+    const float q2 = (uu[i] - (U0[i] * aw + U1[i] * ap1 + U2[i] * ap2)) / U0[i];
+    aw = aw + q2;
+    ax = ap1;
+    ay = ap2;
+    run += q2;
+    acc[i] = run;
   }
 }
 
 template <int K>
 RLENV_D void aba_accel(const float* th, const float* om, float torque, float* acc) {
+  if constexpr (K > kUnrollLinks) {
+    aba_accel_loops<K>(th, om, torque, acc);
+    return;
+  }
   float vw[K], vx[K], vy[K], U0[K], U1[K], U2[K], uu[K];
   // outward: link velocities v_i = X_i v_{i-1} + S qd_i; the root has v_0 = (qd_0, 0, 0)
   vw[0] = om[0];
   vx[0] = 0.0f;
   vy[0] = 0.0f;
-  for_links<1, K, true>([&](int i) {
+  for_links<1, K, true, (K <= kUnrollLinks)>([&](int i) {
     const float qd = om[i] - om[i - 1];
     float sn, cs;
     sincosf(th[i] - th[i - 1], &sn, &cs);
@@ -127,7 +230,7 @@ RLENV_D void aba_accel(const float* th, const float* om, float torque, float* ac
   // parent as the child's contribution (cA, cp)
   float cA00 = 0.0f, cA01 = 0.0f, cA02 = 0.0f, cA11 = 0.0f, cA12 = 0.0f, cA22 = 0.0f;
   float cp0 = 0.0f, cp1 = 0.0f, cp2 = 0.0f;
-  for_links<1, K, false>([&](int i) {
+  for_links<1, K, false, (K <= kUnrollLinks)>([&](int i) {
     const float w = vw[i], x = vx[i], y = vy[i];
     const float qd = om[i] - om[i - 1];
     // own bias p = v x* (I v), I of a unit mass at (1, 0) = [[1,0,1],[0,1,0],[1,0,1]]
@@ -185,7 +288,7 @@ RLENV_D void aba_accel(const float* th, const float* om, float torque, float* ac
   float aw = 0.0f + qdd;
   float run = qdd;
   acc[0] = run;
-  for_links<1, K, true>([&](int i) {
+  for_links<1, K, true, (K <= kUnrollLinks)>([&](int i) {
     const float qd = om[i] - om[i - 1];
     float sn, cs;
     sincosf(th[i] - th[i - 1], &sn, &cs);
@@ -204,47 +307,42 @@ RLENV_D void aba_accel(const float* th, const float* om, float torque, float* ac
 // ---- RK4 step on (theta, omega) (pendulum_np.py:60-66) -----------------------
 // The angle derivative is omega itself, so only the accelerations need the
 // dynamics. Returns wrapped angles and clipped velocities in th, om.
-template <int K, typename Accel>
+template <int K, bool UNROLL, typename Accel>
 RLENV_D void pendulum_rk4(float (&th)[K], float (&om)[K], float torque, Accel accel) {
   float ts[K], os[K], a[K], dth[K], dom[K];
   accel(th, om, torque, a);  // k1 = (om, a1)
-#pragma unroll
-  for (int j = 0; j < K; ++j) {
+  for_range<K, UNROLL>([&](int j) {
     dth[j] = om[j];
     dom[j] = a[j];
     ts[j] = th[j] + pd::HALF_DT * om[j];
     os[j] = om[j] + pd::HALF_DT * a[j];
-  }
+  });
   accel(ts, os, torque, a);  // k2 = (os, a2)
-#pragma unroll
-  for (int j = 0; j < K; ++j) {
+  for_range<K, UNROLL>([&](int j) {
     dth[j] += 2.0f * os[j];
     dom[j] += 2.0f * a[j];
     ts[j] = th[j] + pd::HALF_DT * os[j];
     os[j] = om[j] + pd::HALF_DT * a[j];
-  }
+  });
   accel(ts, os, torque, a);  // k3
-#pragma unroll
-  for (int j = 0; j < K; ++j) {
+  for_range<K, UNROLL>([&](int j) {
     dth[j] += 2.0f * os[j];
     dom[j] += 2.0f * a[j];
     ts[j] = th[j] + pd::DT * os[j];
     os[j] = om[j] + pd::DT * a[j];
-  }
+  });
   accel(ts, os, torque, a);  // k4
-#pragma unroll
-  for (int j = 0; j < K; ++j) {
+  for_range<K, UNROLL>([&](int j) {
     th[j] = pd_wrap(th[j] + pd::SIXTH_DT * (dth[j] + os[j]));
     om[j] = fminf(fmaxf(om[j] + pd::SIXTH_DT * (dom[j] + a[j]), -pd::MAX_VEL), pd::MAX_VEL);
-  }
+  });
 }
 
 // The tip above half the chain's length: -sum_j cos t_j > K / 2.
-template <int K>
+template <int K, bool UNROLL>
 RLENV_D bool pendulum_terminated(const float (&th)[K]) {
   float h = 0.0f;
-#pragma unroll
-  for (int j = 0; j < K; ++j) h += cosf(th[j]);
+  for_range<K, UNROLL>([&](int j) { h += cosf(th[j]); });
   return -h > float(K) * 0.5f;
 }
 

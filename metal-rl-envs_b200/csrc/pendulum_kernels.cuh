@@ -28,32 +28,32 @@ __global__ void __launch_bounds__(128)
 pendulum_kernel(const float* __restrict__ state, const void* __restrict__ action, int dtype,
                 uint32_t seed, int64_t n, int64_t off, float* __restrict__ next,
                 float* __restrict__ reward, uint8_t* __restrict__ done) {
+  constexpr bool U = K <= kUnrollLinks;  // one indexing style for every per-link array of this K
   const int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (e >= n) return;
   float th[K], om[K];
-#pragma unroll
-  for (int j = 0; j < K; ++j) {
+  for_range<K, U>([&](int j) {
     th[j] = __ldg(state + j * n + e);
     om[j] = __ldg(state + (K + j) * n + e);
-  }
+  });
   const float torque = float(action_at(action, dtype, e) - 1) * pd::TORQUE;
-  if (FORM == ARTICULATED) {
-    pendulum_rk4<K>(th, om, torque, [](const float* t, const float* o, float tq, float* a) {
+  if constexpr (FORM == ARTICULATED) {
+    pendulum_rk4<K, U>(th, om, torque, [](const float* t, const float* o, float tq, float* a) {
       aba_accel<K>(t, o, tq, a);
     });
   } else {
-    pendulum_rk4<K>(th, om, torque,
-                    [](const float (&t)[K], const float (&o)[K], float tq, float (&a)[K]) {
-                      mm_accel<K, FORM == MASS_MATRIX_PAIRWISE>(t, o, tq, a);
-                    });
+    pendulum_rk4<K, U>(th, om, torque,
+                       [](const float (&t)[K], const float (&o)[K], float tq, float (&a)[K]) {
+                         mm_accel<K, FORM == MASS_MATRIX_PAIRWISE>(t, o, tq, a);
+                       });
   }
-  const bool d = pendulum_terminated<K>(th);
+  const bool d = pendulum_terminated<K, U>(th);
   const uint32_t h = env_hash(seed, off + e);
-#pragma unroll
-  for (int j = 0; j < 2 * K; ++j) {
-    const float fresh = uniform_pm(pcg_hash(h + uint32_t(j) * kRowStride), pd::RESET_BOUND);
-    next[j * n + e] = d ? fresh : (j < K ? th[j] : om[j - K]);
-  }
+  for_range<K, U>([&](int j) {
+    next[j * n + e] = d ? uniform_pm(pcg_hash(h + uint32_t(j) * kRowStride), pd::RESET_BOUND) : th[j];
+    next[(K + j) * n + e] =
+        d ? uniform_pm(pcg_hash(h + uint32_t(K + j) * kRowStride), pd::RESET_BOUND) : om[j];
+  });
   reward[e] = d ? 0.0f : -1.0f;
   done[e] = d;
 }

@@ -113,15 +113,15 @@ acrobot_rollout_kernel(const float* __restrict__ state, const float* __restrict_
             __ldg(state + 3 * p + m)};
   float survived = 0.0f;
   bool alive = true;
+  // the observation is (cos t1, sin t1, cos t2, sin t2, w1, w2): the state's trig, which the
+  // first RK4 stage and the previous step's termination test use too
+  AcrobotTrig tr = acrobot_trig(s);
   for (int step = 0; step < horizon; ++step) {
     if (!__any_sync(kFull, alive)) break;
-    float s1, c1, s2, c2;
-    sincosf(s.th1, &s1, &c1);
-    sincosf(s.th2, &s2, &c2);
     float l0 = 0.0f, l1 = 0.0f, l2 = 0.0f;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const float hdn = tanhf(c1 * w1[0][u] + s1 * w1[1][u] + c2 * w1[2][u] + s2 * w1[3][u] +
+      const float hdn = tanhf(tr.c1 * w1[0][u] + tr.s1 * w1[1][u] + tr.c2 * w1[2][u] + tr.s2 * w1[3][u] +
                               s.dth1 * w1[4][u] + s.dth2 * w1[5][u] + w1[6][u]);
       l0 += hdn * w2[0][u];
       l1 += hdn * w2[1][u];
@@ -131,8 +131,9 @@ acrobot_rollout_kernel(const float* __restrict__ state, const float* __restrict_
     l1 = group_sum<G>(l1) + b2_1;
     l2 = group_sum<G>(l2) + b2_2;
     if (alive) {
-      s = acrobot_physics(s, float(argmax3(l0, l1, l2) - 1));
-      if (acrobot_terminated(s)) alive = false;
+      s = acrobot_physics(s, tr, float(argmax3(l0, l1, l2) - 1));
+      tr = acrobot_trig(s);
+      if (acrobot_terminated(tr)) alive = false;
       else survived += 1.0f;
     }
   }

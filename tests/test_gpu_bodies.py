@@ -82,6 +82,22 @@ def test_articulated_body_matches_reference(cuda, k):
     check_step(f"pendulum_aba_k{k}", out, g[f"aba_stepped_k{k}"], g[f"aba_done_k{k}"], onext, rtol, atol)
 
 
+@pytest.mark.parametrize("k", [24, 48])
+def test_articulated_body_long_chains_match_oracle(cuda, k):
+    """K values with no golden vector: the oracle (itself pinned to the reference's numpy at
+    K = 2..64) on seeded states of the reference test's distribution."""
+    import pendulum_aba_metal
+
+    r = np.random.default_rng(k)
+    st = np.concatenate([r.uniform(-np.pi, np.pi, (k, 64)), r.uniform(-1, 1, (k, 64))]).astype(np.float32)
+    ac = r.integers(0, 3, 64)
+    p = pendulum_aba_metal.Pendulum(k)
+    p.reseed(45)
+    out = p.step(torch.from_numpy(st).to(cuda), torch.from_numpy(ac).to(cuda))
+    onext, _, odone, stepped = kernels.pendulum_step(st, ac, 46, k, form="aba")
+    check_step(f"pendulum_aba_k{k}", out, stepped, odone, onext, 1e-3, 1e-3)
+
+
 def test_unsupported_k_raises(cuda):
     import pendulum_aba_metal
     import pendulum_metal
