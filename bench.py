@@ -50,6 +50,18 @@ N_ENVS = 262_144
 T_STEPS = 1000
 METRIC = "env steps/s"
 WORKLOAD = "acrobot_batched_step"
+# workload -> (config it measures, default N, default T)
+WORKLOADS = {
+    "acrobot_step": ("BASELINE configs[1]: Acrobot batched step", N_ENVS, T_STEPS),
+    "cartpole_step": ("BASELINE configs[0]: CartPole batched step, T-step kernel", 131_072, T_STEPS),
+    "pendulum_aba": ("BASELINE configs[2]: K-link pendulum, articulated body", 65_536, 100),
+    "pendulum_mm": ("BASELINE configs[2]: K-link pendulum, mass matrix", 65_536, 100),
+    "pendulum_coop": ("BASELINE configs[2]: K-link pendulum, K lanes per env", 65_536, 100),
+    "legged_step": ("BASELINE configs[3]: legged body with C contacts", N_ENVS, 50),
+    "es_cartpole": ("BASELINE configs[4]: ES generation, CartPole P=4096 H=32 horizon 500", 4096, 500),
+    "es_acrobot": ("BASELINE configs[4]: ES generation, Acrobot P=4096 H=32 horizon 500", 4096, 500),
+    "es_legged4": ("BASELINE configs[4]: ES generation, legged4 P=16384 H=16 horizon 1000", 16_384, 1000),
+}
 
 
 def parse():
@@ -62,6 +74,14 @@ def parse():
     p.add_argument("--t", type=int, default=T_STEPS, help="environment steps per bench step")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--workload", default="acrobot_step", choices=sorted(WORKLOADS),
+                   help="acrobot_step is the default line (BASELINE.json configs[1]); the others measure "
+                        "the remaining configs for the design record")
+    p.add_argument("--k", type=int, default=16, help="pendulum links (pendulum workloads)")
+    p.add_argument("--c", type=int, default=4, help="legs (legged workload)")
+    p.add_argument("--iters", type=int, default=8, help="Gauss-Seidel sweeps (legged workload)")
+    p.add_argument("--pop", type=int, default=None, help="ES population (es_* workloads)")
+    p.add_argument("--horizon", type=int, default=None, help="ES horizon (es_* workloads)")
     return p.parse_args()
 
 
@@ -187,11 +207,10 @@ def measured_sgemm_tflops(torch):
         n = 8192
         a = torch.randn(n, n, device="cuda")
         b = torch.randn(n, n, device="cuda")
-        for _ in range(2):
-            a @ b
+        a @ b
         torch.cuda.synchronize()
         best = float("inf")
-        for _ in range(5):
+        for _ in range(3):
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
             a @ b
@@ -378,10 +397,190 @@ def run_ours(args):
     print(json.dumps(line), flush=True)
 
 
+# ---- the other configurations --------------------------------------------------------------------
+
+def _setup_dist(torch):
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+    return dist, rank, world, local, dev
+
+
+def _timed(torch, dist, world, stream, fn, steps, warmup, local):
+    """Run fn() warmup times, then time `steps` calls with CUDA events on `stream` inside
+    barriers; returns (max-over-ranks seconds, clock summary)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        a.record(stream)
+        for _ in range(steps):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t = torch.tensor([a.elapsed_time(b) / 1e3], device=stream.device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item()), clocks.summary()
+
+
+def _graph_steps(torch, launch_one, T):
+    """A CUDA graph of T single-step launches (launch_one(t) enqueues step t on the current
+    stream): one replay runs T per-step kernel launches without host overhead."""
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for t in range(T):  # warm the launches once outside the capture
+            launch_one(t)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    with torch.cuda.graph(g):
+        for t in range(T):
+            launch_one(t)
+    torch.cuda.synchronize()
+    return g
+
+
+def run_workload(args):
+    import torch
+
+    import rlenv_flops
+    import rlenv_lib as rl
+
+    dist, rank, world, local, dev = _setup_dist(torch)
+    lib = rl.load()
+    desc, n_def, t_def = WORKLOADS[args.workload]
+    n = args.n if args.n != N_ENVS else n_def
+    T = args.t if args.t != T_STEPS else t_def
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    g = torch.Generator(device=dev).manual_seed(4321 + rank)
+    extra = {}
+    sgemm = measured_sgemm_tflops(torch) if rank == 0 else None
+    if args.workload == "cartpole_step":
+        actions = torch.randint(0, 2, (T, n), device=dev, generator=g).to(torch.uint8)
+        s0 = rl.reset_uniform(4, n, 0.05, seed=7, index_offset=rank * n, dev=dev)
+        s1 = torch.empty_like(s0)
+        rew, dn = torch.empty((T, n), device=dev), torch.empty((T, n), device=dev, dtype=torch.bool)
+
+        def fn():
+            rl.check(lib.cartpole_step_many(s0.data_ptr(), actions.data_ptr(), rl.U8, 1, T, n, rank * n,
+                                            s1.data_ptr(), rew.data_ptr(), dn.data_ptr(), 0, 0, sp))
+        units, unit, metric, flops = n * T, "env steps/s", METRIC, rlenv_flops.CARTPOLE["flops"]
+        bytes_launch = rlenv_flops.step_many_bytes(4, n, T)
+    elif args.workload in ("pendulum_aba", "pendulum_mm", "pendulum_coop", "legged_step"):
+        if args.workload == "legged_step":
+            c = args.c
+            rows, n_act = 2 * (3 + c), 3 ** c
+            import legged_metal
+
+            stand = torch.from_numpy(legged_metal.stand_pose(c)).to(dev)
+            state_a = rl.reset_uniform(rows, n, 0.05, center=stand, seed=3, index_offset=rank * n, dev=dev)
+
+            def entry(src, dst, t, r, d):
+                rl.check(lib.legged_step(c, args.iters, src.data_ptr(), actions[t].data_ptr(), rl.U8, 1 + t,
+                                         stand.data_ptr(), 0.0, None, n, rank * n, dst.data_ptr(), r.data_ptr(),
+                                         d.data_ptr(), torch.cuda.current_stream().cuda_stream))
+            fl = rlenv_flops.legged_flops(c, args.iters)["flops"]
+            extra = {"legs": c, "sweeps": args.iters}
+        else:
+            k = args.k
+            rows, n_act = 2 * k, 3
+            state_a = rl.reset_uniform(rows, n, 0.1, seed=3, index_offset=rank * n, dev=dev)
+            fn_name = {"pendulum_aba": "pendulum_aba_step", "pendulum_mm": "pendulum_mm_step",
+                       "pendulum_coop": "pendulum_coop_step"}[args.workload]
+            head = (k, 0) if args.workload == "pendulum_mm" else (k,)
+            abi = getattr(lib, fn_name)
+
+            def entry(src, dst, t, r, d):
+                rl.check(abi(*head, src.data_ptr(), actions[t].data_ptr(), rl.U8, 1 + t, n, rank * n, dst.data_ptr(),
+                             r.data_ptr(), d.data_ptr(), torch.cuda.current_stream().cuda_stream))
+            fl = (rlenv_flops.aba_flops(k) if args.workload == "pendulum_aba" else rlenv_flops.mass_matrix_flops(k))["flops"]
+            extra = {"links": k}
+        actions = torch.randint(0, n_act, (T, n), device=dev, generator=g).to(torch.uint8 if n_act < 256 else torch.int32)
+        state_b = torch.empty_like(state_a)
+        rew, dn = torch.empty((T, n), device=dev), torch.empty((T, n), device=dev, dtype=torch.bool)
+
+        def launch_one(t):
+            src, dst = (state_a, state_b) if t % 2 == 0 else (state_b, state_a)
+            entry(src, dst, t, rew[t], dn[t])
+        graph = _graph_steps(torch, launch_one, T)
+
+        def fn():
+            graph.replay()
+        units, unit, metric, flops = n * T, "env steps/s", METRIC, fl
+        bytes_launch = n * T * (2 * 4 * rows + 1 + 5)
+    else:  # es_*
+        import es
+
+        task = {"es_cartpole": "cartpole", "es_acrobot": "acrobot", "es_legged4": "legged4"}[args.workload]
+        pop = args.pop or n_def
+        horizon = args.horizon or t_def
+        cfg = es.Config(task=task, pop=pop, horizon=horizon, sigma=0.1, lr=0.03)
+        backend = es.MetalBackend(es.TASKS[task], 0)
+        hidden = es.TASKS[task].hidden
+        state = {"theta": backend.normal((es.n_params(hidden, es.TASKS[task]),)) * 0.1, "gen": 0, "steps": 0.0}
+
+        def fn():
+            state["gen"] += 1
+            state["theta"], fit, steps = es.generation(backend, state["theta"], cfg, hidden, state["gen"])
+            state["steps"] += float(steps.sum().item())
+        for _ in range(args.warmup):
+            fn()
+        state["steps"] = 0.0
+        secs, clocks = _timed(torch, dist, world, stream, fn, args.steps, 0, local)
+        value = 1e3 * secs / args.steps
+        if rank == 0:
+            line = {"metric": "ES generation ms", "value": value, "unit": "ms", "n_gpus": world, "steps": args.steps,
+                    "warmup": args.warmup, "ms_per_step": value, "higher_is_better": False, "scaling": "strong",
+                    "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded parameters and initial states)",
+                    "config": {"workload": args.workload, "config": desc, "population": pop, "horizon": horizon,
+                               "hidden": hidden, "sigma": 0.1, "lr": 0.03,
+                               "env_steps_per_s": state["steps"] * world / secs if world == 1 else None,
+                               "env_steps_taken_rank0": state["steps"]},
+                    "clocks": clocks}
+            print(json.dumps(line), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    secs, clocks = _timed(torch, dist, world, stream, fn, args.steps, args.warmup, local)
+    per = secs / args.steps
+    if rank == 0:
+        achieved = flops * units / per / 1e12
+        line = {"metric": metric, "value": world * units * args.steps / secs, "unit": unit, "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * per, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": args.workload, "config": desc, "n_envs_per_gpu": n, "env_steps_per_step": T, **extra},
+                "roofline": {"bound": "fp32", "achieved": achieved, "peak": sgemm, "unit": "TFLOP/s",
+                             "frac": achieved / sgemm if sgemm else None, "flops_per_env_step": flops,
+                             "hbm": {"achieved": bytes_launch / per / 1e9, "peak": hbm_peak_gbs()[0], "unit": "GB/s"}},
+                "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload != "acrobot_step":
+        run_workload(args)
     else:
         run_ours(args)
 
