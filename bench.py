@@ -495,7 +495,7 @@ def run_workload(args):
             def entry(src, dst, t, r, d):
                 rl.check(lib.legged_step(c, args.iters, src.data_ptr(), actions[t].data_ptr(), rl.U8, 1 + t,
                                          stand.data_ptr(), 0.0, None, n, rank * n, dst.data_ptr(), r.data_ptr(),
-                                         d.data_ptr(), torch.cuda.current_stream().cuda_stream))
+                                         d.data_ptr(), None, torch.cuda.current_stream().cuda_stream))
             fl = rlenv_flops.legged_flops(c, args.iters)["flops"]
             extra = {"legs": c, "sweeps": args.iters}
         else:

@@ -129,11 +129,16 @@ RLENV_API int rlenv_pendulum_aba_step(int k, const float* state, const void* act
  * |phi| > 1; reset to stand (2(3+c) floats, device) plus uniform +-0.05 on every
  * row. assist_ptr (device, one float) overrides `assist` when not NULL: it is
  * the stiffness of the torso-upright spring-damper of the curriculum.
+ * impulses (2c, n), when not NULL, receives per foot k the tangential (row 2k)
+ * and normal (row 2k + 1) contact impulse summed over the step's four
+ * substeps: the (lt, ln) of legged_np.py:89-96. The reference's step does not
+ * return them; BASELINE.json asks for them among the step's outputs.
  * Built for c in 1..4; iters >= 1. */
 RLENV_API int rlenv_legged_step(int c, int iters, const float* state, const void* action, int action_dtype,
                       uint32_t seed, const float* stand, float assist, const float* assist_ptr,
                       int64_t n, int64_t index_offset,
-                      float* next_state, float* reward, uint8_t* done, void* stream);
+                      float* next_state, float* reward, uint8_t* done, float* impulses,
+                      void* stream);
 
 /* Hopper: the one-legged body with an exact single-contact solve, equal to the
  * legged body with c = 1 and one sweep. Replaces `hopper_step` and

@@ -8,6 +8,8 @@
 // and flag. CartPole threads own 4 consecutive environments (16-byte vector
 // accesses) when N is a multiple of 4 and every buffer is 16-byte aligned;
 // Acrobot, whose RK4 step is bound by instruction issue, owns one per thread.
+#include <type_traits>
+
 #include "classic.cuh"
 
 namespace rlenv {
@@ -20,11 +22,13 @@ namespace {
 // next first RK4 stage needs). kVec is the number of consecutive environments
 // a thread owns: 4 (16-byte accesses) where the step is light enough to be
 // bound by memory, 1 where it is bound by instruction issue and the
-// occupancy of one environment per thread hides latency better.
+// occupancy of one environment per thread hides latency better. kMinBlocks is
+// the launch bound on resident 256-thread blocks per SM.
 struct CartPoleEnv {
   using S = CartPole;
   struct Aux {};
   static constexpr int kVec = 4;
+  static constexpr int kMinBlocks = 1;
   RLENV_D static S from(const float (&r)[4]) { return S{r[0], r[1], r[2], r[3]}; }
   RLENV_D static void to(const S& s, float (&r)[4]) {
     r[0] = s.x; r[1] = s.xd; r[2] = s.th; r[3] = s.thd;
@@ -46,6 +50,9 @@ struct AcrobotEnv {
   using S = Acrobot;
   using Aux = AcrobotTrig;
   static constexpr int kVec = 1;
+  // 8 resident blocks of 256 threads (at most 32 registers): the whole batch of a
+  // 262,144-environment launch is resident at once instead of 1.15 waves
+  static constexpr int kMinBlocks = 8;
   RLENV_D static S from(const float (&r)[4]) { return S{r[0], r[1], r[2], r[3]}; }
   RLENV_D static void to(const S& s, float (&r)[4]) {
     r[0] = s.th1; r[1] = s.th2; r[2] = s.dth1; r[3] = s.dth2;
@@ -156,8 +163,10 @@ RLENV_D void store_states(float* __restrict__ s, int64_t n, int64_t i, const typ
   store_rows<V>(s, n, i, rows);
 }
 
-template <typename Env, typename A, int V>
-__global__ void __launch_bounds__(kThreads)
+// SUMS selects the instance that also accumulates per-environment reward sums
+// and termination counts; the plain chain keeps those registers free.
+template <typename Env, typename A, int V, bool SUMS>
+__global__ void __launch_bounds__(kThreads, Env::kMinBlocks)
 step_many_kernel(const float* __restrict__ state_in, const A* __restrict__ actions, uint32_t seed0,
                  int64_t T, int64_t n, int64_t off, float* __restrict__ state_out,
                  float* __restrict__ reward_seq, uint8_t* __restrict__ done_seq,
@@ -173,25 +182,34 @@ step_many_kernel(const float* __restrict__ state_in, const A* __restrict__ actio
     aux[u] = Env::aux(st[u]);
     rsum[u] = dcnt[u] = 0.0f;
   }
+  // the next step's actions are loaded one step ahead, so their latency hides behind a step
+  int act[V];
+  if (T > 0) load_actions<A, V>(actions, i, act);
   for (int64_t t = 0; t < T; ++t) {
-    int act[V];
-    load_actions<A, V>(actions, t * n + i, act);
+    int nxt[V] = {};
+    if (t + 1 < T) load_actions<A, V>(actions, (t + 1) * n + i, nxt);
     bool d[V];
     float rw[V];
 #pragma unroll
     for (int u = 0; u < V; ++u)
       d[u] = Env::step(st[u], aux[u], act[u], env_hash(seed0 + uint32_t(t), off + i + u), rw[u]);
+#pragma unroll
+    for (int u = 0; u < V; ++u) act[u] = nxt[u];
     if (reward_seq) store_vec<V>(reward_seq, t * n + i, rw);
     if (done_seq) store_flags<V>(done_seq, t * n + i, d);
+    if constexpr (SUMS) {
 #pragma unroll
-    for (int u = 0; u < V; ++u) {
-      rsum[u] += rw[u];
-      dcnt[u] += d[u] ? 1.0f : 0.0f;
+      for (int u = 0; u < V; ++u) {
+        rsum[u] += rw[u];
+        dcnt[u] += d[u] ? 1.0f : 0.0f;
+      }
     }
   }
   store_states<Env, V>(state_out, n, i, st);
-  if (reward_sum) store_vec<V>(reward_sum, i, rsum);
-  if (done_count) store_vec<V>(done_count, i, dcnt);
+  if constexpr (SUMS) {
+    if (reward_sum) store_vec<V>(reward_sum, i, rsum);
+    if (done_count) store_vec<V>(done_count, i, dcnt);
+  }
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -213,16 +231,20 @@ int launch_step_many(const float* state_in, const void* actions, int dtype, uint
   return with_action_type(dtype, [&](auto tag) {
     using A = std::remove_const_t<std::remove_pointer_t<decltype(tag)>>;
     const A* a = static_cast<const A*>(actions);
-    if constexpr (Env::kVec == 4) {
-      if (vec) {
-        step_many_kernel<Env, A, 4><<<grid_for(n / 4), kThreads, 0, s>>>(
-            state_in, a, seed0, T, n, off, state_out, reward_seq, done_seq, reward_sum, done_count);
-        return launch_status();
+    auto go = [&](auto sums) {
+      constexpr bool S = decltype(sums)::value;
+      if constexpr (Env::kVec == 4) {
+        if (vec) {
+          step_many_kernel<Env, A, 4, S><<<grid_for(n / 4), kThreads, 0, s>>>(
+              state_in, a, seed0, T, n, off, state_out, reward_seq, done_seq, reward_sum, done_count);
+          return launch_status();
+        }
       }
-    }
-    step_many_kernel<Env, A, 1><<<grid_for(n), kThreads, 0, s>>>(
-        state_in, a, seed0, T, n, off, state_out, reward_seq, done_seq, reward_sum, done_count);
-    return launch_status();
+      step_many_kernel<Env, A, 1, S><<<grid_for(n), kThreads, 0, s>>>(
+          state_in, a, seed0, T, n, off, state_out, reward_seq, done_seq, reward_sum, done_count);
+      return launch_status();
+    };
+    return (reward_sum || done_count) ? go(std::true_type{}) : go(std::false_type{});
   });
 }
 

@@ -133,7 +133,7 @@ const char* rlenv_strerror(int code) {
   return "unknown rlenv status";
 }
 
-int rlenv_abi_version(void) { return 1; }
+int rlenv_abi_version(void) { return 2; }
 
 int rlenv_es_noise(float* half, int64_t rows, int64_t d, uint64_t seed, uint64_t gen,
                    int64_t row_offset, void* stream) {

@@ -112,10 +112,12 @@ RLENV_D void cholesky_solve(const float (&Lm)[n * (n + 1) / 2], const float (&in
   }
 }
 
-// One substep of H for C legs (legged_np.py:57-97), in place on q and v.
-template <int C, bool BRANCHY>
+// One substep of H for C legs (legged_np.py:57-97), in place on q and v. With
+// IMPULSES, each contact's final (lt, ln) of the substep is added to imp[2k],
+// imp[2k + 1].
+template <int C, bool BRANCHY, bool IMPULSES = false>
 RLENV_D void legged_substep(float (&q)[3 + C], float (&v)[3 + C], const float (&tq)[C],
-                            float assist, int iters) {
+                            float assist, int iters, float* imp = nullptr) {
   constexpr int n = 3 + C;
   float lca[C], lsa[C], dx[C], dy[C], depth[C];
 #pragma unroll
@@ -254,6 +256,13 @@ RLENV_D void legged_substep(float (&q)[3 + C], float (&v)[3 + C], const float (&
     for (int k = 0; k < C; ++k) vi += MiJt[k][i] * lt[k] + MiJn[k][i] * ln[k];
     v[i] = vf[i] + vi;
     q[i] += lg::H * v[i];
+  }
+  if constexpr (IMPULSES) {
+#pragma unroll
+    for (int k = 0; k < C; ++k) {
+      imp[2 * k] += lt[k];
+      imp[2 * k + 1] += ln[k];
+    }
   }
 }
 

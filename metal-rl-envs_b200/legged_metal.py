@@ -80,12 +80,17 @@ class Legged(_rl.StepBody):
     def reset(self, n):
         return _rl.reset_uniform(self.rows, n, RESET_BOUND, center=self._stand.host)
 
-    def step(self, state, action, assist=None):
+    def step(self, state, action, assist=None, impulses=False):
+        """(next_state, reward, done), and with impulses=True a fourth output: the (2c, n)
+        contact impulses of the step, row 2k the tangential and row 2k + 1 the normal impulse
+        of foot k, each summed over the four substeps (the lt, ln of legged_np.py:89-96)."""
         state = _rl.as_state(state, self.rows)
         stand = self._stand.on(state.device)
         if isinstance(assist, torch.Tensor) and assist.device.type == "cuda":
             a_val, a_ptr = 0.0, assist.reshape(-1)[:1].float().contiguous()
         else:
             a_val, a_ptr = (0.0 if assist is None else _rl.float_scalar(assist)), None
-        return self._launch(_rl.lib().legged_step, (self.c, self.iters), state, action,
-                            tail=(stand.data_ptr(), a_val, _rl.ptr(a_ptr)))
+        imp = torch.empty((2 * self.c, state.shape[1]), dtype=torch.float32, device=state.device) if impulses else None
+        out = self._launch(_rl.lib().legged_step, (self.c, self.iters), state, action,
+                           tail=(stand.data_ptr(), a_val, _rl.ptr(a_ptr)), outs=(_rl.ptr(imp),))
+        return out + (imp,) if impulses else out

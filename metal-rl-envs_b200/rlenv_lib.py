@@ -40,7 +40,7 @@ _SIGNATURES = {
     "rlenv_pendulum_aba_step": [c_int, c_void_p, c_void_p, c_int, c_uint32, c_int64, c_int64, c_void_p, c_void_p,
                                 c_void_p, c_void_p],
     "rlenv_legged_step": [c_int, c_int, c_void_p, c_void_p, c_int, c_uint32, c_void_p, c_float, c_void_p, c_int64,
-                          c_int64, c_void_p, c_void_p, c_void_p, c_void_p],
+                          c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
     "rlenv_hopper_step": [c_int, c_void_p, c_void_p, c_int, c_uint32, c_void_p, c_int64, c_int64, c_void_p, c_void_p,
                           c_void_p, c_void_p],
     "rlenv_cartpole_rollout": [c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_void_p, c_void_p],
@@ -248,14 +248,15 @@ class StepBody:
         self.calls += 1
         return self.calls & 0xFFFFFFFF
 
-    def _launch(self, entry, head, state, action, tail=()):
-        """entry(*head, state, action, dtype, seed, *tail, n, index_offset, next, reward, done, stream)."""
+    def _launch(self, entry, head, state, action, tail=(), outs=()):
+        """entry(*head, state, action, dtype, seed, *tail, n, index_offset, next, reward, done,
+        *outs, stream); outs are raw device pointers (or None) of further outputs."""
         state = as_state(state, self.rows)
         n = state.shape[1]
         action, dt = as_actions(action, n, state.device)
         nxt, reward, done = step_outputs(self.rows, n, state.device)
         check(entry(*head, state.data_ptr(), action.data_ptr(), dt, self._next_seed(), *tail, n, 0,
-                    nxt.data_ptr(), reward.data_ptr(), done.data_ptr(), stream_ptr(state.device)))
+                    nxt.data_ptr(), reward.data_ptr(), done.data_ptr(), *outs, stream_ptr(state.device)))
         return nxt, reward, done
 
 

@@ -134,6 +134,23 @@ def physics(state, action, c, iters=LG_ITERS, assist=0.0):
     return np.concatenate([q, v])
 
 
+def step_impulses(state, action, c, iters=LG_ITERS, assist=0.0):
+    """The contact impulses of one step, (2C, N): row 2k the tangential and row 2k + 1 the
+    normal impulse of foot k, each the final (lt, ln) of a substep's Gauss-Seidel solve
+    (legged_np.py:89-96) summed over the four substeps. The reference's step computes them
+    and drops them; this is the checker for the step's optional impulse output."""
+    s = np.asarray(state)
+    d = 3 + c
+    q, v = s[:d], s[d:]
+    tq = torques(action, c)
+    total = np.zeros((2 * c, s.shape[1]), dtype=np.float64)
+    for _ in range(LG_SUBSTEPS):
+        q, v, lt, ln = substep(q, v, tq, c, iters, assist=assist, return_impulses=True)
+        total[0::2] += lt
+        total[1::2] += ln
+    return total.astype(np.float32)
+
+
 def terminated(state):
     """Torso below 0.6 or tilted past 1 rad (legged_np.py:130-132)."""
     return (state[1] < LG_FALL_HEIGHT) | (np.abs(state[2]) > LG_FALL_ANGLE)

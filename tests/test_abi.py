@@ -41,7 +41,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_version_and_messages(lib):
-    assert lib.abi_version() == 1
+    assert lib.abi_version() == 2
     assert "invalid" in lib.strerror(-1) and "instance" in lib.strerror(-2) and lib.strerror(0) == "ok"
 
 
@@ -55,8 +55,8 @@ def test_arguments_rejected_before_launch(lib):
     assert lib.pendulum_mm_step(17, 0, fake, fake, 0, 1, 4, 0, fake, fake, fake, None) == -2
     assert lib.pendulum_coop_step(3, fake, fake, 0, 1, 4, 0, fake, fake, fake, None) == -2
     assert lib.pendulum_aba_step(65, fake, fake, 0, 1, 4, 0, fake, fake, fake, None) == -2
-    assert lib.legged_step(5, 8, fake, fake, 0, 1, fake, 0.0, None, 4, 0, fake, fake, fake, None) == -2
-    assert lib.legged_step(2, 0, fake, fake, 0, 1, fake, 0.0, None, 4, 0, fake, fake, fake, None) == -1  # iters < 1
+    assert lib.legged_step(5, 8, fake, fake, 0, 1, fake, 0.0, None, 4, 0, fake, fake, fake, None, None) == -2
+    assert lib.legged_step(2, 0, fake, fake, 0, 1, fake, 0.0, None, 4, 0, fake, fake, fake, None, None) == -1  # iters < 1
     assert lib.cartpole_rollout(fake, fake, 0, 4, 3, 10, fake, None) == -2                 # hidden 3 not built
     assert lib.legged_rollout(2, 16, 10, 8, 1.0, 0.0, 0.0, 0.0, fake, fake, 0, -1, fake, fake, None) == -1
     assert lib.es_centered_ranks(fake, 1, fake, None) == -1

@@ -220,3 +220,30 @@ def test_legged_trajectory_matches_oracle(cuda, c):
         worst = max(worst, float(np.abs(to_np(s_gpu)[:, both_live] - s_np[:, both_live]).max()))
     record(f"legged{c}_traj50", done_flips=flips, max_abs=worst, n=n)
     assert flips <= n // 100, flips
+
+
+@pytest.mark.parametrize("c", [1, 2, 4])
+def test_legged_impulses_match_oracle(cuda, c):
+    """The optional (2c, n) contact-impulse output against the oracle's per-substep (lt, ln)
+    sums on the golden states; the step itself is unchanged by asking for them."""
+    import legged_metal
+
+    g = golden("legged")
+    st, ac = g[f"state_c{c}"], g[f"action_c{c}"]
+    body = legged_metal.Legged(c)
+    body.reseed(80)
+    plain = body.step(torch.from_numpy(st).to(cuda), torch.from_numpy(ac).to(cuda))
+    body.reseed(80)
+    nxt, rew, done, imp = body.step(torch.from_numpy(st).to(cuda), torch.from_numpy(ac).to(cuda), impulses=True)
+    np.testing.assert_allclose(to_np(nxt), to_np(plain[0]), rtol=1e-6, atol=1e-6)
+    assert (to_np(done) == to_np(plain[2])).all()
+    ref = legged.step_impulses(st, ac, c)
+    got = to_np(imp)
+    assert got.shape == (2 * c, st.shape[1])
+    err = np.abs(got - ref)
+    # impulses are sums of four Gauss-Seidel solves, as sensitive as the velocities they set
+    tol = 1e-4 + 1e-3 * np.abs(ref)
+    bad = (err > tol).mean()
+    record(f"legged_c{c}_impulses", max_abs=float(err.max()), frac_out_of_tol=float(bad))
+    assert bad <= 0.002, (float(err.max()), bad)
+    assert (got[1::2] >= 0).all()

@@ -226,6 +226,36 @@ def test_two_leg_stand_converges_with_sweeps():
     assert drifts[-1] < 1e-6 and drifts[2] < 1e-2, drifts
 
 
+@pytest.mark.parametrize("c", [1, 2, 4])
+def test_step_impulses_carry_the_weight_of_a_standing_body(c):
+    """At rest on every foot, the normal impulses of one step (four substeps of 0.01) add up
+    to the body's weight times 0.04 (plus the Baumgarte correction of a resting contact), and
+    the step with impulses is the same step."""
+    pose = legged.static_pose(c)[:, None]
+    hold = np.full(1, (3**c - 1) // 2)  # zero torque on every leg
+    imp = legged.step_impulses(pose, hold, c)
+    weight = (legged.LG_M_T + c * legged.LG_M_F) * legged.LG_GRAVITY * legged.LG_H * legged.LG_SUBSTEPS
+    assert imp.shape == (2 * c, 1) and imp.dtype == np.float32
+    assert abs(float(imp[1::2].sum()) / weight - 1.0) < 0.06
+    # symmetric stance: the tangential impulses nearly cancel (the sweep order is not symmetric)
+    assert abs(float(imp[0::2].sum())) < 0.01 * weight
+
+
+def test_step_impulses_cone_and_flight():
+    r = np.random.default_rng(5)
+    for c in (2, 4):
+        st = legged.stand_pose(c)[:, None] + r.uniform(-0.05, 0.05, (2 * (3 + c), 512)).astype(np.float32)
+        act = r.integers(0, 3**c, 512)
+        imp = legged.step_impulses(st, act, c)
+        lt, ln = imp[0::2], imp[1::2]
+        assert (ln >= 0).all() and (ln > 0).any()
+        # each substep's impulse is inside the cone, so the sum is too
+        assert (np.abs(lt) <= legged.LG_MU * ln + 1e-5).all()
+    high = legged.stand_pose(2)[:, None].copy()
+    high[1] += 1.0  # every foot a metre above the floor
+    assert (legged.step_impulses(high, np.zeros(1, np.int64), 2) == 0).all()
+
+
 def test_random_policy_keeps_legged_bodies_above_the_floor():
     r = np.random.default_rng(0)
     for c in (2, 4):
