@@ -54,6 +54,8 @@ WORKLOAD = "acrobot_batched_step"
 WORKLOADS = {
     "acrobot_step": ("BASELINE configs[1]: Acrobot batched step", N_ENVS, T_STEPS),
     "cartpole_step": ("BASELINE configs[0]: CartPole batched step, T-step kernel", 131_072, T_STEPS),
+    "cartpole_single": ("BASELINE configs[0]: CartPole single-step kernel, one launch per step, N past L2", 1 << 24, 20),
+    "acrobot_single": ("BASELINE configs[1]: Acrobot single-step kernel, one launch per step, N past L2", 1 << 24, 20),
     "pendulum_aba": ("BASELINE configs[2]: K-link pendulum, articulated body", 65_536, 100),
     "pendulum_mm": ("BASELINE configs[2]: K-link pendulum, mass matrix", 65_536, 100),
     "pendulum_coop": ("BASELINE configs[2]: K-link pendulum, K lanes per env", 65_536, 100),
@@ -61,6 +63,7 @@ WORKLOADS = {
     "es_cartpole": ("BASELINE configs[4]: ES generation, CartPole P=4096 H=32 horizon 500", 4096, 500),
     "es_acrobot": ("BASELINE configs[4]: ES generation, Acrobot P=4096 H=32 horizon 500", 4096, 500),
     "es_legged4": ("BASELINE configs[4]: ES generation, legged4 P=16384 H=16 horizon 1000", 16_384, 1000),
+    "es_ranks": ("es.py:214-215 centred ranks of P fitness values: sort kernel and counting kernel", 262_144, 1),
 }
 
 
@@ -80,6 +83,7 @@ def parse():
     p.add_argument("--k", type=int, default=16, help="pendulum links (pendulum workloads)")
     p.add_argument("--c", type=int, default=4, help="legs (legged workload)")
     p.add_argument("--iters", type=int, default=8, help="Gauss-Seidel sweeps (legged workload)")
+    p.add_argument("--no-impulses", action="store_true", help="legged workload without the contact-impulse output")
     p.add_argument("--pop", type=int, default=None, help="ES population (es_* workloads)")
     p.add_argument("--horizon", type=int, default=None, help="ES horizon (es_* workloads)")
     return p.parse_args()
@@ -471,6 +475,7 @@ def run_workload(args):
     sp = stream.cuda_stream
     g = torch.Generator(device=dev).manual_seed(4321 + rank)
     extra = {}
+    hbm_bound = False
     sgemm = measured_sgemm_tflops(torch) if rank == 0 else None
     if args.workload == "cartpole_step":
         actions = torch.randint(0, 2, (T, n), device=dev, generator=g).to(torch.uint8)
@@ -483,6 +488,32 @@ def run_workload(args):
                                             s1.data_ptr(), rew.data_ptr(), dn.data_ptr(), 0, 0, sp))
         units, unit, metric, flops = n * T, "env steps/s", METRIC, rlenv_flops.CARTPOLE["flops"]
         bytes_launch = rlenv_flops.step_many_bytes(4, n, T)
+    elif args.workload in ("cartpole_single", "acrobot_single"):
+        # The drop-in single step (cartpole_metal.step / acrobot_metal.step): state in, next state,
+        # reward and done out, int32 actions as the reference draws them; N is large enough that
+        # every step streams 688 MB through HBM, far past the 126 MB L2.
+        env = args.workload.split("_")[0]
+        n_act = 2 if env == "cartpole" else 3
+        abi = getattr(lib, f"{env}_step")
+        actions = torch.randint(0, n_act, (T, n), device=dev, generator=g, dtype=torch.int32)
+        state_a = rl.reset_uniform(4, n, 0.05, seed=7, index_offset=rank * n, dev=dev)
+        state_b = torch.empty_like(state_a)
+        rew, dn = torch.empty((T, n), device=dev), torch.empty((T, n), device=dev, dtype=torch.bool)
+
+        def launch_one(t):
+            src, dst = (state_a, state_b) if t % 2 == 0 else (state_b, state_a)
+            rl.check(abi(src.data_ptr(), actions[t].data_ptr(), rl.I32, 1 + t, n, rank * n, dst.data_ptr(),
+                         rew[t].data_ptr(), dn[t].data_ptr(), torch.cuda.current_stream().cuda_stream))
+        graph = _graph_steps(torch, launch_one, T)
+
+        def fn():
+            graph.replay()
+        units, unit, metric = n * T, "env steps/s", METRIC
+        flops = (rlenv_flops.CARTPOLE if env == "cartpole" else rlenv_flops.ACROBOT)["flops"]
+        bytes_launch = n * T * rlenv_flops.step_bytes(4, 4)
+        extra = {"action_dtype": "int32", "bytes_per_env_step": rlenv_flops.step_bytes(4, 4),
+                 "l2": "state, actions and outputs (688 MB per step at N = 2^24) exceed L2"}
+        hbm_bound = True
     elif args.workload in ("pendulum_aba", "pendulum_mm", "pendulum_coop", "legged_step"):
         if args.workload == "legged_step":
             c = args.c
@@ -492,12 +523,15 @@ def run_workload(args):
             stand = torch.from_numpy(legged_metal.stand_pose(c)).to(dev)
             state_a = rl.reset_uniform(rows, n, 0.05, center=stand, seed=3, index_offset=rank * n, dev=dev)
 
+            # BASELINE's legged outputs per step: state, contact impulses and the fall flag
+            imp = torch.empty((2 * c, n), device=dev) if not args.no_impulses else None
+
             def entry(src, dst, t, r, d):
                 rl.check(lib.legged_step(c, args.iters, src.data_ptr(), actions[t].data_ptr(), rl.U8, 1 + t,
                                          stand.data_ptr(), 0.0, None, n, rank * n, dst.data_ptr(), r.data_ptr(),
-                                         d.data_ptr(), None, torch.cuda.current_stream().cuda_stream))
+                                         d.data_ptr(), rl.ptr(imp), torch.cuda.current_stream().cuda_stream))
             fl = rlenv_flops.legged_flops(c, args.iters)["flops"]
-            extra = {"legs": c, "sweeps": args.iters}
+            extra = {"legs": c, "sweeps": args.iters, "impulses": imp is not None}
         else:
             k = args.k
             rows, n_act = 2 * k, 3
@@ -524,7 +558,29 @@ def run_workload(args):
         def fn():
             graph.replay()
         units, unit, metric, flops = n * T, "env steps/s", METRIC, fl
-        bytes_launch = n * T * (2 * 4 * rows + 1 + 5)
+        bytes_launch = n * T * (2 * 4 * rows + 1 + 5 + (8 * args.c if extra.get("impulses") else 0))
+    elif args.workload == "es_ranks":
+        import es
+
+        pop = args.pop or n_def
+        fit = torch.randn(pop, device=dev, generator=g)
+        ms = {}
+        for kind in (True, False):
+            secs, clocks = _timed(torch, dist, world, stream, lambda: es.centered_ranks(torch, fit, sorted_kernel=kind),
+                                  args.steps, args.warmup, local)
+            ms[kind] = 1e3 * secs / args.steps
+        if rank == 0:
+            line = {"metric": "ES centred ranks ms", "value": ms[True], "unit": "ms", "n_gpus": world,
+                    "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms[True], "higher_is_better": False,
+                    "scaling": "replicas", "vs_baseline": None, "dtype": "f32", "data": "synthetic (normal fitness)",
+                    "config": {"workload": args.workload, "config": desc, "population": pop,
+                               "kernel": "rlenv_es_centered_ranks_sorted (bitonic tiles, merge-by-rank passes)",
+                               "counting_kernel_ms": ms[False], "l2": "fitness and keys (12 B per member) stay in L2"},
+                    "clocks": clocks}
+            print(json.dumps(line), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
     else:  # es_*
         import es
 
@@ -562,14 +618,17 @@ def run_workload(args):
     per = secs / args.steps
     if rank == 0:
         achieved = flops * units / per / 1e12
+        gbs, hbm_peak = bytes_launch / per / 1e9, hbm_peak_gbs()[0]
+        fp32 = {"bound": "fp32", "achieved": achieved, "peak": sgemm, "unit": "TFLOP/s",
+                "frac": achieved / sgemm if sgemm else None, "flops_per_env_step": flops}
+        hbm = {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
+               "bytes_per_launch": bytes_launch / T, "peak_kind": "measured (MEASURED_PEAKS.json)"}
+        roof = {**hbm, "fp32": fp32} if hbm_bound else {**fp32, "hbm": hbm}
         line = {"metric": metric, "value": world * units * args.steps / secs, "unit": unit, "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * per, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
                 "config": {"workload": args.workload, "config": desc, "n_envs_per_gpu": n, "env_steps_per_step": T, **extra},
-                "roofline": {"bound": "fp32", "achieved": achieved, "peak": sgemm, "unit": "TFLOP/s",
-                             "frac": achieved / sgemm if sgemm else None, "flops_per_env_step": flops,
-                             "hbm": {"achieved": bytes_launch / per / 1e9, "peak": hbm_peak_gbs()[0], "unit": "GB/s"}},
-                "clocks": clocks}
+                "roofline": roof, "clocks": clocks}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -198,8 +198,24 @@ RLENV_API int rlenv_es_perturb(const float* theta, int64_t d, float sigma, uint6
 
 /* Centred ranks (es.py:214-215): ranks[i] = r_i / (p - 1) - 0.5 with r_i the
  * position of fitness[i] in ascending order, ties broken by index (a stable
- * sort). p >= 2. */
+ * sort), NaN after every number as in numpy's sort. p >= 2. O(p^2) work in
+ * one launch: the faster choice up to a few thousand members. */
 RLENV_API int rlenv_es_centered_ranks(const float* fitness, int64_t p, float* ranks, void* stream);
+
+/* Device scratch in bytes that rlenv_es_centered_ranks_sorted needs for p
+ * members: 16 p above 4,096 members, 0 up to that; -1 for p < 0. */
+RLENV_API int64_t rlenv_es_ranks_scratch_bytes(int64_t p);
+
+/* The ranks of rlenv_es_centered_ranks, bit for bit, in O(p log p) work: a
+ * sort of unique (fitness order, index) keys instead of p^2 comparisons, for
+ * large populations (the reference's own results run es.py at P = 262,144).
+ * Both kernels order fitness as numpy's sort does: NaN after every number.
+ * scratch: caller-allocated device memory, 8-byte aligned, of at least
+ * rlenv_es_ranks_scratch_bytes(p) bytes (may be NULL when that is 0); nothing
+ * in it needs to be initialised. 2 <= p <= 2^31. Same reference interface as
+ * rlenv_es_centered_ranks (es.py:214-215). */
+RLENV_API int rlenv_es_centered_ranks_sorted(const float* fitness, int64_t p, float* ranks,
+                                             void* scratch, int64_t scratch_bytes, void* stream);
 
 /* Rank-weighted antithetic update (es.py:224-225):
  * theta_out = theta + lr / (2 * pairs * sigma) * sum_j (ranks[j] - ranks[j + pairs]) * half[j],

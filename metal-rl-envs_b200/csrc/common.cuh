@@ -112,6 +112,19 @@ RLENV_D float noise_at(uint64_t seed, uint64_t gen, int64_t pair, int64_t j) {
   return v[j & 3];
 }
 
+// An unsigned key whose order is numpy's sort order of float32: every number
+// by value (-0 and +0 equal), then NaN, every NaN equal. Negative numbers have
+// their bits inverted, the rest get the sign bit set (the usual order-preserving
+// map of IEEE floats to unsigned integers).
+RLENV_D uint32_t rank_order_key(float f) {
+  if (f != f) return 0xFFFFFFFFu;
+  const uint32_t b = __float_as_uint(f == 0.0f ? 0.0f : f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+// Centred rank of sorted position r among p members (es.py:214-215).
+RLENV_D float centered_rank(int64_t r, int64_t p) { return float(r) / float(p - 1) - 0.5f; }
+
 // Index of element (i, j), j <= i, of a lower triangle stored row by row.
 RLENV_HD constexpr int tri(int i, int j) { return i * (i + 1) / 2 + j; }
 

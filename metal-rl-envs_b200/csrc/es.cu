@@ -50,28 +50,30 @@ perturb_kernel(const float* __restrict__ theta, int64_t d, float sigma, uint64_t
   }
 }
 
-// Stable ranks by counting: rank_i = #{j : f_j < f_i} + #{j < i : f_j == f_i}.
-// Fitness tiles are staged through shared memory; every block sees every
-// element, so each thread's count is exact.
+// Stable ranks by counting: rank_i = #{j : f_j < f_i} + #{j < i : f_j == f_i},
+// in numpy's sort order: NaN after every number, NaNs equal among themselves
+// (ties by index), -0 equal to +0. Fitness tiles are staged through shared
+// memory; every block sees every element, so each thread's count is exact.
+// Each fitness is compared as its order key (rank_order_key, common.cuh).
 __global__ void __launch_bounds__(256)
 ranks_kernel(const float* __restrict__ f, int64_t p, float* __restrict__ ranks) {
-  __shared__ float tile[1024];
+  __shared__ uint32_t tile[1024];
   const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  const float fi = i < p ? __ldg(f + i) : 0.0f;
+  const uint32_t ki = i < p ? rank_order_key(__ldg(f + i)) : 0u;
   int64_t below = 0;
   for (int64_t base = 0; base < p; base += 1024) {
     const int64_t len = (p - base) < 1024 ? (p - base) : 1024;
     __syncthreads();
-    for (int64_t k = threadIdx.x; k < len; k += blockDim.x) tile[k] = __ldg(f + base + k);
+    for (int64_t k = threadIdx.x; k < len; k += blockDim.x) tile[k] = rank_order_key(__ldg(f + base + k));
     __syncthreads();
     if (i < p) {
       for (int64_t k = 0; k < len; ++k) {
-        const float fj = tile[k];
-        below += (fj < fi) || (fj == fi && base + k < i);
+        const uint32_t kj = tile[k];
+        below += (kj < ki) || (kj == ki && base + k < i);
       }
     }
   }
-  if (i < p) ranks[i] = float(below) / float(p - 1) - 0.5f;
+  if (i < p) ranks[i] = centered_rank(below, p);
 }
 
 // theta_out = theta + lr / (2 pairs sigma) * sum_j (ranks[j] - ranks[j + pairs]) noise_j.

@@ -32,13 +32,23 @@ constexpr float ASSIST_DAMPING = 0.1f;
 // contact above the floor, one that would pull, or one already separating.
 // inv_det, inv_dp and inv_dm are 1 / det, 1 / (Ann + mu Atn) and
 // 1 / (Ann - mu Atn), which depend on the block only and so are computed once
-// per substep. BRANCHY skips the solve of an airborne contact with a branch
-// (the variant of hopper_metal.py:110) instead of computing it and selecting
-// zero.
+// per substep; a sliding direction whose denominator is not positive has a
+// zero reciprocal, so its normal impulse is zero (the reference's Painleve
+// guard). BRANCHY skips the solve of an airborne contact with a branch (the
+// variant of hopper_metal.py:110) instead of computing it and selecting zero.
+struct ContactConsts {
+  float inv_det, inv_dp, inv_dm;
+};
+
+RLENV_D ContactConsts contact_consts(float Att, float Atn, float Ann) {
+  const float den_p = Ann + lg::MU * Atn, den_m = Ann - lg::MU * Atn;
+  return ContactConsts{1.0f / (Att * Ann - Atn * Atn), den_p > 0.0f ? 1.0f / den_p : 0.0f,
+                       den_m > 0.0f ? 1.0f / den_m : 0.0f};
+}
+
 template <bool BRANCHY>
-RLENV_D void contact_impulse(float Att, float Atn, float Ann, float inv_det, float den_p,
-                             float inv_dp, float den_m, float inv_dm, float wt, float wn,
-                             float depth, float& lt, float& ln) {
+RLENV_D void contact_impulse(float Att, float Atn, float Ann, const ContactConsts& k, float wt,
+                             float wn, float depth, float& lt, float& ln) {
   const bool touching = depth >= 0.0f;
   if (BRANCHY && !touching) {
     lt = 0.0f;
@@ -47,11 +57,11 @@ RLENV_D void contact_impulse(float Att, float Atn, float Ann, float inv_det, flo
   }
   const float target = lg::BAUMGARTE_OVER_H * fmaxf(depth, 0.0f);
   const float gap = target - wn;
-  const float ln_stick = (Att * gap + Atn * wt) * inv_det;
-  const float lt_stick = (-Ann * wt - Atn * gap) * inv_det;
+  const float ln_stick = (Att * gap + Atn * wt) * k.inv_det;
+  const float lt_stick = (-Ann * wt - Atn * gap) * k.inv_det;
   const bool sticks = fabsf(lt_stick) <= lg::MU * ln_stick;
-  const float ln_p = den_p > 0.0f ? fmaxf(gap * inv_dp, 0.0f) : 0.0f;
-  const float ln_m = den_m > 0.0f ? fmaxf(gap * inv_dm, 0.0f) : 0.0f;
+  const float ln_p = fmaxf(gap * k.inv_dp, 0.0f);
+  const float ln_m = fmaxf(gap * k.inv_dm, 0.0f);
   const float slip_p = wt + (Att * lg::MU + Atn) * ln_p;
   const float sgn = slip_p <= 0.0f ? 1.0f : -1.0f;
   const float ln_slide = slip_p <= 0.0f ? ln_p : ln_m;
@@ -93,16 +103,28 @@ RLENV_D void cholesky_packed(float (&Lm)[n * (n + 1) / 2], float (&inv_diag)[n])
   }
 }
 
-template <int n>
-RLENV_D void cholesky_solve(const float (&Lm)[n * (n + 1) / 2], const float (&inv_diag)[n],
-                            float (&b)[n]) {
+// L y = b in place, for a b whose first LEAD entries are exactly zero (they
+// stay zero and are skipped).
+template <int n, int LEAD = 0>
+RLENV_D void forward_solve(const float (&Lm)[n * (n + 1) / 2], const float (&inv_diag)[n],
+                           float (&b)[n]) {
 #pragma unroll
   for (int i = 0; i < n; ++i) {
+    if (i < LEAD) {
+      b[i] = 0.0f;
+      continue;
+    }
     float v = b[i];
 #pragma unroll
-    for (int p = 0; p < i; ++p) v -= Lm[tri(i, p)] * b[p];
+    for (int p = LEAD; p < i; ++p) v -= Lm[tri(i, p)] * b[p];
     b[i] = v * inv_diag[i];
   }
+}
+
+// L^T x = y in place.
+template <int n>
+RLENV_D void back_solve(const float (&Lm)[n * (n + 1) / 2], const float (&inv_diag)[n],
+                        float (&b)[n]) {
 #pragma unroll
   for (int i = n - 1; i >= 0; --i) {
     float v = b[i];
@@ -110,6 +132,22 @@ RLENV_D void cholesky_solve(const float (&Lm)[n * (n + 1) / 2], const float (&in
     for (int p = i + 1; p < n; ++p) v -= Lm[tri(p, i)] * b[p];
     b[i] = v * inv_diag[i];
   }
+}
+
+template <int n>
+RLENV_D void cholesky_solve(const float (&Lm)[n * (n + 1) / 2], const float (&inv_diag)[n],
+                            float (&b)[n]) {
+  forward_solve<n>(Lm, inv_diag, b);
+  back_solve<n>(Lm, inv_diag, b);
+}
+
+// Dot product of two length-n vectors from index LEAD on.
+template <int n, int LEAD = 0>
+RLENV_D float dot_from(const float (&a)[n], const float (&b)[n]) {
+  float s = 0.0f;
+#pragma unroll
+  for (int i = LEAD; i < n; ++i) s += a[i] * b[i];
+  return s;
 }
 
 // One substep of H for C legs (legged_np.py:57-97), in place on q and v. With
@@ -171,20 +209,37 @@ RLENV_D void legged_substep(float (&q)[3 + C], float (&v)[3 + C], const float (&
 #pragma unroll
   for (int i = 0; i < n; ++i) vf[i] = v[i] + lg::H * f[i];
 
-  // M^-1 J_k^T for every foot, then the Delassus blocks J_k M^-1 J_l^T and the
-  // free relative velocities J_k v_free
-  float MiJt[C][n], MiJn[C][n];
+  // W = L^-1 J^T, one column per contact row (the normal rows start with a zero),
+  // so the Delassus matrix J M^-1 J^T = W^T W is a table of dot products. It is
+  // symmetric: Att and Ann are kept as packed lower triangles over the contacts,
+  // and the tangent-normal block in full (Ant[k][l] = Atn[l][k]).
+  float att[C * (C + 1) / 2], ann[C * (C + 1) / 2], atn[C][C];
+  {
+    float Wt[C][n], Wn[C][n];
 #pragma unroll
-  for (int k = 0; k < C; ++k) {
+    for (int k = 0; k < C; ++k) {
 #pragma unroll
-    for (int i = 0; i < n; ++i) {
-      MiJt[k][i] = jt_nz(k, i) ? jt_at(i, lca[k]) : 0.0f;
-      MiJn[k][i] = jn_nz(k, i) ? jn_at(i, lsa[k]) : 0.0f;
+      for (int i = 0; i < n; ++i) {
+        Wt[k][i] = jt_nz(k, i) ? jt_at(i, lca[k]) : 0.0f;
+        Wn[k][i] = jn_nz(k, i) ? jn_at(i, lsa[k]) : 0.0f;
+      }
+      forward_solve<n, 0>(Lm, inv_diag, Wt[k]);
+      forward_solve<n, 1>(Lm, inv_diag, Wn[k]);
     }
-    cholesky_solve<n>(Lm, inv_diag, MiJt[k]);
-    cholesky_solve<n>(Lm, inv_diag, MiJn[k]);
+#pragma unroll
+    for (int k = 0; k < C; ++k) {
+#pragma unroll
+      for (int l = 0; l <= k; ++l) {
+        att[tri(k, l)] = dot_from<n, 0>(Wt[k], Wt[l]);
+        ann[tri(k, l)] = dot_from<n, 1>(Wn[k], Wn[l]);
+      }
+#pragma unroll
+      for (int l = 0; l < C; ++l) atn[k][l] = dot_from<n, 1>(Wt[k], Wn[l]);
+    }
   }
-  float Att[C][C], Atn[C][C], Ant[C][C], Ann[C][C], w0t[C], w0n[C];
+  // free relative velocities J_k v_free and the per-contact constants
+  float w0t[C], w0n[C];
+  ContactConsts cc[C];
 #pragma unroll
   for (int k = 0; k < C; ++k) {
     float wt = 0.0f, wn = 0.0f;
@@ -195,36 +250,7 @@ RLENV_D void legged_substep(float (&q)[3 + C], float (&v)[3 + C], const float (&
     }
     w0t[k] = wt;
     w0n[k] = wn;
-#pragma unroll
-    for (int l = 0; l < C; ++l) {
-      float tt = 0.0f, tn = 0.0f, nt = 0.0f, nn = 0.0f;
-#pragma unroll
-      for (int i = 0; i < n; ++i) {
-        if (jt_nz(k, i)) {
-          tt += jt_at(i, lca[k]) * MiJt[l][i];
-          tn += jt_at(i, lca[k]) * MiJn[l][i];
-        }
-        if (jn_nz(k, i)) {
-          nt += jn_at(i, lsa[k]) * MiJt[l][i];
-          nn += jn_at(i, lsa[k]) * MiJn[l][i];
-        }
-      }
-      Att[k][l] = tt;
-      Atn[k][l] = tn;
-      Ant[k][l] = nt;
-      Ann[k][l] = nn;
-    }
-  }
-  // per-contact constants of the exact block solve
-  float inv_det[C], den_p[C], inv_dp[C], den_m[C], inv_dm[C];
-#pragma unroll
-  for (int k = 0; k < C; ++k) {
-    const float a = Att[k][k], b = Atn[k][k], d = Ann[k][k];
-    inv_det[k] = 1.0f / (a * d - b * b);
-    den_p[k] = d + lg::MU * b;
-    den_m[k] = d - lg::MU * b;
-    inv_dp[k] = 1.0f / (den_p[k] > 0.0f ? den_p[k] : 1.0f);
-    inv_dm[k] = 1.0f / (den_m[k] > 0.0f ? den_m[k] : 1.0f);
+    cc[k] = contact_consts(att[tri(k, k)], atn[k][k], ann[tri(k, k)]);
   }
   // block projected Gauss-Seidel: each contact solved exactly given the others
   float lt[C], ln[C];
@@ -241,20 +267,30 @@ RLENV_D void legged_substep(float (&q)[3 + C], float (&v)[3 + C], const float (&
 #pragma unroll
       for (int l = 0; l < C; ++l) {
         if (l == k) continue;
-        st += Att[k][l] * lt[l] + Atn[k][l] * ln[l];
-        sn += Ant[k][l] * lt[l] + Ann[k][l] * ln[l];
+        const int kl = k > l ? tri(k, l) : tri(l, k);
+        st += att[kl] * lt[l] + atn[k][l] * ln[l];
+        sn += atn[l][k] * lt[l] + ann[kl] * ln[l];
       }
-      contact_impulse<BRANCHY>(Att[k][k], Atn[k][k], Ann[k][k], inv_det[k], den_p[k], inv_dp[k],
-                               den_m[k], inv_dm[k], w0t[k] + st, w0n[k] + sn, depth[k], lt[k],
-                               ln[k]);
+      contact_impulse<BRANCHY>(att[tri(k, k)], atn[k][k], ann[tri(k, k)], cc[k], w0t[k] + st,
+                               w0n[k] + sn, depth[k], lt[k], ln[k]);
     }
   }
+  // v = v_free + M^-1 J^T lambda, one solve with the factor of M
+  float r[n];
 #pragma unroll
   for (int i = 0; i < n; ++i) {
-    float vi = 0.0f;
+    float ri = 0.0f;
 #pragma unroll
-    for (int k = 0; k < C; ++k) vi += MiJt[k][i] * lt[k] + MiJn[k][i] * ln[k];
-    v[i] = vf[i] + vi;
+    for (int k = 0; k < C; ++k) {
+      if (jt_nz(k, i)) ri += jt_at(i, lca[k]) * lt[k];
+      if (jn_nz(k, i)) ri += jn_at(i, lsa[k]) * ln[k];
+    }
+    r[i] = ri;
+  }
+  cholesky_solve<n>(Lm, inv_diag, r);
+#pragma unroll
+  for (int i = 0; i < n; ++i) {
+    v[i] = vf[i] + r[i];
     q[i] += lg::H * v[i];
   }
   if constexpr (IMPULSES) {

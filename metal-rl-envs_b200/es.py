@@ -205,12 +205,33 @@ def curriculum(cfg, gen):
     return cfg.assist_k0 * ramp, cfg.start_velocity * ramp
 
 
-def centered_ranks(xp, values):
-    """rank / (P - 1) - 0.5 with ranks from a stable ascending sort, on the device."""
+# Populations from this size up are ranked by the O(P log P) sort kernel, smaller ones by the
+# one-launch O(P^2) counting kernel; both give the same bits. Measured on a B200, the sort is
+# already faster at P = 2,048 (39 us against 52 us per call) and 370x faster at P = 262,144.
+SORTED_RANKS_FROM = 1024
+_rank_scratch = {}
+
+
+def _scratch(dev, nbytes):
+    buf = _rank_scratch.get(dev)
+    if buf is None or buf.numel() < nbytes:
+        buf = _rank_scratch[dev] = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    return buf
+
+
+def centered_ranks(xp, values, sorted_kernel=None):
+    """rank / (P - 1) - 0.5 with ranks from a stable ascending sort (NaN last), on the device.
+    sorted_kernel forces the sort (True) or the counting kernel (False); None picks by size."""
     values = values.contiguous().float()
     out = torch.empty_like(values)
-    _rl.check(_rl.lib().es_centered_ranks(values.data_ptr(), values.shape[0], out.data_ptr(),
-                                          _rl.stream_ptr(values.device)))
+    p, sp = values.shape[0], _rl.stream_ptr(values.device)
+    if sorted_kernel if sorted_kernel is not None else p >= SORTED_RANKS_FROM:
+        need = _rl.lib().es_ranks_scratch_bytes(p)
+        scratch = _scratch(values.device, need) if need > 0 else None
+        _rl.check(_rl.lib().es_centered_ranks_sorted(values.data_ptr(), p, out.data_ptr(), _rl.ptr(scratch),
+                                                     need, sp))
+    else:
+        _rl.check(_rl.lib().es_centered_ranks(values.data_ptr(), p, out.data_ptr(), sp))
     return out
 
 

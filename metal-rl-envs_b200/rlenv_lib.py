@@ -24,7 +24,8 @@ LIB_PATH = Path(__file__).resolve().parent / "librlenv.so"
 I32, I64, U8 = 0, 1, 2
 _DTYPES = {torch.int32: I32, torch.int64: I64, torch.uint8: U8, torch.bool: U8}
 
-# name -> argument types; every function returns int
+# name -> argument types; every function returns int except those in _RESTYPES
+_RESTYPES = {"rlenv_es_ranks_scratch_bytes": c_int64}
 _SIGNATURES = {
     "rlenv_abi_version": [],
     "rlenv_cartpole_step": [c_void_p, c_void_p, c_int, c_uint32, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p],
@@ -50,6 +51,8 @@ _SIGNATURES = {
     "rlenv_es_noise": [c_void_p, c_int64, c_int64, c_uint64, c_uint64, c_int64, c_void_p],
     "rlenv_es_perturb": [c_void_p, c_int64, c_float, c_uint64, c_uint64, c_int64, c_int64, c_int64, c_void_p, c_void_p],
     "rlenv_es_centered_ranks": [c_void_p, c_int64, c_void_p, c_void_p],
+    "rlenv_es_ranks_scratch_bytes": [c_int64],
+    "rlenv_es_centered_ranks_sorted": [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_void_p],
     "rlenv_es_update": [c_void_p, c_void_p, c_int64, c_int64, c_float, c_float, c_uint64, c_uint64, c_void_p, c_void_p],
     "rlenv_reset_uniform": [c_void_p, c_int, c_int64, c_void_p, c_float, c_uint32, c_int64, c_void_p],
 }
@@ -65,7 +68,7 @@ class _Lib:
         for name, args in _SIGNATURES.items():
             fn = getattr(self.cdll, name)
             fn.argtypes = args
-            fn.restype = c_int
+            fn.restype = _RESTYPES.get(name, c_int)
             setattr(self, name[len("rlenv_"):], fn)
         self.cdll.rlenv_strerror.argtypes = [c_int]
         self.cdll.rlenv_strerror.restype = ctypes.c_char_p

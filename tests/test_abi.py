@@ -14,7 +14,7 @@ HEADER = ROOT / "include" / "rlenv.h"
 
 
 def _declared():
-    return sorted(set(re.findall(r"RLENV_API\s+(?:int|const char\*)\s+(rlenv_\w+)\(", HEADER.read_text())))
+    return sorted(set(re.findall(r"RLENV_API\s+(?:int64_t|int|const char\*)\s+(rlenv_\w+)\(", HEADER.read_text())))
 
 
 @pytest.fixture(scope="module")
@@ -60,6 +60,12 @@ def test_arguments_rejected_before_launch(lib):
     assert lib.cartpole_rollout(fake, fake, 0, 4, 3, 10, fake, None) == -2                 # hidden 3 not built
     assert lib.legged_rollout(2, 16, 10, 8, 1.0, 0.0, 0.0, 0.0, fake, fake, 0, -1, fake, fake, None) == -1
     assert lib.es_centered_ranks(fake, 1, fake, None) == -1
+    assert lib.es_ranks_scratch_bytes(4096) == 0 and lib.es_ranks_scratch_bytes(4097) == 16 * 4097
+    assert lib.es_ranks_scratch_bytes(-1) == -1
+    assert lib.es_centered_ranks_sorted(fake, 1, fake, None, 0, None) == -1                  # p < 2
+    assert lib.es_centered_ranks_sorted(fake, 5000, fake, None, 0, None) == -1               # no scratch
+    assert lib.es_centered_ranks_sorted(fake, 5000, fake, fake, 16 * 4999, None) == -1       # too little
+    assert lib.es_centered_ranks_sorted(fake, 5000, fake, ctypes.c_void_p(0x1004), 16 * 5000, None) == -1  # misaligned
     assert lib.es_perturb(fake, 10, 0.1, 1, 1, 4, 6, 4, fake, None) == -1                   # past the population
     assert lib.es_update(fake, fake, 10, 4, 0.1, 0.0, 1, 1, fake, None) == -1               # sigma 0
 

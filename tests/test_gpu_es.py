@@ -53,6 +53,46 @@ def test_centered_ranks_stable(cuda, p):
     np.testing.assert_allclose(known, [1 / 6, -0.5, -1 / 6, 0.5], atol=1e-6)
 
 
+def _ranks_both(cuda, vals):
+    """The counting kernel's and the sort kernel's ranks of the same fitness."""
+    import es
+
+    t = torch.from_numpy(vals).to(cuda)
+    return (to_np(es.centered_ranks(torch, t, sorted_kernel=False)),
+            to_np(es.centered_ranks(torch, t, sorted_kernel=True)))
+
+
+@pytest.mark.parametrize("p", [2, 3, 1000, 4095, 4096, 4097, 8192, 10000, 65536, 100003])
+def test_sorted_ranks_equal_counting_and_oracle(cuda, p):
+    """One tile, one tile plus one, whole and ragged merge passes: the same bits everywhere."""
+    vals = np.random.default_rng(p).integers(0, max(2, p // 8), p).astype(np.float32)  # many ties
+    count, srt = _ranks_both(cuda, vals)
+    np.testing.assert_array_equal(srt, count)
+    np.testing.assert_array_equal(srt, oes.centered_ranks(vals, stable=True))
+
+
+def test_ranks_order_special_values_as_numpy(cuda):
+    """NaN after every number (NaNs tied), -0 equal to +0, infinities at the ends; across tiles."""
+    base = [np.nan, 1.0, -0.0, 0.0, np.inf, -np.inf, np.nan, 0.0, -1.0, 1.0, -0.0, 3.0e38, -3.0e38, 1e-45]
+    vals = np.array(base * 700, dtype=np.float32)
+    count, srt = _ranks_both(cuda, vals)
+    np.testing.assert_array_equal(srt, count)
+    np.testing.assert_array_equal(srt, oes.centered_ranks(vals, stable=True))
+
+
+def test_sorted_ranks_at_the_references_largest_population(cuda):
+    """P = 262,144 (the reference's own largest ES runs): a permutation, equal to the counting
+    kernel and to numpy's stable double argsort."""
+    p = 262_144
+    vals = np.random.default_rng(7).normal(size=p).astype(np.float32)
+    vals[::97] = np.round(vals[::97])  # some ties among many distinct values
+    count, srt = _ranks_both(cuda, vals)
+    np.testing.assert_array_equal(srt, count)
+    np.testing.assert_array_equal(srt, oes.centered_ranks(vals, stable=True))
+    pos = np.rint((srt.astype(np.float64) + 0.5) * (p - 1)).astype(np.int64)
+    assert np.array_equal(np.sort(pos), np.arange(p))
+
+
 def test_update_matches_float64(cuda):
     import rlenv_lib as rl
 
