@@ -217,6 +217,16 @@ RLENV_API int64_t rlenv_es_ranks_scratch_bytes(int64_t p);
 RLENV_API int rlenv_es_centered_ranks_sorted(const float* fitness, int64_t p, float* ranks,
                                              void* scratch, int64_t scratch_bytes, void* stream);
 
+/* rlenv_es_centered_ranks_sorted for callers that cannot allocate device
+ * memory: no counterpart in the reference, which has no such caller. It
+ * allocates nothing; its scratch is a fixed 1 MiB array inside the library
+ * (per device), so 2 <= p <= 65,536 and larger p is rejected with
+ * RLENV_EINVAL. Nothing in the array needs to start at zero. Calls on one
+ * device whose executions overlap (different streams or host threads) share
+ * the array and race; issue them on one stream. Same ranks, bit for bit, as
+ * the other two rank entry points. */
+RLENV_API int rlenv_es_centered_ranks_static(const float* fitness, int64_t p, float* ranks, void* stream);
+
 /* Rank-weighted antithetic update (es.py:224-225):
  * theta_out = theta + lr / (2 * pairs * sigma) * sum_j (ranks[j] - ranks[j + pairs]) * half[j],
  * with half regenerated from (seed, gen) and a fixed summation order, so every

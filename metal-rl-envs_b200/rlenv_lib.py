@@ -53,6 +53,7 @@ _SIGNATURES = {
     "rlenv_es_centered_ranks": [c_void_p, c_int64, c_void_p, c_void_p],
     "rlenv_es_ranks_scratch_bytes": [c_int64],
     "rlenv_es_centered_ranks_sorted": [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_void_p],
+    "rlenv_es_centered_ranks_static": [c_void_p, c_int64, c_void_p, c_void_p],
     "rlenv_es_update": [c_void_p, c_void_p, c_int64, c_int64, c_float, c_float, c_uint64, c_uint64, c_void_p, c_void_p],
     "rlenv_reset_uniform": [c_void_p, c_int, c_int64, c_void_p, c_float, c_uint32, c_int64, c_void_p],
 }
