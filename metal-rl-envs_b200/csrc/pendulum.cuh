@@ -73,7 +73,9 @@ RLENV_D void mm_accel(const float (&th)[K], const float (&om)[K], float torque, 
     rhs[i] = -r - (pd::G * float(K - i)) * s[i];
   }
   rhs[0] += torque;
-  // Cholesky in place, then forward and back substitution.
+  // Cholesky in place with the reciprocals of the diagonal, then forward and
+  // back substitution: K divisions instead of K (K + 3) / 2.
+  float inv_d[K];
 #pragma unroll
   for (int i = 0; i < K; ++i) {
 #pragma unroll
@@ -81,7 +83,12 @@ RLENV_D void mm_accel(const float (&th)[K], const float (&om)[K], float torque, 
       float v = L[tri(i, j)];
 #pragma unroll
       for (int p = 0; p < j; ++p) v -= L[tri(i, p)] * L[tri(j, p)];
-      L[tri(i, j)] = (i == j) ? sqrtf(v) : v / L[tri(j, j)];
+      if (i == j) {
+        L[tri(i, i)] = sqrtf(v);
+        inv_d[i] = 1.0f / L[tri(i, i)];
+      } else {
+        L[tri(i, j)] = v * inv_d[j];
+      }
     }
   }
 #pragma unroll
@@ -89,14 +96,14 @@ RLENV_D void mm_accel(const float (&th)[K], const float (&om)[K], float torque, 
     float v = rhs[i];
 #pragma unroll
     for (int p = 0; p < i; ++p) v -= L[tri(i, p)] * acc[p];
-    acc[i] = v / L[tri(i, i)];
+    acc[i] = v * inv_d[i];
   }
 #pragma unroll
   for (int i = K - 1; i >= 0; --i) {
     float v = acc[i];
 #pragma unroll
     for (int p = i + 1; p < K; ++p) v -= L[tri(p, i)] * acc[p];
-    acc[i] = v / L[tri(i, i)];
+    acc[i] = v * inv_d[i];
   }
 }
 
@@ -127,18 +134,20 @@ RLENV_D void for_links(F&& f) {
 template <int K>
 __device__ __noinline__ void aba_accel_loops(const float* th, const float* om, float torque,
                                              float* acc) {
-  float vw[K], vx[K], vy[K], U0[K], U1[K], U2[K], uu[K];
+  float vw[K], vx[K], vy[K], sn[K], cs[K], U0[K], U1[K], U2[K], uu[K], iD[K];
   vw[0] = om[0];
   vx[0] = 0.0f;
   vy[0] = 0.0f;
   for (int i = 1; i < K; ++i) {
     const float qd = om[i] - om[i - 1];
-    float sn, cs;
-    sincosf(th[i] - th[i - 1], &sn, &cs);
+    float s, c;
+    sincosf(th[i] - th[i - 1], &s, &c);
+    sn[i] = s;
+    cs[i] = c;
     const float pw = vw[i - 1], px = vx[i - 1], xy = vy[i - 1] + pw;
     vw[i] = pw + qd;
-    vx[i] = cs * px + sn * xy;
-    vy[i] = -sn * px + cs * xy;
+    vx[i] = c * px + s * xy;
+    vy[i] = -s * px + c * xy;
   }
   float cA00 = 0.0f, cA01 = 0.0f, cA02 = 0.0f, cA11 = 0.0f, cA12 = 0.0f, cA22 = 0.0f;
   float cp0 = 0.0f, cp1 = 0.0f, cp2 = 0.0f;
@@ -153,28 +162,28 @@ __device__ __noinline__ void aba_accel_loops(const float* th, const float* om, f
     U1[i] = a01;
     U2[i] = a02;
     uu[i] = -p0;
-    const float D = a00;
-    const float Ia00 = a00 - a00 * a00 / D, Ia01 = a01 - a00 * a01 / D, Ia02 = a02 - a00 * a02 / D;
-    const float Ia11 = a11 - a01 * a01 / D, Ia12 = a12 - a01 * a02 / D, Ia22 = a22 - a02 * a02 / D;
+    const float r = 1.0f / a00;
+    iD[i] = r;
+    const float Ia00 = a00 - a00 * a00 * r, Ia01 = a01 - a00 * a01 * r, Ia02 = a02 - a00 * a02 * r;
+    const float Ia11 = a11 - a01 * a01 * r, Ia12 = a12 - a01 * a02 * r, Ia22 = a22 - a02 * a02 * r;
     const float c1 = qd * y, c2 = -qd * x;
-    const float g = uu[i] / D;
+    const float g = uu[i] * r;
     const float pa0 = p0 + (Ia01 * c1 + Ia02 * c2) + a00 * g;
     const float pa1 = p1 + (Ia11 * c1 + Ia12 * c2) + a01 * g;
     const float pa2 = p2 + (Ia12 * c1 + Ia22 * c2) + a02 * g;
-    float sn, cs;
-    sincosf(th[i] - th[i - 1], &sn, &cs);
-    const float B00 = Ia00 + Ia01 * sn + Ia02 * cs, B01 = Ia01 * cs - Ia02 * sn, B02 = Ia01 * sn + Ia02 * cs;
-    const float B10 = Ia01 + Ia11 * sn + Ia12 * cs, B11 = Ia11 * cs - Ia12 * sn, B12 = Ia11 * sn + Ia12 * cs;
-    const float B20 = Ia02 + Ia12 * sn + Ia22 * cs, B21 = Ia12 * cs - Ia22 * sn, B22 = Ia12 * sn + Ia22 * cs;
-    cA00 = B00 + sn * B10 + cs * B20;
-    cA01 = B01 + sn * B11 + cs * B21;
-    cA02 = B02 + sn * B12 + cs * B22;
-    cA11 = cs * B11 - sn * B21;
-    cA12 = cs * B12 - sn * B22;
-    cA22 = sn * B12 + cs * B22;
-    cp0 = pa0 + sn * pa1 + cs * pa2;
-    cp1 = cs * pa1 - sn * pa2;
-    cp2 = sn * pa1 + cs * pa2;
+    const float s = sn[i], c = cs[i];
+    const float B00 = Ia00 + Ia01 * s + Ia02 * c, B01 = Ia01 * c - Ia02 * s, B02 = Ia01 * s + Ia02 * c;
+    const float B10 = Ia01 + Ia11 * s + Ia12 * c, B11 = Ia11 * c - Ia12 * s, B12 = Ia11 * s + Ia12 * c;
+    const float B20 = Ia02 + Ia12 * s + Ia22 * c, B21 = Ia12 * c - Ia22 * s, B22 = Ia12 * s + Ia22 * c;
+    cA00 = B00 + s * B10 + c * B20;
+    cA01 = B01 + s * B11 + c * B21;
+    cA02 = B02 + s * B12 + c * B22;
+    cA11 = c * B11 - s * B21;
+    cA12 = c * B12 - s * B22;
+    cA22 = s * B12 + c * B22;
+    cp0 = pa0 + s * pa1 + c * pa2;
+    cp1 = c * pa1 - s * pa2;
+    cp2 = s * pa1 + c * pa2;
   }
   {
     const float w = vw[0], x = vx[0], y = vy[0], fy = w + y;
@@ -192,12 +201,10 @@ __device__ __noinline__ void aba_accel_loops(const float* th, const float* om, f
   acc[0] = run;
   for (int i = 1; i < K; ++i) {
     const float qd = om[i] - om[i - 1];
-    float sn, cs;
-    sincosf(th[i] - th[i - 1], &sn, &cs);
     const float xy = ay + aw;
-    const float ap1 = cs * ax + sn * xy + qd * vy[i];
-    const float ap2 = -sn * ax + cs * xy - qd * vx[i];
-    const float q2 = (uu[i] - (U0[i] * aw + U1[i] * ap1 + U2[i] * ap2)) / U0[i];
+    const float ap1 = cs[i] * ax + sn[i] * xy + qd * vy[i];
+    const float ap2 = -sn[i] * ax + cs[i] * xy - qd * vx[i];
+    const float q2 = (uu[i] - (U0[i] * aw + U1[i] * ap1 + U2[i] * ap2)) * iD[i];
     aw = aw + q2;
     ax = ap1;
     ay = ap2;
@@ -206,31 +213,29 @@ __device__ __noinline__ void aba_accel_loops(const float* th, const float* om, f
   }
 }
 
+// The three passes fully unrolled, every per-link array in registers (K <= kUnrollLinks).
 template <int K>
-RLENV_D void aba_accel(const float* th, const float* om, float torque, float* acc) {
-  if constexpr (K > kUnrollLinks) {
-    aba_accel_loops<K>(th, om, torque, acc);
-    return;
-  }
-  float vw[K], vx[K], vy[K], U0[K], U1[K], U2[K], uu[K];
+RLENV_D void aba_accel_unrolled(const float* th, const float* om, float torque, float* acc) {
+  // per link: velocity, the joint rotation's sine and cosine (evaluated once, used by all three
+  // passes), U = I^A S, u and 1 / D
+  float vw[K], vx[K], vy[K], sn[K], cs[K], U0[K], U1[K], U2[K], uu[K], iD[K];
   // outward: link velocities v_i = X_i v_{i-1} + S qd_i; the root has v_0 = (qd_0, 0, 0)
   vw[0] = om[0];
   vx[0] = 0.0f;
   vy[0] = 0.0f;
-  for_links<1, K, true, (K <= kUnrollLinks)>([&](int i) {
+  for_links<1, K, true, true>([&](int i) {
     const float qd = om[i] - om[i - 1];
-    float sn, cs;
-    sincosf(th[i] - th[i - 1], &sn, &cs);
+    sincosf(th[i] - th[i - 1], &sn[i], &cs[i]);
     const float pw = vw[i - 1], px = vx[i - 1], xy = vy[i - 1] + pw;  // joint at (1, 0)
     vw[i] = pw + qd;
-    vx[i] = cs * px + sn * xy;
-    vy[i] = -sn * px + cs * xy;
+    vx[i] = cs[i] * px + sn[i] * xy;
+    vy[i] = -sn[i] * px + cs[i] * xy;
   });
   // inward: articulated inertia and bias force of the subtree, carried to the
   // parent as the child's contribution (cA, cp)
   float cA00 = 0.0f, cA01 = 0.0f, cA02 = 0.0f, cA11 = 0.0f, cA12 = 0.0f, cA22 = 0.0f;
   float cp0 = 0.0f, cp1 = 0.0f, cp2 = 0.0f;
-  for_links<1, K, false, (K <= kUnrollLinks)>([&](int i) {
+  for_links<1, K, false, true>([&](int i) {
     const float w = vw[i], x = vx[i], y = vy[i];
     const float qd = om[i] - om[i - 1];
     // own bias p = v x* (I v), I of a unit mass at (1, 0) = [[1,0,1],[0,1,0],[1,0,1]]
@@ -244,29 +249,29 @@ RLENV_D void aba_accel(const float* th, const float* om, float torque, float* ac
     U1[i] = a01;
     U2[i] = a02;
     uu[i] = -p0;
-    const float D = a00;
-    const float Ia00 = a00 - a00 * a00 / D, Ia01 = a01 - a00 * a01 / D, Ia02 = a02 - a00 * a02 / D;
-    const float Ia11 = a11 - a01 * a01 / D, Ia12 = a12 - a01 * a02 / D, Ia22 = a22 - a02 * a02 / D;
+    const float r = 1.0f / a00;  // D = a00
+    iD[i] = r;
+    const float Ia00 = a00 - a00 * a00 * r, Ia01 = a01 - a00 * a01 * r, Ia02 = a02 - a00 * a02 * r;
+    const float Ia11 = a11 - a01 * a01 * r, Ia12 = a12 - a01 * a02 * r, Ia22 = a22 - a02 * a02 * r;
     const float c1 = qd * y, c2 = -qd * x;  // c_i = v_i x S qd
-    const float g = uu[i] / D;
+    const float g = uu[i] * r;
     const float pa0 = p0 + (Ia01 * c1 + Ia02 * c2) + a00 * g;
     const float pa1 = p1 + (Ia11 * c1 + Ia12 * c2) + a01 * g;
     const float pa2 = p2 + (Ia12 * c1 + Ia22 * c2) + a02 * g;
-    float sn, cs;
-    sincosf(th[i] - th[i - 1], &sn, &cs);
+    const float s = sn[i], c = cs[i];
     // B = Ia X with X = [[1,0,0],[s,c,s],[c,-s,c]] (r = 1); parent gets X^T B and X^T pa
-    const float B00 = Ia00 + Ia01 * sn + Ia02 * cs, B01 = Ia01 * cs - Ia02 * sn, B02 = Ia01 * sn + Ia02 * cs;
-    const float B10 = Ia01 + Ia11 * sn + Ia12 * cs, B11 = Ia11 * cs - Ia12 * sn, B12 = Ia11 * sn + Ia12 * cs;
-    const float B20 = Ia02 + Ia12 * sn + Ia22 * cs, B21 = Ia12 * cs - Ia22 * sn, B22 = Ia12 * sn + Ia22 * cs;
-    cA00 = B00 + sn * B10 + cs * B20;
-    cA01 = B01 + sn * B11 + cs * B21;
-    cA02 = B02 + sn * B12 + cs * B22;
-    cA11 = cs * B11 - sn * B21;
-    cA12 = cs * B12 - sn * B22;
-    cA22 = sn * B12 + cs * B22;
-    cp0 = pa0 + sn * pa1 + cs * pa2;
-    cp1 = cs * pa1 - sn * pa2;
-    cp2 = sn * pa1 + cs * pa2;
+    const float B00 = Ia00 + Ia01 * s + Ia02 * c, B01 = Ia01 * c - Ia02 * s, B02 = Ia01 * s + Ia02 * c;
+    const float B10 = Ia01 + Ia11 * s + Ia12 * c, B11 = Ia11 * c - Ia12 * s, B12 = Ia11 * s + Ia12 * c;
+    const float B20 = Ia02 + Ia12 * s + Ia22 * c, B21 = Ia12 * c - Ia22 * s, B22 = Ia12 * s + Ia22 * c;
+    cA00 = B00 + s * B10 + c * B20;
+    cA01 = B01 + s * B11 + c * B21;
+    cA02 = B02 + s * B12 + c * B22;
+    cA11 = c * B11 - s * B21;
+    cA12 = c * B12 - s * B22;
+    cA22 = s * B12 + c * B22;
+    cp0 = pa0 + s * pa1 + c * pa2;
+    cp1 = c * pa1 - s * pa2;
+    cp2 = s * pa1 + c * pa2;
   });
   {  // root link: its inertia and bias with the whole chain's contribution
     const float w = vw[0], x = vx[0], y = vy[0];
@@ -288,20 +293,27 @@ RLENV_D void aba_accel(const float* th, const float* om, float torque, float* ac
   float aw = 0.0f + qdd;
   float run = qdd;
   acc[0] = run;
-  for_links<1, K, true, (K <= kUnrollLinks)>([&](int i) {
+  for_links<1, K, true, true>([&](int i) {
     const float qd = om[i] - om[i - 1];
-    float sn, cs;
-    sincosf(th[i] - th[i - 1], &sn, &cs);
     const float xy = ay + aw;
-    const float ap1 = cs * ax + sn * xy + qd * vy[i];
-    const float ap2 = -sn * ax + cs * xy - qd * vx[i];
-    const float q2 = (uu[i] - (U0[i] * aw + U1[i] * ap1 + U2[i] * ap2)) / U0[i];
+    const float ap1 = cs[i] * ax + sn[i] * xy + qd * vy[i];
+    const float ap2 = -sn[i] * ax + cs[i] * xy - qd * vx[i];
+    const float q2 = (uu[i] - (U0[i] * aw + U1[i] * ap1 + U2[i] * ap2)) * iD[i];
     aw = aw + q2;
     ax = ap1;
     ay = ap2;
     run += q2;
     acc[i] = run;
   });
+}
+
+template <int K>
+RLENV_D void aba_accel(const float* th, const float* om, float torque, float* acc) {
+  if constexpr (K > kUnrollLinks) {
+    aba_accel_loops<K>(th, om, torque, acc);
+  } else {
+    aba_accel_unrolled<K>(th, om, torque, acc);
+  }
 }
 
 // ---- RK4 step on (theta, omega) (pendulum_np.py:60-66) -----------------------
