@@ -104,6 +104,37 @@ def test_chain_of_steps_stays_valid(cuda, name):
         assert np.all(np.abs(out[:2]) <= np.pi)
 
 
+@pytest.mark.parametrize("dtype", [torch.int32, torch.uint8, torch.int64])
+def test_cartpole_four_envs_per_thread_path(cuda, dtype):
+    """From about 606K environments the CartPole kernels step four environments per thread
+    (16-byte accesses); that path against the oracle at N = 2^20 + 4, one step and a T-step
+    chain, with a shard offset."""
+    import cartpole_metal
+    import rlenv_lib as rl
+
+    n = (1 << 20) + 4
+    r = np.random.default_rng(5)
+    st = r.uniform(-2.5, 2.5, (4, n)).astype(np.float32)
+    act = r.integers(0, 2, n)
+    nxt, rew, dn = (torch.empty((4, n), device=cuda), torch.empty(n, device=cuda),
+                    torch.empty(n, dtype=torch.bool, device=cuda))
+    a_t = torch.from_numpy(act).to(cuda, dtype)
+    rl.check(rl.lib().cartpole_step(torch.from_numpy(st).to(cuda).data_ptr(), a_t.data_ptr(), rl._DTYPES[dtype], 9, n,
+                                    4096, nxt.data_ptr(), rew.data_ptr(), dn.data_ptr(), rl.stream_ptr()))
+    onext, oreward, odone, stepped = kernels.cartpole_step(st, act, 9, index_offset=4096)
+    check_step(f"cartpole_vec4_{dtype}", (nxt, rew, dn), stepped, odone, onext, RTOL, ATOL, ref_reward=oreward)
+    # the T-step kernel on the same path equals the chain of single steps
+    T = 4
+    acts = torch.randint(0, 2, (T, n), device=cuda, generator=torch.Generator(device=cuda).manual_seed(2)).to(dtype)
+    state0 = cartpole_metal.reset(n)
+    cartpole_metal.reseed(300)
+    s = state0
+    for t in range(T):
+        s, _, _ = cartpole_metal.step(s, acts[t])
+    cartpole_metal.reseed(300)
+    assert torch.equal(cartpole_metal.step_many(state0, acts)[0], s)
+
+
 @pytest.mark.parametrize("name", ["cartpole", "acrobot"])
 @pytest.mark.parametrize("dtype", [torch.uint8, torch.int64])
 def test_step_many_equals_chained_steps(cuda, name, dtype):
