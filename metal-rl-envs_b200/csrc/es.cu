@@ -52,28 +52,49 @@ perturb_kernel(const float* __restrict__ theta, int64_t d, float sigma, uint64_t
 
 // Stable ranks by counting: rank_i = #{j : f_j < f_i} + #{j < i : f_j == f_i},
 // in numpy's sort order: NaN after every number, NaNs equal among themselves
-// (ties by index), -0 equal to +0. Fitness tiles are staged through shared
-// memory; every block sees every element, so each thread's count is exact.
-// Each fitness is compared as its order key (rank_order_key, common.cuh).
-__global__ void __launch_bounds__(256)
+// (ties by index), -0 equal to +0; each fitness is compared as its order key
+// (rank_order_key, common.cuh). A warp owns kRankMembersPerWarp members and its
+// lanes stride over tiles of keys staged in shared memory, comparing each key
+// with all of the warp's members; the per-lane counts are summed by shuffles.
+// Integer counts, so the result does not depend on the split.
+constexpr int kRankTile = 4096;
+constexpr int kRankMembersPerWarp = 4;
+constexpr int kRankThreads = 256;
+constexpr int kRankMembersPerBlock = kRankThreads / 32 * kRankMembersPerWarp;
+
+__global__ void __launch_bounds__(kRankThreads)
 ranks_kernel(const float* __restrict__ f, int64_t p, float* __restrict__ ranks) {
-  __shared__ uint32_t tile[1024];
-  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  const uint32_t ki = i < p ? rank_order_key(__ldg(f + i)) : 0u;
-  int64_t below = 0;
-  for (int64_t base = 0; base < p; base += 1024) {
-    const int64_t len = (p - base) < 1024 ? (p - base) : 1024;
+  __shared__ uint32_t tile[kRankTile];
+  const int lane = threadIdx.x & 31;
+  const int64_t first = int64_t(blockIdx.x) * kRankMembersPerBlock +
+                        int64_t(threadIdx.x >> 5) * kRankMembersPerWarp;
+  uint32_t key[kRankMembersPerWarp];
+  int cnt[kRankMembersPerWarp];
+#pragma unroll
+  for (int m = 0; m < kRankMembersPerWarp; ++m) {
+    key[m] = first + m < p ? rank_order_key(__ldg(f + first + m)) : 0u;
+    cnt[m] = 0;
+  }
+  for (int64_t base = 0; base < p; base += kRankTile) {
+    const int len = int((p - base) < kRankTile ? (p - base) : kRankTile);
     __syncthreads();
-    for (int64_t k = threadIdx.x; k < len; k += blockDim.x) tile[k] = rank_order_key(__ldg(f + base + k));
+    for (int k = threadIdx.x; k < len; k += kRankThreads) tile[k] = rank_order_key(__ldg(f + base + k));
     __syncthreads();
-    if (i < p) {
-      for (int64_t k = 0; k < len; ++k) {
-        const uint32_t kj = tile[k];
-        below += (kj < ki) || (kj == ki && base + k < i);
-      }
+    for (int k = lane; k < len; k += 32) {
+      const uint32_t kj = tile[k];
+      const int64_t j = base + k;
+#pragma unroll
+      for (int m = 0; m < kRankMembersPerWarp; ++m)
+        cnt[m] += (kj < key[m]) || (kj == key[m] && j < first + m);
     }
   }
-  if (i < p) ranks[i] = centered_rank(below, p);
+#pragma unroll
+  for (int m = 0; m < kRankMembersPerWarp; ++m) {
+    int c = cnt[m];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+    if (lane == m && first + m < p) ranks[first + m] = centered_rank(c, p);
+  }
 }
 
 // theta_out = theta + lr / (2 pairs sigma) * sum_j (ranks[j] - ranks[j + pairs]) noise_j.
@@ -164,7 +185,8 @@ int rlenv_es_perturb(const float* theta, int64_t d, float sigma, uint64_t seed, 
 int rlenv_es_centered_ranks(const float* fitness, int64_t p, float* ranks, void* stream) {
   using namespace rlenv;
   if (p < 2 || !fitness || !ranks) return RLENV_EINVAL;
-  ranks_kernel<<<grid_for(p), 256, 0, as_stream(stream)>>>(fitness, p, ranks);
+  ranks_kernel<<<grid_for(p, kRankMembersPerBlock), kRankThreads, 0, as_stream(stream)>>>(fitness, p,
+                                                                                          ranks);
   return launch_status();
 }
 

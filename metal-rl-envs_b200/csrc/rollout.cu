@@ -3,14 +3,15 @@
 // entirely on chip (cartpole_rollout_metal.py, acrobot_rollout_metal.py,
 // legged_rollout_metal.py).
 //
-// CartPole and Acrobot: a group of G = min(H, 32) lanes shares one member.
+// CartPole and Acrobot: a group of G lanes shares one member (G a power of two
+// up to H, chosen at launch from the population size: lanes_for below).
 // Lane l owns hidden units l, l + G, ...: their first-layer column, bias and
 // second-layer row stay in registers for the whole rollout. The hidden
 // activations never leave the lane; the logits are a butterfly sum over the
-// group, which leaves the same bits in every lane. Every lane of a group then
-// steps the same physics on the same inputs, so control flow stays uniform
-// in the group, and the group stops at its member's first termination. A
-// population of 4,096 members thus runs as 131,072 threads instead of 4,096.
+// group, which leaves the same bits in every lane (addition is commutative, and
+// every lane adds the same pairs). Every lane of a group then steps the same
+// physics on the same inputs, so control flow stays uniform in the group, and
+// the group stops at its member's first termination.
 //
 // Legged: one thread per member; the hidden layer is formed from weights read
 // through the read-only cache, then four substeps of the contact dynamics.
@@ -38,11 +39,11 @@ RLENV_D int argmax3(float l0, float l1, float l2) {
   return a;
 }
 
-template <int H>
+template <int H, int G>
 __global__ void __launch_bounds__(256)
 cartpole_rollout_kernel(const float* __restrict__ state, const float* __restrict__ theta,
                         int64_t stride, int64_t p, int horizon, float* __restrict__ fitness) {
-  constexpr int G = H < 32 ? H : 32;
+  static_assert(G <= H && H % G == 0 && G <= 32, "a group owns whole hidden units");
   constexpr int U = H / G;
   const int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const int lane = int(threadIdx.x) % G;
@@ -86,11 +87,11 @@ cartpole_rollout_kernel(const float* __restrict__ state, const float* __restrict
   if (valid && lane == 0) fitness[m] = survived;
 }
 
-template <int H>
+template <int H, int G>
 __global__ void __launch_bounds__(256)
 acrobot_rollout_kernel(const float* __restrict__ state, const float* __restrict__ theta,
                        int64_t stride, int64_t p, int horizon, float* __restrict__ fitness) {
-  constexpr int G = H < 32 ? H : 32;
+  static_assert(G <= H && H % G == 0 && G <= 32, "a group owns whole hidden units");
   constexpr int U = H / G;
   const int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const int lane = int(threadIdx.x) % G;
@@ -199,31 +200,63 @@ legged_rollout_kernel(const float* __restrict__ state, const float* __restrict__
 
 using ClassicRollout = void (*)(const float*, const float*, int64_t, int64_t, int, float*);
 
-ClassicRollout pick_cartpole(int h) {
-  switch (h) {
-    case 1: return &cartpole_rollout_kernel<1>;
-    case 2: return &cartpole_rollout_kernel<2>;
-    case 4: return &cartpole_rollout_kernel<4>;
-    case 8: return &cartpole_rollout_kernel<8>;
-    case 16: return &cartpole_rollout_kernel<16>;
-    case 32: return &cartpole_rollout_kernel<32>;
-    case 64: return &cartpole_rollout_kernel<64>;
+// Lanes per member. Every lane of a group steps the same physics, so wide groups repeat it;
+// narrow groups leave few warps and long per-lane MLP chains. The group is the widest power of
+// two (at most H and kMaxLanes) that keeps the launch within kTargetThreads, chosen on a B200
+// at H = 32, horizon 500 (ES generation rollouts; fitness is identical at every width):
+//  - CartPole (about 60 instructions of physics a step): 16 lanes at P = 4,096 and 16,384
+//    (182 and 199 us; 186 and 212 us at 32 lanes, 664 and 670 us at 1).
+//  - Acrobot (about 530): 8 lanes at P = 4,096 (600 us against 1,326 at 32) and 2 at P = 16,384
+//    (760 us against 4,267 at 32), about 32K threads in both.
+struct LanePolicy {
+  int max_lanes;
+  int64_t target_threads;
+};
+constexpr LanePolicy kCartPoleLanes{16, int64_t(1) << 18};
+constexpr LanePolicy kAcrobotLanes{32, int64_t(1) << 15};
+
+int lanes_for(const LanePolicy& pol, int h, int64_t p) {
+  const int cap = h < pol.max_lanes ? h : pol.max_lanes;
+  int g = 1;
+  while (2 * g <= cap && p * 2 * g <= pol.target_threads) g *= 2;
+  return g;
+}
+
+template <template <int, int> class Kern, int H>
+ClassicRollout pick_width(int g) {
+  switch (g) {
+    case 1: return Kern<H, 1>::run;
+    case 2: if constexpr (H >= 2) return Kern<H, 2>::run; else return nullptr;
+    case 4: if constexpr (H >= 4) return Kern<H, 4>::run; else return nullptr;
+    case 8: if constexpr (H >= 8) return Kern<H, 8>::run; else return nullptr;
+    case 16: if constexpr (H >= 16) return Kern<H, 16>::run; else return nullptr;
+    case 32: if constexpr (H >= 32) return Kern<H, 32>::run; else return nullptr;
     default: return nullptr;
   }
 }
 
-ClassicRollout pick_acrobot(int h) {
+template <template <int, int> class Kern>
+ClassicRollout pick_classic(int h, int g) {
   switch (h) {
-    case 1: return &acrobot_rollout_kernel<1>;
-    case 2: return &acrobot_rollout_kernel<2>;
-    case 4: return &acrobot_rollout_kernel<4>;
-    case 8: return &acrobot_rollout_kernel<8>;
-    case 16: return &acrobot_rollout_kernel<16>;
-    case 32: return &acrobot_rollout_kernel<32>;
-    case 64: return &acrobot_rollout_kernel<64>;
+    case 1: return pick_width<Kern, 1>(g);
+    case 2: return pick_width<Kern, 2>(g);
+    case 4: return pick_width<Kern, 4>(g);
+    case 8: return pick_width<Kern, 8>(g);
+    case 16: return pick_width<Kern, 16>(g);
+    case 32: return pick_width<Kern, 32>(g);
+    case 64: return pick_width<Kern, 64>(g);
     default: return nullptr;
   }
 }
+
+template <int H, int G>
+struct CartPoleRollout {
+  static constexpr ClassicRollout run = &cartpole_rollout_kernel<H, G>;
+};
+template <int H, int G>
+struct AcrobotRollout {
+  static constexpr ClassicRollout run = &acrobot_rollout_kernel<H, G>;
+};
 
 using LeggedRollout = void (*)(const float*, const float*, int64_t, int64_t, int, int, float, float,
                                float, float, float*, float*);
@@ -251,13 +284,12 @@ LeggedRollout pick_legged(int c, int h) {
   }
 }
 
-int launch_classic(ClassicRollout fn, int h, const float* state, const float* theta,
+int launch_classic(ClassicRollout fn, int g, const float* state, const float* theta,
                    int64_t stride, int64_t p, int horizon, float* fitness, void* stream) {
   if (p < 0 || horizon < 0 || stride < 0) return RLENV_EINVAL;
   if (!fn) return RLENV_EUNSUPPORTED;
   if (p == 0) return RLENV_OK;
   if (!state || !theta || !fitness) return RLENV_EINVAL;
-  const int g = h < 32 ? h : 32;
   fn<<<grid_for(p * g, 256), 256, 0, as_stream(stream)>>>(state, theta, stride, p, horizon,
                                                           fitness);
   return launch_status();
@@ -270,14 +302,18 @@ extern "C" {
 
 int rlenv_cartpole_rollout(const float* state, const float* theta, int64_t theta_stride, int64_t p,
                            int hidden, int horizon, float* fitness, void* stream) {
-  return rlenv::launch_classic(rlenv::pick_cartpole(hidden), hidden, state, theta, theta_stride, p,
-                               horizon, fitness, stream);
+  using namespace rlenv;
+  const int g = lanes_for(kCartPoleLanes, hidden, p);
+  return launch_classic(pick_classic<CartPoleRollout>(hidden, g), g, state, theta, theta_stride, p,
+                        horizon, fitness, stream);
 }
 
 int rlenv_acrobot_rollout(const float* state, const float* theta, int64_t theta_stride, int64_t p,
                           int hidden, int horizon, float* fitness, void* stream) {
-  return rlenv::launch_classic(rlenv::pick_acrobot(hidden), hidden, state, theta, theta_stride, p,
-                               horizon, fitness, stream);
+  using namespace rlenv;
+  const int g = lanes_for(kAcrobotLanes, hidden, p);
+  return launch_classic(pick_classic<AcrobotRollout>(hidden, g), g, state, theta, theta_stride, p,
+                        horizon, fitness, stream);
 }
 
 int rlenv_legged_rollout(int c, int hidden, int horizon, int iters, float alive, float fall,

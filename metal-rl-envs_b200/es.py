@@ -206,9 +206,10 @@ def curriculum(cfg, gen):
 
 
 # Populations from this size up are ranked by the O(P log P) sort kernel, smaller ones by the
-# one-launch O(P^2) counting kernel; both give the same bits. Measured on a B200, the sort is
-# already faster at P = 2,048 (39 us against 52 us per call) and 370x faster at P = 262,144.
-SORTED_RANKS_FROM = 1024
+# one-launch O(P^2) counting kernel; both give the same bits. Measured per call on a B200: the
+# counting kernel is faster up to P = 8,192 (34 us against 44), the sort from P = 16,384 (50 us
+# against 101; 90 us against 19 ms at P = 262,144).
+SORTED_RANKS_FROM = 16384
 _rank_scratch = {}
 
 
