@@ -531,7 +531,8 @@ def run_workload(args):
                                          stand.data_ptr(), 0.0, None, n, rank * n, dst.data_ptr(), r.data_ptr(),
                                          d.data_ptr(), rl.ptr(imp), torch.cuda.current_stream().cuda_stream))
             fl = rlenv_flops.legged_flops(c, args.iters)["flops"]
-            extra = {"legs": c, "sweeps": args.iters, "impulses": imp is not None}
+            extra = {"legs": c, "sweeps": args.iters, "impulses": imp is not None,
+                     "flops_per_env_step_reference_algorithm": rlenv_flops.legged_reference_flops(c, args.iters)["flops"]}
         else:
             k = args.k
             rows, n_act = 2 * k, 3

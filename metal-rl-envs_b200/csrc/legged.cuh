@@ -83,71 +83,63 @@ RLENV_HD constexpr bool jn_nz(int k, int i) { return i == 1 || i == 2 || i == 3 
 RLENV_D float jt_at(int i, float lca) { return i == 0 ? 1.0f : lca; }
 RLENV_D float jn_at(int i, float lsa) { return i == 1 ? 1.0f : lsa; }
 
-template <int n>
-RLENV_D void cholesky_packed(float (&Lm)[n * (n + 1) / 2], float (&inv_diag)[n]) {
+// ---- the mass matrix in closed form ----------------------------------------
+// M = diag(M_T, M_T, I_T, 0..) + M_F sum_k (Jt_k^T Jt_k + Jn_k^T Jn_k) (legged_np.py:67-72)
+// is an arrowhead matrix: each leg coordinate 3+k couples only to the torso
+// (x, y, phi), never to another leg, and its diagonal is D = M_F (lca^2 + lsa^2)
+// = M_F L^2. Eliminating the legs first leaves the torso's Schur complement
+//   S = [[M_T + (M_F/L^2) sum lsa^2, -(M_F/L^2) sum lca lsa, 0],
+//        [-(M_F/L^2) sum lca lsa, M_T + (M_F/L^2) sum lca^2, 0],
+//        [0, 0, I_T]]
+// (the phi row and column reduce exactly: a leg's own rotation carries the
+// torso's), so M x = b is solved by the 2x2 inverse of S's upper block and a
+// few products per leg: no Cholesky factor and no square roots. The solution
+// is the reference's dense Cholesky solution in exact arithmetic; in float32
+// it differs by rounding only.
+template <int C>
+struct MassInverse {
+  float lca[C], lsa[C];  // L cos a_k, L sin a_k of every foot
+  float s00, s01, s11;   // inverse of S's upper 2x2 block
+};
+
+template <int C>
+RLENV_D void mass_inverse_init(MassInverse<C>& m) {
+  constexpr float kScale = lg::M_F / (lg::L * lg::L);
+  float sss = 0.0f, scc = 0.0f, scs = 0.0f;
 #pragma unroll
-  for (int i = 0; i < n; ++i) {
-#pragma unroll
-    for (int j = 0; j <= i; ++j) {
-      float v = Lm[tri(i, j)];
-#pragma unroll
-      for (int p = 0; p < j; ++p) v -= Lm[tri(i, p)] * Lm[tri(j, p)];
-      if (i == j) {
-        const float d = sqrtf(v);
-        Lm[tri(i, i)] = d;
-        inv_diag[i] = 1.0f / d;
-      } else {
-        Lm[tri(i, j)] = v * inv_diag[j];
-      }
-    }
+  for (int k = 0; k < C; ++k) {
+    sss += m.lsa[k] * m.lsa[k];
+    scc += m.lca[k] * m.lca[k];
+    scs += m.lca[k] * m.lsa[k];
   }
+  const float a = lg::M_T + kScale * sss, d = lg::M_T + kScale * scc, b = -kScale * scs;
+  const float inv_det = 1.0f / (a * d - b * b);
+  m.s00 = d * inv_det;
+  m.s01 = -b * inv_det;
+  m.s11 = a * inv_det;
 }
 
-// L y = b in place, for a b whose first LEAD entries are exactly zero (they
-// stay zero and are skipped).
-template <int n, int LEAD = 0>
-RLENV_D void forward_solve(const float (&Lm)[n * (n + 1) / 2], const float (&inv_diag)[n],
-                           float (&b)[n]) {
+// b <- M^-1 b.
+template <int C>
+RLENV_D void mass_solve(const MassInverse<C>& m, float (&b)[3 + C]) {
+  constexpr float kInvD = 1.0f / (lg::M_F * lg::L * lg::L);
+  constexpr float kInvL2 = 1.0f / (lg::L * lg::L);
+  float r0 = b[0], r1 = b[1], r2 = b[2], t[C];
 #pragma unroll
-  for (int i = 0; i < n; ++i) {
-    if (i < LEAD) {
-      b[i] = 0.0f;
-      continue;
-    }
-    float v = b[i];
-#pragma unroll
-    for (int p = LEAD; p < i; ++p) v -= Lm[tri(i, p)] * b[p];
-    b[i] = v * inv_diag[i];
+  for (int k = 0; k < C; ++k) {
+    t[k] = b[3 + k] * kInvD;
+    r0 -= (m.lca[k] * kInvL2) * b[3 + k];
+    r1 -= (m.lsa[k] * kInvL2) * b[3 + k];
+    r2 -= b[3 + k];
   }
-}
-
-// L^T x = y in place.
-template <int n>
-RLENV_D void back_solve(const float (&Lm)[n * (n + 1) / 2], const float (&inv_diag)[n],
-                        float (&b)[n]) {
+  const float x0 = m.s00 * r0 + m.s01 * r1;
+  const float x1 = m.s01 * r0 + m.s11 * r1;
+  const float x2 = r2 * (1.0f / lg::I_T);
 #pragma unroll
-  for (int i = n - 1; i >= 0; --i) {
-    float v = b[i];
-#pragma unroll
-    for (int p = i + 1; p < n; ++p) v -= Lm[tri(p, i)] * b[p];
-    b[i] = v * inv_diag[i];
-  }
-}
-
-template <int n>
-RLENV_D void cholesky_solve(const float (&Lm)[n * (n + 1) / 2], const float (&inv_diag)[n],
-                            float (&b)[n]) {
-  forward_solve<n>(Lm, inv_diag, b);
-  back_solve<n>(Lm, inv_diag, b);
-}
-
-// Dot product of two length-n vectors from index LEAD on.
-template <int n, int LEAD = 0>
-RLENV_D float dot_from(const float (&a)[n], const float (&b)[n]) {
-  float s = 0.0f;
-#pragma unroll
-  for (int i = LEAD; i < n; ++i) s += a[i] * b[i];
-  return s;
+  for (int k = 0; k < C; ++k) b[3 + k] = t[k] - (m.lca[k] * x0 + m.lsa[k] * x1) * kInvL2 - x2;
+  b[0] = x0;
+  b[1] = x1;
+  b[2] = x2;
 }
 
 // One substep of H for C legs (legged_np.py:57-97), in place on q and v. With
@@ -157,38 +149,26 @@ template <int C, bool BRANCHY, bool IMPULSES = false>
 RLENV_D void legged_substep(float (&q)[3 + C], float (&v)[3 + C], const float (&tq)[C],
                             float assist, int iters, float* imp = nullptr) {
   constexpr int n = 3 + C;
-  float lca[C], lsa[C], dx[C], dy[C], depth[C];
+  MassInverse<C> mi;
+  float dx[C], dy[C], depth[C];
 #pragma unroll
   for (int k = 0; k < C; ++k) {
     float sa, ca;
     sincosf(q[2] + q[3 + k], &sa, &ca);
     const float ad = v[2] + v[3 + k];
-    lca[k] = lg::L * ca;
-    lsa[k] = lg::L * sa;
+    mi.lca[k] = lg::L * ca;
+    mi.lsa[k] = lg::L * sa;
     dx[k] = -lg::L * sa * ad * ad;  // foot acceleration at zero joint acceleration
     dy[k] = lg::L * ca * ad * ad;
     depth[k] = -(q[1] - lg::L * ca);
   }
-  // mass matrix M = M_T diag(1,1,0..) + I_T e_phi e_phi^T + M_F sum_k J_k^T J_k,
-  // lower triangle packed, and the generalised forces
-  float Lm[n * (n + 1) / 2];
+  const float (&lca)[C] = mi.lca;
+  const float (&lsa)[C] = mi.lsa;
+  mass_inverse_init<C>(mi);
+  // generalised forces, then the free velocity v + H M^-1 f
   float f[n];
 #pragma unroll
   for (int i = 0; i < n; ++i) {
-#pragma unroll
-    for (int j = 0; j <= i; ++j) {
-      float s = 0.0f;
-#pragma unroll
-      for (int k = 0; k < C; ++k) {
-        const bool tt = jt_nz(k, i) && jt_nz(k, j);
-        const bool nn = jn_nz(k, i) && jn_nz(k, j);
-        if (tt && nn) s += jt_at(i, lca[k]) * jt_at(j, lca[k]) + jn_at(i, lsa[k]) * jn_at(j, lsa[k]);
-        else if (tt) s += jt_at(i, lca[k]) * jt_at(j, lca[k]);
-        else if (nn) s += jn_at(i, lsa[k]) * jn_at(j, lsa[k]);
-      }
-      const float base = (i == j) ? (i < 2 ? lg::M_T : (i == 2 ? lg::I_T : 0.0f)) : 0.0f;
-      Lm[tri(i, j)] = base + lg::M_F * s;
-    }
     float drift = 0.0f, jn_sum = 0.0f;
 #pragma unroll
     for (int k = 0; k < C; ++k) {
@@ -201,40 +181,39 @@ RLENV_D void legged_substep(float (&q)[3 + C], float (&v)[3 + C], const float (&
     if (i >= 3) f[i] += tq[i - 3];
   }
   f[2] = f[2] - assist * q[2] - (lg::ASSIST_DAMPING * assist) * v[2];
-
-  float inv_diag[n];
-  cholesky_packed<n>(Lm, inv_diag);
-  cholesky_solve<n>(Lm, inv_diag, f);
+  mass_solve<C>(mi, f);
   float vf[n];
 #pragma unroll
   for (int i = 0; i < n; ++i) vf[i] = v[i] + lg::H * f[i];
 
-  // W = L^-1 J^T, one column per contact row (the normal rows start with a zero),
-  // so the Delassus matrix J M^-1 J^T = W^T W is a table of dot products. It is
-  // symmetric: Att and Ann are kept as packed lower triangles over the contacts,
-  // and the tangent-normal block in full (Ant[k][l] = Atn[l][k]).
+  // Delassus matrix J M^-1 J^T in closed form: with g_k = (lsa_k, -lca_k) / L^2
+  // and G[k][l] = g_k . S^-1 g_l (S's upper block), the blocks of contacts k, l are
+  //   Att = lsa_k lsa_l G + [k = l] lca_k^2 / D,  Atn = -lsa_k lca_l G + [k = l] lca_k lsa_k / D,
+  //   Ann = lca_k lca_l G + [k = l] lsa_k^2 / D   (Atn[k][l] pairs k's tangent with l's normal).
+  // Att and Ann are kept as packed lower triangles over the contacts, Atn in full.
+  constexpr float kInvD = 1.0f / (lg::M_F * lg::L * lg::L);
+  constexpr float kInvL2 = 1.0f / (lg::L * lg::L);
   float att[C * (C + 1) / 2], ann[C * (C + 1) / 2], atn[C][C];
   {
-    float Wt[C][n], Wn[C][n];
+    float h0[C], h1[C];  // S^-1 g_l
 #pragma unroll
-    for (int k = 0; k < C; ++k) {
-#pragma unroll
-      for (int i = 0; i < n; ++i) {
-        Wt[k][i] = jt_nz(k, i) ? jt_at(i, lca[k]) : 0.0f;
-        Wn[k][i] = jn_nz(k, i) ? jn_at(i, lsa[k]) : 0.0f;
-      }
-      forward_solve<n, 0>(Lm, inv_diag, Wt[k]);
-      forward_solve<n, 1>(Lm, inv_diag, Wn[k]);
+    for (int l = 0; l < C; ++l) {
+      const float g0 = lsa[l] * kInvL2, g1 = -lca[l] * kInvL2;
+      h0[l] = mi.s00 * g0 + mi.s01 * g1;
+      h1[l] = mi.s01 * g0 + mi.s11 * g1;
     }
 #pragma unroll
     for (int k = 0; k < C; ++k) {
+      const float g0 = lsa[k] * kInvL2, g1 = -lca[k] * kInvL2;
 #pragma unroll
-      for (int l = 0; l <= k; ++l) {
-        att[tri(k, l)] = dot_from<n, 0>(Wt[k], Wt[l]);
-        ann[tri(k, l)] = dot_from<n, 1>(Wn[k], Wn[l]);
+      for (int l = 0; l < C; ++l) {
+        const float gam = g0 * h0[l] + g1 * h1[l];
+        atn[k][l] = -lsa[k] * lca[l] * gam + (k == l ? lca[k] * lsa[k] * kInvD : 0.0f);
+        if (l <= k) {
+          att[tri(k, l)] = lsa[k] * lsa[l] * gam + (k == l ? lca[k] * lca[k] * kInvD : 0.0f);
+          ann[tri(k, l)] = lca[k] * lca[l] * gam + (k == l ? lsa[k] * lsa[k] * kInvD : 0.0f);
+        }
       }
-#pragma unroll
-      for (int l = 0; l < C; ++l) atn[k][l] = dot_from<n, 1>(Wt[k], Wn[l]);
     }
   }
   // free relative velocities J_k v_free and the per-contact constants
@@ -275,7 +254,7 @@ RLENV_D void legged_substep(float (&q)[3 + C], float (&v)[3 + C], const float (&
                                w0n[k] + sn, depth[k], lt[k], ln[k]);
     }
   }
-  // v = v_free + M^-1 J^T lambda, one solve with the factor of M
+  // v = v_free + M^-1 J^T lambda
   float r[n];
 #pragma unroll
   for (int i = 0; i < n; ++i) {
@@ -287,7 +266,7 @@ RLENV_D void legged_substep(float (&q)[3 + C], float (&v)[3 + C], const float (&
     }
     r[i] = ri;
   }
-  cholesky_solve<n>(Lm, inv_diag, r);
+  mass_solve<C>(mi, r);
 #pragma unroll
   for (int i = 0; i < n; ++i) {
     v[i] = vf[i] + r[i];
