@@ -131,6 +131,68 @@ def cpu_throughput(n, budget_s, processes):
     return total / max(secs), sample, processes
 
 
+def _steps_baseline(step, make, n, budget_s, label):
+    """Single-thread env steps/s of an oracle step loop: one untimed warm-up step, then at least
+    5 timed steps (more while the budget lasts) over n environments."""
+    state, acts = make(n)
+    state = step(state, acts(0), 0)
+    t0, steps = time.perf_counter(), 0
+    while steps < 5 or (time.perf_counter() - t0 < budget_s and steps < 1000):
+        state = step(state, acts(steps + 1), steps + 1)
+        steps += 1
+    secs = time.perf_counter() - t0
+    sample = f"{label}: N={n} environments, {steps} timed steps after 1 warm-up, numpy {np.__version__}, 1 thread"
+    return {"value": n * steps / secs, "unit": "env steps/s", "cores": 1, "kind": "port", "sample": sample}
+
+
+def cpu_workload_baseline(workload, args, n, budget_s=10.0):
+    """The reference's numpy path for a bench workload, restated in oracle/ and timed on one host
+    core over a bounded sample of the workload (the reference reports numpy single-threaded)."""
+    sys.path.insert(0, str(ROOT))
+    from oracle import es as oes
+    from oracle import kernels, legged
+
+    rng = np.random.default_rng(0)
+    if workload in ("cartpole_step", "cartpole_single", "acrobot_single"):
+        cp = workload.startswith("cartpole")
+        fn, n_act, bound = (kernels.cartpole_step, 2, 0.05) if cp else (kernels.acrobot_step, 3, 0.1)
+        make = lambda m: (rng.uniform(-bound, bound, (4, m)).astype(np.float32), lambda t: rng.integers(0, n_act, m))
+        return _steps_baseline(lambda s, a, t: fn(s, a, 1 + t)[0], make, min(n, 131_072), budget_s,
+                               "cartpole_np.step" if cp else "acrobot_np.step")
+    if workload in ("pendulum_aba", "pendulum_mm", "pendulum_coop"):
+        k, form = args.k, ("aba" if workload == "pendulum_aba" else "mass_matrix")
+        make = lambda m: (np.concatenate([rng.uniform(-0.1, 0.1, (k, m)), np.zeros((k, m))]).astype(np.float32),
+                          lambda t: rng.integers(0, 3, m))
+        return _steps_baseline(lambda s, a, t: kernels.pendulum_step(s, a, 1 + t, k, form=form)[0], make,
+                               min(n, 4096), budget_s,
+                               f"pendulum_{'aba_' if form == 'aba' else ''}np.Pendulum({k}).step")
+    if workload == "legged_step":
+        c, iters = args.c, args.iters
+        stand = legged.stand_pose(c)[:, None]
+        make = lambda m: ((stand + rng.uniform(-0.05, 0.05, (2 * (3 + c), m))).astype(np.float32),
+                          lambda t: rng.integers(0, 3 ** c, m))
+        return _steps_baseline(lambda s, a, t: kernels.legged_step(s, a, 1 + t, c, iters)[0], make,
+                               min(n, 4096), budget_s, f"legged_np.Legged({c}, {iters}).step")
+    # es_*: one generation of es.py's numpy backend at a bounded population and horizon
+    task = {"es_cartpole": "cartpole", "es_acrobot": "acrobot", "es_legged4": "legged4"}[workload]
+    spec = oes.TASKS[task]
+    pop = min(args.pop or WORKLOADS[workload][1], 1024 if task != "legged4" else 256)
+    horizon = min(args.horizon or WORKLOADS[workload][2], 500 if task != "legged4" else 100)
+    cfg = oes.Config(task=task, pop=pop, horizon=horizon, sigma=0.1, lr=0.03)
+    theta = rng.normal(size=(oes.n_params(spec.hidden, spec),)).astype(np.float32) * 0.1
+    oes.generation(spec, theta, cfg, spec.hidden, rng, 1)  # warm-up
+    t0, gens, taken = time.perf_counter(), 0, 0.0
+    while gens < 1 or (time.perf_counter() - t0 < budget_s and gens < 20):
+        theta, _, steps = oes.generation(spec, theta, cfg, spec.hidden, rng, gens + 2)
+        taken += float(steps.sum())
+        gens += 1
+    secs = time.perf_counter() - t0
+    return {"value": taken / secs, "unit": "env steps/s (steps taken)", "cores": 1, "kind": "port",
+            "ms_per_generation_of_sample": 1e3 * secs / gens,
+            "sample": f"es.generation, numpy backend: P={pop}, horizon {horizon}, {gens} timed generations "
+                      f"after 1 warm-up, numpy {np.__version__}, 1 thread"}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -603,14 +665,23 @@ def run_workload(args):
         secs, clocks = _timed(torch, dist, world, stream, fn, args.steps, 0, local)
         value = 1e3 * secs / args.steps
         if rank == 0:
+            fl = rlenv_flops.es_member_step_flops(task)
+            taken_per_s = state["steps"] / secs  # rank 0's shard; every shard takes about as many
+            achieved = fl["flops"] * taken_per_s * world / 1e12
             line = {"metric": "ES generation ms", "value": value, "unit": "ms", "n_gpus": world, "steps": args.steps,
                     "warmup": args.warmup, "ms_per_step": value, "higher_is_better": False, "scaling": "strong",
                     "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded parameters and initial states)",
                     "config": {"workload": args.workload, "config": desc, "population": pop, "horizon": horizon,
                                "hidden": hidden, "sigma": 0.1, "lr": 0.03,
-                               "env_steps_per_s": state["steps"] * world / secs if world == 1 else None,
-                               "env_steps_taken_rank0": state["steps"]},
+                               "member_steps_nominal_per_generation": pop * horizon,
+                               "member_steps_taken_per_generation": state["steps"] * world / args.steps,
+                               "env_steps_per_s": taken_per_s * world},
+                    "roofline": {"bound": "fp32", "achieved": achieved, "peak": sgemm, "unit": "TFLOP/s",
+                                 "frac": achieved / sgemm if sgemm else None, "flops_per_member_step": fl["flops"],
+                                 "scope": "whole generation (perturb, rollout, ranks, update) over steps taken"},
                     "clocks": clocks}
+            if world == 1 and not args.no_cpu_baseline:
+                line["cpu_baseline"] = cpu_workload_baseline(args.workload, args, pop)
             print(json.dumps(line), flush=True)
         if world > 1:
             dist.destroy_process_group()
@@ -625,11 +696,16 @@ def run_workload(args):
         hbm = {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
                "bytes_per_launch": bytes_launch / T, "peak_kind": "measured (MEASURED_PEAKS.json)"}
         roof = {**hbm, "fp32": fp32} if hbm_bound else {**fp32, "hbm": hbm}
+        if extra.get("impulses"):
+            # the last timed step's normal impulses: the share of feet in active contact
+            extra["contact_active_fraction"] = float((imp[1::2] > 0).float().mean().item())
         line = {"metric": metric, "value": world * units * args.steps / secs, "unit": unit, "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * per, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
                 "config": {"workload": args.workload, "config": desc, "n_envs_per_gpu": n, "env_steps_per_step": T, **extra},
                 "roofline": roof, "clocks": clocks}
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_workload_baseline(args.workload, args, n)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

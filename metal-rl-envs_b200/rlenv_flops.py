@@ -70,3 +70,20 @@ def legged_reference_flops(c, iters=8):
     sub = (10 * c + (n * (n + 1) // 2) * 2 * c + 8 * n * c + n ** 3 / 3 + (2 * c + 1) * 2 * n * n
            + 24 * c * c + 12 * c + iters * c * (8 * (c - 1) + 40) + 4 * n * c + 4 * n)
     return dict(flops=round(4 * sub), transcendentals=4 * (2 * c + n))
+
+
+def es_member_step_flops(task):
+    """Per member-step of a fused ES rollout: the obs-H-out tanh MLP (FMA = 2, one tanh per hidden
+    unit) plus the body's step. CartPole 4-32-2 and Acrobot 6-32-3 (obs = cos/sin of both angles
+    and both velocities); legged4 13-16-12 (three logits per leg) plus 4 substeps at 8 sweeps."""
+    if task == "cartpole":
+        mlp = 2 * (4 * 32 + 32 * 2) + 32 + 2
+        return dict(flops=mlp + CARTPOLE["flops"], transcendentals=32 + CARTPOLE["transcendentals"])
+    if task == "acrobot":
+        mlp = 2 * (6 * 32 + 32 * 3) + 32 + 3
+        return dict(flops=mlp + ACROBOT["flops"], transcendentals=32 + ACROBOT["transcendentals"])
+    if task == "legged4":
+        mlp = 2 * (13 * 16 + 16 * 12) + 16 + 12
+        body = legged_flops(4, 8)
+        return dict(flops=mlp + body["flops"], transcendentals=16 + body["transcendentals"])
+    raise ValueError(task)

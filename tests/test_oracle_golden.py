@@ -110,3 +110,16 @@ def test_es_generation_matches_reference(name, pop, horizon):
     np.testing.assert_allclose(fit, g[f"{name}_fit"], rtol=1e-5, atol=1e-5)
     np.testing.assert_array_equal(steps, g[f"{name}_steps"])
     np.testing.assert_allclose(new, g[f"{name}_theta1"], rtol=1e-5, atol=1e-6)
+
+
+def test_es_solve_fixture_reproduces():
+    """tests/golden/es_solve.npz (10-seed generations-to-solve of the oracle's train loop) is
+    what the committed script computes: seed 3 of each task rerun here."""
+    from oracle import es as oes
+
+    g = golden("es_solve")
+    for task in ("cartpole", "acrobot"):
+        pop, max_gen = (int(x) for x in g[f"{task}_config"])
+        r = oes.train(oes.Config(task=task, pop=pop, max_generations=max_gen, time_budget=1e9), 3)
+        assert (r.solved, r.generations, r.env_steps) == (bool(g[f"{task}_solved"][3]), int(g[f"{task}_generations"][3]),
+                                                          int(g[f"{task}_env_steps"][3]))
