@@ -125,6 +125,21 @@ RLENV_D uint32_t rank_order_key(float f) {
 // Centred rank of sorted position r among p members (es.py:214-215).
 RLENV_D float centered_rank(int64_t r, int64_t p) { return float(r) / float(p - 1) - 0.5f; }
 
+// x - 2 pi floor((x + pi) / 2 pi): an angle to [-pi, pi), bit for bit as that
+// float32 expression (acrobot_np.py:87-89, pendulum_np.py:110-111). The quotient is
+// formed by a multiply; it can fall on the other side of an integer than the
+// division only within a few ulp of one, and there (or far outside the angles a
+// step produces) the division decides.
+RLENV_D float wrap_to_pi(float x) {
+  constexpr float kPi = 3.141592653589793f, kTwoPi = 6.283185307179586f;
+  const float y = x + kPi;
+  const float q = y * (1.0f / kTwoPi);
+  float f = floorf(q);
+  const float r = q - f;
+  if (r < 2e-6f || r > 1.0f - 2e-6f || fabsf(q) > 8.0f) f = floorf(y / kTwoPi);
+  return x - kTwoPi * f;
+}
+
 // Index of element (i, j), j <= i, of a lower triangle stored row by row.
 RLENV_HD constexpr int tri(int i, int j) { return i * (i + 1) / 2 + j; }
 

@@ -19,7 +19,7 @@ constexpr float TWO_PI = 6.283185307179586f;
 constexpr float RESET_BOUND = 0.1f;
 }  // namespace pd
 
-RLENV_D float pd_wrap(float x) { return x - pd::TWO_PI * floorf((x + pd::PI) / pd::TWO_PI); }
+RLENV_D float pd_wrap(float x) { return wrap_to_pi(x); }  // pendulum_np.py wrap
 
 // Calls f(i) for i = 0 .. N-1, fully unrolled when UNROLL, as a plain loop
 // otherwise. A per-environment array is either always indexed by constants
