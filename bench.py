@@ -586,12 +586,12 @@ def run_workload(args):
             state_a = rl.reset_uniform(rows, n, 0.05, center=stand, seed=3, index_offset=rank * n, dev=dev)
 
             # BASELINE's legged outputs per step: state, contact impulses and the fall flag
-            imp = torch.empty((2 * c, n), device=dev) if not args.no_impulses else None
+            imp = torch.empty((T, 2 * c, n), device=dev) if not args.no_impulses else None
 
-            def entry(src, dst, t, r, d):
-                rl.check(lib.legged_step(c, args.iters, src.data_ptr(), actions[t].data_ptr(), rl.U8, 1 + t,
-                                         stand.data_ptr(), 0.0, None, n, rank * n, dst.data_ptr(), r.data_ptr(),
-                                         d.data_ptr(), rl.ptr(imp), torch.cuda.current_stream().cuda_stream))
+            def launch_many(src, dst, r, d):
+                rl.check(lib.legged_step_many(c, args.iters, src.data_ptr(), actions.data_ptr(), rl.U8, 1,
+                                              stand.data_ptr(), 0.0, None, T, n, rank * n, dst.data_ptr(),
+                                              r.data_ptr(), d.data_ptr(), rl.ptr(imp), sp))
             fl = rlenv_flops.legged_flops(c, args.iters)["flops"]
             extra = {"legs": c, "sweeps": args.iters, "impulses": imp is not None,
                      "flops_per_env_step_reference_algorithm": rlenv_flops.legged_reference_flops(c, args.iters)["flops"]}
@@ -599,29 +599,26 @@ def run_workload(args):
             k = args.k
             rows, n_act = 2 * k, 3
             state_a = rl.reset_uniform(rows, n, 0.1, seed=3, index_offset=rank * n, dev=dev)
-            fn_name = {"pendulum_aba": "pendulum_aba_step", "pendulum_mm": "pendulum_mm_step",
-                       "pendulum_coop": "pendulum_coop_step"}[args.workload]
+            fn_name = {"pendulum_aba": "pendulum_aba_step_many", "pendulum_mm": "pendulum_mm_step_many",
+                       "pendulum_coop": "pendulum_coop_step_many"}[args.workload]
             head = (k, 0) if args.workload == "pendulum_mm" else (k,)
             abi = getattr(lib, fn_name)
 
-            def entry(src, dst, t, r, d):
-                rl.check(abi(*head, src.data_ptr(), actions[t].data_ptr(), rl.U8, 1 + t, n, rank * n, dst.data_ptr(),
-                             r.data_ptr(), d.data_ptr(), torch.cuda.current_stream().cuda_stream))
+            def launch_many(src, dst, r, d):
+                rl.check(abi(*head, src.data_ptr(), actions.data_ptr(), rl.U8, 1, T, n, rank * n, dst.data_ptr(),
+                             r.data_ptr(), d.data_ptr(), sp))
             fl = (rlenv_flops.aba_flops(k) if args.workload == "pendulum_aba" else rlenv_flops.mass_matrix_flops(k))["flops"]
             extra = {"links": k}
         actions = torch.randint(0, n_act, (T, n), device=dev, generator=g).to(torch.uint8 if n_act < 256 else torch.int32)
         state_b = torch.empty_like(state_a)
         rew, dn = torch.empty((T, n), device=dev), torch.empty((T, n), device=dev, dtype=torch.bool)
-
-        def launch_one(t):
-            src, dst = (state_a, state_b) if t % 2 == 0 else (state_b, state_a)
-            entry(src, dst, t, rew[t], dn[t])
-        graph = _graph_steps(torch, launch_one, T)
+        extra["kernel"] = "T-step kernel: T steps per launch, state on chip between steps"
 
         def fn():
-            graph.replay()
+            launch_many(state_a, state_b, rew, dn)
         units, unit, metric, flops = n * T, "env steps/s", METRIC, fl
-        bytes_launch = n * T * (2 * 4 * rows + 1 + 5 + (8 * args.c if extra.get("impulses") else 0))
+        # the state is read and written once per launch; actions, rewards, dones (and impulses) every step
+        bytes_launch = n * 2 * 4 * rows + n * T * (1 + 5 + (8 * args.c if extra.get("impulses") else 0))
     elif args.workload == "es_ranks":
         import es
 
@@ -698,7 +695,7 @@ def run_workload(args):
         roof = {**hbm, "fp32": fp32} if hbm_bound else {**fp32, "hbm": hbm}
         if extra.get("impulses"):
             # the last timed step's normal impulses: the share of feet in active contact
-            extra["contact_active_fraction"] = float((imp[1::2] > 0).float().mean().item())
+            extra["contact_active_fraction"] = float((imp[-1, 1::2] > 0).float().mean().item())
         line = {"metric": metric, "value": world * units * args.steps / secs, "unit": unit, "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * per, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",

@@ -106,6 +106,18 @@ RLENV_API int rlenv_pendulum_mm_step(int k, int pairwise_trig, const float* stat
                            int action_dtype, uint32_t seed, int64_t n, int64_t index_offset,
                            float* next_state, float* reward, uint8_t* done, void* stream);
 
+/* `steps` consecutive steps of rlenv_pendulum_mm_step in one launch, the state
+ * kept on chip: actions (steps, n); step t draws its resets from seed0 + t and
+ * writes row t of reward_seq / done_seq (steps, n), each of which may be NULL.
+ * Equal bit for bit to `steps` single-step calls with seeds seed0, seed0 + 1, ...
+ * The reference has no multi-step call; it replaces a caller's loop of
+ * Pendulum.step (bench_pendulum.py:36-48). The same holds for the *_step_many
+ * entry points below. */
+RLENV_API int rlenv_pendulum_mm_step_many(int k, int pairwise_trig, const float* state, const void* actions,
+                                int action_dtype, uint32_t seed0, int64_t steps, int64_t n,
+                                int64_t index_offset, float* state_out, float* reward_seq,
+                                uint8_t* done_seq, void* stream);
+
 /* Mass-matrix form with k lanes of a warp per environment, lane j owning row j
  * of the mass matrix. Replaces `pendulum{K}_coop_step`
  * (pendulum_metal_coop.py:28-149). k in {2, 4, 8, 16, 32}. */
@@ -113,12 +125,22 @@ RLENV_API int rlenv_pendulum_coop_step(int k, const float* state, const void* ac
                              uint32_t seed, int64_t n, int64_t index_offset,
                              float* next_state, float* reward, uint8_t* done, void* stream);
 
+RLENV_API int rlenv_pendulum_coop_step_many(int k, const float* state, const void* actions, int action_dtype,
+                                  uint32_t seed0, int64_t steps, int64_t n, int64_t index_offset,
+                                  float* state_out, float* reward_seq, uint8_t* done_seq,
+                                  void* stream);
+
 /* Articulated-body (Featherstone) form, O(k) per stage, one thread per
  * environment. Replaces `pendulum{K}_aba_step` (pendulum_aba_metal.py:14-144).
  * Built for k in 1..16, 24, 32, 48, 64. */
 RLENV_API int rlenv_pendulum_aba_step(int k, const float* state, const void* action, int action_dtype,
                             uint32_t seed, int64_t n, int64_t index_offset,
                             float* next_state, float* reward, uint8_t* done, void* stream);
+
+RLENV_API int rlenv_pendulum_aba_step_many(int k, const float* state, const void* actions, int action_dtype,
+                                 uint32_t seed0, int64_t steps, int64_t n, int64_t index_offset,
+                                 float* state_out, float* reward_seq, uint8_t* done_seq,
+                                 void* stream);
 
 /* ---- Hopper and legged bodies ---------------------------------------------
  * Legged body with c legs and c hard contacts (legged_metal.py:13-185):
@@ -140,6 +162,15 @@ RLENV_API int rlenv_legged_step(int c, int iters, const float* state, const void
                       float* next_state, float* reward, uint8_t* done, float* impulses,
                       void* stream);
 
+/* `steps` legged steps in one launch (see rlenv_pendulum_mm_step_many);
+ * impulse_seq, when not NULL, is (steps, 2c, n): step t's impulses as
+ * rlenv_legged_step writes them. */
+RLENV_API int rlenv_legged_step_many(int c, int iters, const float* state, const void* actions,
+                           int action_dtype, uint32_t seed0, const float* stand, float assist,
+                           const float* assist_ptr, int64_t steps, int64_t n, int64_t index_offset,
+                           float* state_out, float* reward_seq, uint8_t* done_seq,
+                           float* impulse_seq, void* stream);
+
 /* Hopper: the one-legged body with an exact single-contact solve, equal to the
  * legged body with c = 1 and one sweep. Replaces `hopper_step` and
  * `hopper_step_branchy` (hopper_metal.py:13-138): branchy != 0 skips the
@@ -148,6 +179,11 @@ RLENV_API int rlenv_legged_step(int c, int iters, const float* state, const void
 RLENV_API int rlenv_hopper_step(int branchy, const float* state, const void* action, int action_dtype,
                       uint32_t seed, const float* stand, int64_t n, int64_t index_offset,
                       float* next_state, float* reward, uint8_t* done, void* stream);
+
+RLENV_API int rlenv_hopper_step_many(int branchy, const float* state, const void* actions, int action_dtype,
+                           uint32_t seed0, const float* stand, int64_t steps, int64_t n,
+                           int64_t index_offset, float* state_out, float* reward_seq,
+                           uint8_t* done_seq, void* stream);
 
 /* ---- Fused ES rollouts ------------------------------------------------------
  * One launch runs a whole population: member i runs its own MLP policy from

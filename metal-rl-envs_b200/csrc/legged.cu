@@ -29,13 +29,18 @@ RLENV_D void decode_torques(int a, float (&tq)[C]) {
   }
 }
 
+// T steps per launch with the state in registers; step t reads actions[t * n + e],
+// draws its resets from seed0 + t, and writes reward_seq / done_seq row t (when not
+// null) and, with IMPULSES, rows [t * 2C, t * 2C + 2C) of impulse_seq. One step is
+// the launch with T = 1, so a chain of single steps and one T-step launch agree bit
+// for bit.
 template <int C, bool BRANCHY, bool IMPULSES>
 __global__ void __launch_bounds__(128)
-legged_kernel(const float* __restrict__ state, const void* __restrict__ action, int dtype,
-              uint32_t seed, const float* __restrict__ stand, float assist,
-              const float* __restrict__ assist_ptr, int iters, int64_t n, int64_t off,
-              float* __restrict__ next, float* __restrict__ reward, uint8_t* __restrict__ done,
-              float* __restrict__ impulses) {
+legged_kernel(const float* __restrict__ state, const void* __restrict__ actions, int dtype,
+              uint32_t seed0, const float* __restrict__ stand, float assist,
+              const float* __restrict__ assist_ptr, int iters, int64_t T, int64_t n, int64_t off,
+              float* __restrict__ next, float* __restrict__ reward_seq,
+              uint8_t* __restrict__ done_seq, float* __restrict__ impulse_seq) {
   constexpr int nq = 3 + C;
   const int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (e >= n) return;
@@ -45,33 +50,47 @@ legged_kernel(const float* __restrict__ state, const void* __restrict__ action, 
     q[i] = __ldg(state + i * n + e);
     v[i] = __ldg(state + (nq + i) * n + e);
   }
-  float tq[C];
-  decode_torques<C>(action_at(action, dtype, e), tq);
   const float k_assist = assist_ptr ? __ldg(assist_ptr) : assist;
-  float imp[2 * C];
+  int act = T > 0 ? action_at(actions, dtype, e) : 0;  // loaded one step ahead
+  for (int64_t t = 0; t < T; ++t) {
+    float tq[C];
+    decode_torques<C>(act, tq);
+    if (t + 1 < T) act = action_at(actions, dtype, (t + 1) * n + e);
+    float imp[2 * C];
 #pragma unroll
-  for (int k = 0; k < 2 * C; ++k) imp[k] = 0.0f;
+    for (int k = 0; k < 2 * C; ++k) imp[k] = 0.0f;
 #pragma unroll 1
-  for (int sub = 0; sub < lg::SUBSTEPS; ++sub)
-    legged_substep<C, BRANCHY, IMPULSES>(q, v, tq, k_assist, iters, imp);
-  if constexpr (IMPULSES) {
+    for (int sub = 0; sub < lg::SUBSTEPS; ++sub)
+      legged_substep<C, BRANCHY, IMPULSES>(q, v, tq, k_assist, iters, imp);
+    if constexpr (IMPULSES) {
 #pragma unroll
-    for (int k = 0; k < 2 * C; ++k) impulses[k * n + e] = imp[k];
-  }
-  const bool d = legged_terminated<C>(q);
-  const uint32_t h = env_hash(seed, off + e);
+      for (int k = 0; k < 2 * C; ++k) impulse_seq[(t * 2 * C + k) * n + e] = imp[k];
+    }
+    const bool d = legged_terminated<C>(q);
+    const float rw = d ? 0.0f : v[0] + 1.0f;
+    if (d) {
+      const uint32_t h = env_hash(seed0 + uint32_t(t), off + e);
 #pragma unroll
-  for (int i = 0; i < 2 * nq; ++i) {
-    const float fresh =
-        __fadd_rn(__ldg(stand + i), uniform_pm(pcg_hash(h + uint32_t(i) * kRowStride), lg::RESET_BOUND));
-    next[i * n + e] = d ? fresh : (i < nq ? q[i] : v[i - nq]);
+      for (int i = 0; i < 2 * nq; ++i) {
+        const float fresh =
+            __fadd_rn(__ldg(stand + i), uniform_pm(pcg_hash(h + uint32_t(i) * kRowStride), lg::RESET_BOUND));
+        if (i < nq) q[i] = fresh;
+        else v[i - nq] = fresh;
+      }
+    }
+    if (reward_seq) reward_seq[t * n + e] = rw;
+    if (done_seq) done_seq[t * n + e] = d;
   }
-  reward[e] = d ? 0.0f : v[0] + 1.0f;
-  done[e] = d;
+#pragma unroll
+  for (int i = 0; i < nq; ++i) {
+    next[i * n + e] = q[i];
+    next[(nq + i) * n + e] = v[i];
+  }
 }
 
 using LeggedFn = void (*)(const float*, const void*, int, uint32_t, const float*, float,
-                          const float*, int, int64_t, int64_t, float*, float*, uint8_t*, float*);
+                          const float*, int, int64_t, int64_t, int64_t, float*, float*, uint8_t*,
+                          float*);
 
 template <bool IMPULSES>
 LeggedFn pick_c(int c, bool branchy) {
@@ -89,18 +108,18 @@ LeggedFn pick(int c, bool branchy, bool impulses) {
   return impulses ? pick_c<true>(c, branchy) : pick_c<false>(c, branchy);
 }
 
-int launch_legged(int c, bool branchy, int iters, const float* state, const void* action,
-                  int dtype, uint32_t seed, const float* stand, float assist,
-                  const float* assist_ptr, int64_t n, int64_t off, float* next, float* reward,
-                  uint8_t* done, float* impulses, void* stream) {
-  if (n < 0 || !valid_dtype(dtype) || iters < 1) return RLENV_EINVAL;
-  LeggedFn fn = pick(c, branchy, impulses != nullptr);
+int launch_legged(int c, bool branchy, int iters, const float* state, const void* actions,
+                  int dtype, uint32_t seed0, const float* stand, float assist,
+                  const float* assist_ptr, int64_t T, int64_t n, int64_t off, float* next,
+                  float* reward_seq, uint8_t* done_seq, float* impulse_seq, void* stream) {
+  if (n < 0 || T < 0 || !valid_dtype(dtype) || iters < 1) return RLENV_EINVAL;
+  LeggedFn fn = pick(c, branchy, impulse_seq != nullptr);
   if (!fn) return RLENV_EUNSUPPORTED;
   if (n == 0) return RLENV_OK;
-  if (!state || !action || !stand || !next || !reward || !done) return RLENV_EINVAL;
-  fn<<<grid_for(n, 128), 128, 0, as_stream(stream)>>>(state, action, dtype, seed, stand, assist,
-                                                      assist_ptr, iters, n, off, next, reward,
-                                                      done, impulses);
+  if (!state || (T > 0 && !actions) || !stand || !next) return RLENV_EINVAL;
+  fn<<<grid_for(n, 128), 128, 0, as_stream(stream)>>>(state, actions, dtype, seed0, stand, assist,
+                                                      assist_ptr, iters, T, n, off, next,
+                                                      reward_seq, done_seq, impulse_seq);
   return launch_status();
 }
 
@@ -113,16 +132,38 @@ int rlenv_legged_step(int c, int iters, const float* state, const void* action, 
                       uint32_t seed, const float* stand, float assist, const float* assist_ptr,
                       int64_t n, int64_t index_offset, float* next_state, float* reward,
                       uint8_t* done, float* impulses, void* stream) {
+  if (n > 0 && (!reward || !done)) return RLENV_EINVAL;
   return rlenv::launch_legged(c, false, iters, state, action, action_dtype, seed, stand, assist,
-                              assist_ptr, n, index_offset, next_state, reward, done, impulses,
+                              assist_ptr, 1, n, index_offset, next_state, reward, done, impulses,
                               stream);
+}
+
+int rlenv_legged_step_many(int c, int iters, const float* state, const void* actions,
+                           int action_dtype, uint32_t seed0, const float* stand, float assist,
+                           const float* assist_ptr, int64_t steps, int64_t n, int64_t index_offset,
+                           float* state_out, float* reward_seq, uint8_t* done_seq,
+                           float* impulse_seq, void* stream) {
+  return rlenv::launch_legged(c, false, iters, state, actions, action_dtype, seed0, stand, assist,
+                              assist_ptr, steps, n, index_offset, state_out, reward_seq, done_seq,
+                              impulse_seq, stream);
 }
 
 int rlenv_hopper_step(int branchy, const float* state, const void* action, int action_dtype,
                       uint32_t seed, const float* stand, int64_t n, int64_t index_offset,
                       float* next_state, float* reward, uint8_t* done, void* stream) {
+  if (n > 0 && (!reward || !done)) return RLENV_EINVAL;
   return rlenv::launch_legged(1, branchy != 0, 1, state, action, action_dtype, seed, stand, 0.0f,
-                              nullptr, n, index_offset, next_state, reward, done, nullptr, stream);
+                              nullptr, 1, n, index_offset, next_state, reward, done, nullptr,
+                              stream);
+}
+
+int rlenv_hopper_step_many(int branchy, const float* state, const void* actions, int action_dtype,
+                           uint32_t seed0, const float* stand, int64_t steps, int64_t n,
+                           int64_t index_offset, float* state_out, float* reward_seq,
+                           uint8_t* done_seq, void* stream) {
+  return rlenv::launch_legged(1, branchy != 0, 1, state, actions, action_dtype, seed0, stand, 0.0f,
+                              nullptr, steps, n, index_offset, state_out, reward_seq, done_seq,
+                              nullptr, stream);
 }
 
 }  // extern "C"

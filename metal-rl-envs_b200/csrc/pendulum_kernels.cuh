@@ -23,11 +23,16 @@ RLENV_D int action_at(const void* a, int dtype, int64_t i) {
 
 enum Form { MASS_MATRIX = 0, MASS_MATRIX_PAIRWISE = 1, ARTICULATED = 2 };
 
+// T steps of N environments in one launch, the state in registers (local
+// memory above kUnrollLinks) between steps; step t reads actions[t * n + e],
+// draws its resets from seed0 + t and writes reward_seq / done_seq row t when
+// those are not null. One step is the launch with T = 1, so a chain of single
+// steps and one T-step launch run the same code and agree bit for bit.
 template <int K, int FORM>
 __global__ void __launch_bounds__(128)
-pendulum_kernel(const float* __restrict__ state, const void* __restrict__ action, int dtype,
-                uint32_t seed, int64_t n, int64_t off, float* __restrict__ next,
-                float* __restrict__ reward, uint8_t* __restrict__ done) {
+pendulum_kernel(const float* __restrict__ state, const void* __restrict__ actions, int dtype,
+                uint32_t seed0, int64_t T, int64_t n, int64_t off, float* __restrict__ next,
+                float* __restrict__ reward_seq, uint8_t* __restrict__ done_seq) {
   constexpr bool U = K <= kUnrollLinks;  // one indexing style for every per-link array of this K
   const int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (e >= n) return;
@@ -36,26 +41,36 @@ pendulum_kernel(const float* __restrict__ state, const void* __restrict__ action
     th[j] = __ldg(state + j * n + e);
     om[j] = __ldg(state + (K + j) * n + e);
   });
-  const float torque = float(action_at(action, dtype, e) - 1) * pd::TORQUE;
-  if constexpr (FORM == ARTICULATED) {
-    pendulum_rk4<K, U>(th, om, torque, [](const float* t, const float* o, float tq, float* a) {
-      aba_accel<K>(t, o, tq, a);
-    });
-  } else {
-    pendulum_rk4<K, U>(th, om, torque,
-                       [](const float (&t)[K], const float (&o)[K], float tq, float (&a)[K]) {
-                         mm_accel<K, FORM == MASS_MATRIX_PAIRWISE>(t, o, tq, a);
-                       });
+  // each step's action is loaded one step ahead, off the step's dependency chain
+  int act = T > 0 ? action_at(actions, dtype, e) : 0;
+  for (int64_t t = 0; t < T; ++t) {
+    const float torque = float(act - 1) * pd::TORQUE;
+    if (t + 1 < T) act = action_at(actions, dtype, (t + 1) * n + e);
+    if constexpr (FORM == ARTICULATED) {
+      pendulum_rk4<K, U>(th, om, torque, [](const float* a_t, const float* a_o, float tq, float* a) {
+        aba_accel<K>(a_t, a_o, tq, a);
+      });
+    } else {
+      pendulum_rk4<K, U>(th, om, torque,
+                         [](const float (&a_t)[K], const float (&a_o)[K], float tq, float (&a)[K]) {
+                           mm_accel<K, FORM == MASS_MATRIX_PAIRWISE>(a_t, a_o, tq, a);
+                         });
+    }
+    const bool d = pendulum_terminated<K, U>(th);
+    if (d) {
+      const uint32_t h = env_hash(seed0 + uint32_t(t), off + e);
+      for_range<K, U>([&](int j) {
+        th[j] = uniform_pm(pcg_hash(h + uint32_t(j) * kRowStride), pd::RESET_BOUND);
+        om[j] = uniform_pm(pcg_hash(h + uint32_t(K + j) * kRowStride), pd::RESET_BOUND);
+      });
+    }
+    if (reward_seq) reward_seq[t * n + e] = d ? 0.0f : -1.0f;
+    if (done_seq) done_seq[t * n + e] = d;
   }
-  const bool d = pendulum_terminated<K, U>(th);
-  const uint32_t h = env_hash(seed, off + e);
   for_range<K, U>([&](int j) {
-    next[j * n + e] = d ? uniform_pm(pcg_hash(h + uint32_t(j) * kRowStride), pd::RESET_BOUND) : th[j];
-    next[(K + j) * n + e] =
-        d ? uniform_pm(pcg_hash(h + uint32_t(K + j) * kRowStride), pd::RESET_BOUND) : om[j];
+    next[j * n + e] = th[j];
+    next[(K + j) * n + e] = om[j];
   });
-  reward[e] = d ? 0.0f : -1.0f;
-  done[e] = d;
 }
 
 // ---- K lanes per environment (pendulum_metal_coop.py:28-149) -----------------
@@ -121,46 +136,53 @@ RLENV_D float coop_accel(float th_j, float om_j, float torque, int j) {
 
 template <int K>
 __global__ void __launch_bounds__(256)
-pendulum_coop_kernel(const float* __restrict__ state, const void* __restrict__ action, int dtype,
-                     uint32_t seed, int64_t n, int64_t off, float* __restrict__ next,
-                     float* __restrict__ reward, uint8_t* __restrict__ done) {
-  const int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+pendulum_coop_kernel(const float* __restrict__ state, const void* __restrict__ actions, int dtype,
+                     uint32_t seed0, int64_t T, int64_t n, int64_t off, float* __restrict__ next,
+                     float* __restrict__ reward_seq, uint8_t* __restrict__ done_seq) {
+  const int64_t t_id = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const int j = int(threadIdx.x) & (K - 1);
-  const int64_t e_raw = t / K;
+  const int64_t e_raw = t_id / K;
   const bool valid = e_raw < n;
   const int64_t e = valid ? e_raw : n - 1;  // idle lanes mirror the last env to keep shuffles full
-  const float th = __ldg(state + j * n + e);
-  const float om = __ldg(state + (K + j) * n + e);
-  const float torque = float(action_at(action, dtype, e) - 1) * pd::TORQUE;
-  const float a1 = coop_accel<K>(th, om, torque, j);
-  float dth = om, dom = a1;
-  float ts = th + pd::HALF_DT * om, os = om + pd::HALF_DT * a1;
-  const float a2 = coop_accel<K>(ts, os, torque, j);
-  dth += 2.0f * os;
-  dom += 2.0f * a2;
-  ts = th + pd::HALF_DT * os;
-  os = om + pd::HALF_DT * a2;
-  const float a3 = coop_accel<K>(ts, os, torque, j);
-  dth += 2.0f * os;
-  dom += 2.0f * a3;
-  ts = th + pd::DT * os;
-  os = om + pd::DT * a3;
-  const float a4 = coop_accel<K>(ts, os, torque, j);
-  const float nth = pd_wrap(th + pd::SIXTH_DT * (dth + os));
-  const float nom = fminf(fmaxf(om + pd::SIXTH_DT * (dom + a4), -pd::MAX_VEL), pd::MAX_VEL);
-  const bool d = -seg_sum<K>(cosf(nth)) > float(K) * 0.5f;
-  if (!valid) return;
-  const uint32_t h = env_hash(seed, off + e);
-  next[j * n + e] = d ? uniform_pm(pcg_hash(h + uint32_t(j) * kRowStride), pd::RESET_BOUND) : nth;
-  next[(K + j) * n + e] =
-      d ? uniform_pm(pcg_hash(h + uint32_t(K + j) * kRowStride), pd::RESET_BOUND) : nom;
-  if (j == 0) {
-    reward[e] = d ? 0.0f : -1.0f;
-    done[e] = d;
+  float th = __ldg(state + j * n + e);
+  float om = __ldg(state + (K + j) * n + e);
+  int act = T > 0 ? action_at(actions, dtype, e) : 0;  // loaded one step ahead
+  for (int64_t t = 0; t < T; ++t) {
+    const float torque = float(act - 1) * pd::TORQUE;
+    if (t + 1 < T) act = action_at(actions, dtype, (t + 1) * n + e);
+    const float a1 = coop_accel<K>(th, om, torque, j);
+    float dth = om, dom = a1;
+    float ts = th + pd::HALF_DT * om, os = om + pd::HALF_DT * a1;
+    const float a2 = coop_accel<K>(ts, os, torque, j);
+    dth += 2.0f * os;
+    dom += 2.0f * a2;
+    ts = th + pd::HALF_DT * os;
+    os = om + pd::HALF_DT * a2;
+    const float a3 = coop_accel<K>(ts, os, torque, j);
+    dth += 2.0f * os;
+    dom += 2.0f * a3;
+    ts = th + pd::DT * os;
+    os = om + pd::DT * a3;
+    const float a4 = coop_accel<K>(ts, os, torque, j);
+    th = pd_wrap(th + pd::SIXTH_DT * (dth + os));
+    om = fminf(fmaxf(om + pd::SIXTH_DT * (dom + a4), -pd::MAX_VEL), pd::MAX_VEL);
+    const bool d = -seg_sum<K>(cosf(th)) > float(K) * 0.5f;
+    if (d) {
+      const uint32_t h = env_hash(seed0 + uint32_t(t), off + e);
+      th = uniform_pm(pcg_hash(h + uint32_t(j) * kRowStride), pd::RESET_BOUND);
+      om = uniform_pm(pcg_hash(h + uint32_t(K + j) * kRowStride), pd::RESET_BOUND);
+    }
+    if (valid && j == 0) {
+      if (reward_seq) reward_seq[t * n + e] = d ? 0.0f : -1.0f;
+      if (done_seq) done_seq[t * n + e] = d;
+    }
   }
+  if (!valid) return;
+  next[j * n + e] = th;
+  next[(K + j) * n + e] = om;
 }
 
-using StepFn = void (*)(const float*, const void*, int, uint32_t, int64_t, int64_t, float*, float*,
+using StepFn = void (*)(const float*, const void*, int, uint32_t, int64_t, int64_t, int64_t, float*, float*,
                         uint8_t*);
 
 // Per-translation-unit pickers: nullptr when the unit does not build this K.

@@ -32,3 +32,11 @@ class Hopper(_rl.StepBody):
         state = _rl.as_state(state, self.rows)
         stand = self._stand.on(state.device)
         return self._launch(_rl.lib().hopper_step, (int(self.branchy),), state, action, tail=(stand.data_ptr(),))
+
+    def step_many(self, state, actions, rewards=True, dones=True):
+        """T steps in one launch for actions (T, N): equal bit for bit to T `step` calls (the same
+        seeds are drawn). Returns (final_state, rewards (T, N) or None, dones (T, N) or None)."""
+        state = _rl.as_state(state, self.rows)
+        stand = self._stand.on(state.device)
+        return self._launch_many(_rl.lib().hopper_step_many, (int(self.branchy),), state, actions,
+                                 tail=(stand.data_ptr(),), rewards=rewards, dones=dones)

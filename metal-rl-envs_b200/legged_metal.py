@@ -80,17 +80,36 @@ class Legged(_rl.StepBody):
     def reset(self, n):
         return _rl.reset_uniform(self.rows, n, RESET_BOUND, center=self._stand.host)
 
+    @staticmethod
+    def _assist(assist):
+        """(value, device tensor or None) of the torso-assist stiffness argument."""
+        if isinstance(assist, torch.Tensor) and assist.device.type == "cuda":
+            return 0.0, assist.reshape(-1)[:1].float().contiguous()
+        return (0.0 if assist is None else _rl.float_scalar(assist)), None
+
     def step(self, state, action, assist=None, impulses=False):
         """(next_state, reward, done), and with impulses=True a fourth output: the (2c, n)
         contact impulses of the step, row 2k the tangential and row 2k + 1 the normal impulse
         of foot k, each summed over the four substeps (the lt, ln of legged_np.py:89-96)."""
         state = _rl.as_state(state, self.rows)
         stand = self._stand.on(state.device)
-        if isinstance(assist, torch.Tensor) and assist.device.type == "cuda":
-            a_val, a_ptr = 0.0, assist.reshape(-1)[:1].float().contiguous()
-        else:
-            a_val, a_ptr = (0.0 if assist is None else _rl.float_scalar(assist)), None
+        a_val, a_ptr = self._assist(assist)
         imp = torch.empty((2 * self.c, state.shape[1]), dtype=torch.float32, device=state.device) if impulses else None
         out = self._launch(_rl.lib().legged_step, (self.c, self.iters), state, action,
                            tail=(stand.data_ptr(), a_val, _rl.ptr(a_ptr)), outs=(_rl.ptr(imp),))
         return out + (imp,) if impulses else out
+
+    def step_many(self, state, actions, assist=None, impulses=False, rewards=True, dones=True):
+        """T steps in one launch for actions (T, N): equal bit for bit to T `step` calls (the same
+        seeds are drawn). Returns (final_state, rewards (T, N) or None, dones (T, N) or None), and
+        with impulses=True a fourth output (T, 2c, N): each step's impulses as `step` returns them."""
+        state = _rl.as_state(state, self.rows)
+        stand = self._stand.on(state.device)
+        a_val, a_ptr = self._assist(assist)
+        steps = len(actions)
+        imp = (torch.empty((steps, 2 * self.c, state.shape[1]), dtype=torch.float32, device=state.device),) \
+            if impulses else ()
+        out = self._launch_many(_rl.lib().legged_step_many, (self.c, self.iters), state, actions,
+                                tail=(stand.data_ptr(), a_val, _rl.ptr(a_ptr)), rewards=rewards, dones=dones,
+                                extra=imp or (None,))
+        return out if impulses else out[:3]

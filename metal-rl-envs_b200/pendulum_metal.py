@@ -33,3 +33,9 @@ class Pendulum(_rl.StepBody):
 
     def step(self, state, action):
         return self._launch(_rl.lib().pendulum_mm_step, (self.k, int(self.pairwise_trig)), state, action)
+
+    def step_many(self, state, actions, rewards=True, dones=True):
+        """T steps in one launch for actions (T, N): equal bit for bit to T `step` calls (the same
+        seeds are drawn). Returns (final_state, rewards (T, N) or None, dones (T, N) or None)."""
+        return self._launch_many(_rl.lib().pendulum_mm_step_many, (self.k, int(self.pairwise_trig)), state, actions,
+                                 rewards=rewards, dones=dones)

@@ -25,3 +25,9 @@ class Pendulum(_rl.StepBody):
 
     def step(self, state, action):
         return self._launch(_rl.lib().pendulum_coop_step, (self.k,), state, action)
+
+    def step_many(self, state, actions, rewards=True, dones=True):
+        """T steps in one launch for actions (T, N): equal bit for bit to T `step` calls (the same
+        seeds are drawn). Returns (final_state, rewards (T, N) or None, dones (T, N) or None)."""
+        return self._launch_many(_rl.lib().pendulum_coop_step_many, (self.k,), state, actions, rewards=rewards,
+                                 dones=dones)

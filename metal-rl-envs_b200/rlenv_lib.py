@@ -48,6 +48,16 @@ _SIGNATURES = {
     "rlenv_acrobot_rollout": [c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_void_p, c_void_p],
     "rlenv_legged_rollout": [c_int, c_int, c_int, c_int, c_float, c_float, c_float, c_float, c_void_p, c_void_p,
                              c_int64, c_int64, c_void_p, c_void_p, c_void_p],
+    "rlenv_pendulum_mm_step_many": [c_int, c_int, c_void_p, c_void_p, c_int, c_uint32, c_int64, c_int64, c_int64,
+                                    c_void_p, c_void_p, c_void_p, c_void_p],
+    "rlenv_pendulum_coop_step_many": [c_int, c_void_p, c_void_p, c_int, c_uint32, c_int64, c_int64, c_int64,
+                                      c_void_p, c_void_p, c_void_p, c_void_p],
+    "rlenv_pendulum_aba_step_many": [c_int, c_void_p, c_void_p, c_int, c_uint32, c_int64, c_int64, c_int64,
+                                     c_void_p, c_void_p, c_void_p, c_void_p],
+    "rlenv_legged_step_many": [c_int, c_int, c_void_p, c_void_p, c_int, c_uint32, c_void_p, c_float, c_void_p,
+                               c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
+    "rlenv_hopper_step_many": [c_int, c_void_p, c_void_p, c_int, c_uint32, c_void_p, c_int64, c_int64, c_int64,
+                               c_void_p, c_void_p, c_void_p, c_void_p],
     "rlenv_es_noise": [c_void_p, c_int64, c_int64, c_uint64, c_uint64, c_int64, c_void_p],
     "rlenv_es_perturb": [c_void_p, c_int64, c_float, c_uint64, c_uint64, c_int64, c_int64, c_int64, c_void_p, c_void_p],
     "rlenv_es_centered_ranks": [c_void_p, c_int64, c_void_p, c_void_p],
@@ -251,6 +261,32 @@ class StepBody:
     def _next_seed(self):
         self.calls += 1
         return self.calls & 0xFFFFFFFF
+
+    def _next_seeds(self, steps):
+        """The first of `steps` consecutive per-call seeds, as `steps` single calls would draw them."""
+        first = (self.calls + 1) & 0xFFFFFFFF
+        self.calls += steps
+        return first
+
+    def _launch_many(self, entry, head, state, actions, tail=(), rewards=True, dones=True, extra=()):
+        """entry(*head, state, actions, dtype, seed0, *tail, steps, n, index_offset, state_out,
+        reward_seq, done_seq, *extra, stream) for actions (T, N): T steps in one launch, equal to T
+        `step` calls. `extra` are further output tensors passed after done_seq. Returns
+        (final_state, rewards (T, N) or None, dones (T, N) or None, *extra)."""
+        state = as_state(state, self.rows)
+        n, dev = state.shape[1], state.device
+        if not isinstance(actions, torch.Tensor):
+            actions = torch.as_tensor(np.asarray(actions))
+        if actions.dim() != 2 or actions.shape[1] != n:
+            raise ValueError(f"actions must have shape (T, {n}); got {tuple(actions.shape)}")
+        steps = actions.shape[0]
+        actions, dt = as_actions(actions, steps * n, dev, "actions")
+        final = torch.empty_like(state)
+        rseq = torch.empty((steps, n), dtype=torch.float32, device=dev) if rewards else None
+        dseq = torch.empty((steps, n), dtype=torch.bool, device=dev) if dones else None
+        check(entry(*head, state.data_ptr(), actions.data_ptr(), dt, self._next_seeds(steps), *tail, steps, n, 0,
+                    final.data_ptr(), ptr(rseq), ptr(dseq), *(ptr(x) for x in extra), stream_ptr(dev)))
+        return (final, rseq, dseq, *extra)
 
     def _launch(self, entry, head, state, action, tail=(), outs=()):
         """entry(*head, state, action, dtype, seed, *tail, n, index_offset, next, reward, done,

@@ -57,6 +57,12 @@ def test_arguments_rejected_before_launch(lib):
     assert lib.pendulum_aba_step(65, fake, fake, 0, 1, 4, 0, fake, fake, fake, None) == -2
     assert lib.legged_step(5, 8, fake, fake, 0, 1, fake, 0.0, None, 4, 0, fake, fake, fake, None, None) == -2
     assert lib.legged_step(2, 0, fake, fake, 0, 1, fake, 0.0, None, 4, 0, fake, fake, fake, None, None) == -1  # iters < 1
+    assert lib.pendulum_mm_step_many(17, 0, fake, fake, 0, 1, 5, 4, 0, fake, None, None, None) == -2
+    assert lib.pendulum_aba_step_many(8, fake, fake, 0, 1, -1, 4, 0, fake, None, None, None) == -1     # steps < 0
+    assert lib.pendulum_coop_step_many(4, fake, None, 0, 1, 5, 4, 0, fake, None, None, None) == -1     # no actions
+    assert lib.pendulum_aba_step_many(8, None, None, 0, 1, 0, 0, 0, None, None, None, None) == 0       # empty batch
+    assert lib.legged_step_many(2, 8, fake, fake, 9, 1, fake, 0.0, None, 3, 4, 0, fake, None, None, None, None) == -1
+    assert lib.hopper_step_many(1, fake, fake, 0, 1, fake, 3, -4, 0, fake, None, None, None) == -1     # n < 0
     assert lib.cartpole_rollout(fake, fake, 0, 4, 3, 10, fake, None) == -2                 # hidden 3 not built
     assert lib.legged_rollout(2, 16, 10, 8, 1.0, 0.0, 0.0, 0.0, fake, fake, 0, -1, fake, fake, None) == -1
     assert lib.es_centered_ranks(fake, 1, fake, None) == -1

@@ -247,3 +247,74 @@ def test_legged_impulses_match_oracle(cuda, c):
     record(f"legged_c{c}_impulses", max_abs=float(err.max()), frac_out_of_tol=float(bad))
     assert bad <= 0.002, (float(err.max()), bad)
     assert (got[1::2] >= 0).all()
+
+
+# ---- T steps per launch ----------------------------------------------------------------------
+
+def _bodies():
+    import hopper_metal
+    import legged_metal
+    import pendulum_aba_metal
+    import pendulum_metal
+    import pendulum_metal_coop
+
+    return {
+        "mm_k4": (pendulum_metal.Pendulum(4), 3),
+        "mm_pairwise_k8": (pendulum_metal.Pendulum(8, pairwise_trig=True), 3),
+        "mm_k16": (pendulum_metal.Pendulum(16), 3),
+        "coop_k4": (pendulum_metal_coop.Pendulum(4), 3),
+        "coop_k16": (pendulum_metal_coop.Pendulum(16), 3),
+        "aba_k4": (pendulum_aba_metal.Pendulum(4), 3),
+        "aba_k24": (pendulum_aba_metal.Pendulum(24), 3),
+        "hopper": (hopper_metal.Hopper(), 3),
+        "hopper_branchy": (hopper_metal.Hopper(branchy=True), 3),
+        "legged2": (legged_metal.Legged(2), 9),
+        "legged4": (legged_metal.Legged(4, 4), 81),
+    }
+
+
+@pytest.mark.parametrize("name", ["mm_k4", "mm_pairwise_k8", "mm_k16", "coop_k4", "coop_k16", "aba_k4", "aba_k24",
+                                  "hopper", "hopper_branchy", "legged2", "legged4"])
+def test_step_many_equals_chained_steps(cuda, name):
+    """T steps in one launch are bit-identical to T single-step launches with the same seeds:
+    states, rewards and done flags, across resets (started near the termination boundary)."""
+    body, n_act = _bodies()[name]
+    n, T = 1000, 30
+    state0 = body.reset(n)
+    # half the environments start past their termination test, so the window includes resets:
+    # a chain standing upright (the pendulum's goal), a torso tilted past 1 rad
+    if name.startswith(("mm", "coop", "aba")):
+        state0[: state0.shape[0] // 2, : n // 2] = np.pi
+    else:
+        state0[2, : n // 2] = 1.5
+    gen = torch.Generator(device=cuda).manual_seed(3)
+    acts = torch.randint(0, n_act, (T, n), device=cuda, generator=gen).to(torch.int32)
+    body.reseed(500)
+    s, rews, dones = state0, [], []
+    for t in range(T):
+        s, r, d = body.step(s, acts[t])
+        rews.append(r)
+        dones.append(d)
+    body.reseed(500)
+    fin, rseq, dseq = body.step_many(state0, acts)[:3]
+    assert torch.equal(fin, s), name
+    assert torch.equal(rseq, torch.stack(rews)) and torch.equal(dseq, torch.stack(dones)), name
+    assert body.calls == 500 + T
+    assert int(dseq.sum()) > 0, "the window should include resets"
+
+
+def test_legged_step_many_impulses_equal_single_steps(cuda):
+    import legged_metal
+
+    body = legged_metal.Legged(4)
+    n, T = 512, 10
+    state0 = body.reset(n)
+    acts = torch.randint(0, 81, (T, n), device=cuda, generator=torch.Generator(device=cuda).manual_seed(4))
+    body.reseed(7)
+    s, imps = state0, []
+    for t in range(T):
+        s, _, _, imp = body.step(s, acts[t], impulses=True)
+        imps.append(imp)
+    body.reseed(7)
+    fin, _, _, imp_seq = body.step_many(state0, acts, impulses=True)
+    assert torch.equal(fin, s) and torch.equal(imp_seq, torch.stack(imps))
