@@ -318,3 +318,91 @@ def test_legged_step_many_impulses_equal_single_steps(cuda):
     body.reseed(7)
     fin, _, _, imp_seq = body.step_many(state0, acts, impulses=True)
     assert torch.equal(fin, s) and torch.equal(imp_seq, torch.stack(imps))
+
+
+def _abi_launchers(name, stand):
+    """(single-step launcher, T-step launcher, rows, n_actions) calling the C ABI with an index
+    offset: launch(state, action, seed, n, off) -> (next, reward, done)."""
+    import rlenv_lib as rl
+
+    lib = rl.lib()
+    sp = rl.stream_ptr()
+    kind, arg = name.split("_")[0], int(name.split("_")[-1][1:]) if name[-1].isdigit() else 0
+
+    def outs(rows, n, steps=None):
+        shape = (n,) if steps is None else (steps, n)
+        return (torch.empty((rows, n), device="cuda"), torch.empty(shape, device="cuda"),
+                torch.empty(shape, dtype=torch.bool, device="cuda"))
+
+    if kind in ("mm", "coop", "aba"):
+        k, rows, n_act = arg, 2 * arg, 3
+        one = {"mm": lambda *a: lib.pendulum_mm_step(k, 0, *a), "coop": lambda *a: lib.pendulum_coop_step(k, *a),
+               "aba": lambda *a: lib.pendulum_aba_step(k, *a)}[kind]
+        many = {"mm": lambda *a: lib.pendulum_mm_step_many(k, 0, *a),
+                "coop": lambda *a: lib.pendulum_coop_step_many(k, *a),
+                "aba": lambda *a: lib.pendulum_aba_step_many(k, *a)}[kind]
+        tail = ()
+    else:
+        c = arg
+        rows, n_act = 2 * (3 + c), 3 ** c
+        one = lambda s, a, dt, seed, n, off, *o: lib.legged_step(c, 8, s, a, dt, seed, stand.data_ptr(), 0.0, None, n,  # noqa: E731
+                                                                off, *o, None, sp)
+        many = lambda s, a, dt, seed, T, n, off, *o: lib.legged_step_many(c, 8, s, a, dt, seed, stand.data_ptr(),  # noqa: E731
+                                                                          0.0, None, T, n, off, *o, None, sp)
+
+    def launch_one(state, action, seed, off):
+        n = state.shape[1]
+        nxt, r, d = outs(rows, n)
+        if kind == "legged":
+            rl.check(one(state.data_ptr(), action.data_ptr(), rl.I32, seed, n, off, nxt.data_ptr(), r.data_ptr(),
+                         d.data_ptr()))
+        else:
+            rl.check(one(state.data_ptr(), action.data_ptr(), rl.I32, seed, n, off, nxt.data_ptr(), r.data_ptr(),
+                         d.data_ptr(), sp))
+        return nxt, r, d
+
+    def launch_many(state, actions, seed, off):
+        T, n = actions.shape
+        nxt, r, d = outs(rows, n, T)
+        if kind == "legged":
+            rl.check(many(state.data_ptr(), actions.data_ptr(), rl.I32, seed, T, n, off, nxt.data_ptr(), r.data_ptr(),
+                          d.data_ptr()))
+        else:
+            rl.check(many(state.data_ptr(), actions.data_ptr(), rl.I32, seed, T, n, off, nxt.data_ptr(), r.data_ptr(),
+                          d.data_ptr(), sp))
+        return nxt, r, d
+
+    return launch_one, launch_many, rows, n_act
+
+
+@pytest.mark.parametrize("name", ["mm_k4", "mm_k12", "coop_k8", "aba_k5", "aba_k32", "legged_c1", "legged_c3"])
+def test_shards_at_index_offsets_equal_the_whole_batch(cuda, name):
+    """Two shards stepped with index_offset = their first global environment (ragged sizes)
+    reproduce the unsharded batch bit for bit, resets included: what bench.py --gpus N and a
+    sharded caller rely on."""
+    import legged_metal
+
+    c = int(name[-1]) if name.startswith("legged") else 1
+    stand = torch.from_numpy(legged_metal.stand_pose(c)).to(cuda)
+    one, many, rows, n_act = _abi_launchers(name, stand)
+    n, cut, T = 777, 301, 12
+    r = np.random.default_rng(len(name))
+    if name.startswith("legged"):
+        st = (legged_metal.stand_pose(c)[:, None] + r.uniform(-0.05, 0.05, (rows, n))).astype(np.float32)
+        st[2, ::3] = 1.5  # a third start past the tilt limit: resets in the first step
+    else:
+        st = r.uniform(-0.1, 0.1, (rows, n)).astype(np.float32)
+        st[: rows // 2, ::3] = np.pi  # a third start upright: resets in the first step
+    state = torch.from_numpy(st).to(cuda)
+    act = torch.from_numpy(r.integers(0, n_act, (T, n)).astype(np.int32)).to(cuda)
+    whole = one(state, act[0], 9, 0)
+    parts = [one(state[:, :cut].contiguous(), act[0, :cut].contiguous(), 9, 0),
+             one(state[:, cut:].contiguous(), act[0, cut:].contiguous(), 9, cut)]
+    assert bool(whole[2].any()), "the batch should reset somewhere"
+    for w, a, b in zip(whole, *parts):
+        assert torch.equal(w, torch.cat([a, b], dim=-1)), name
+    whole = many(state, act, 40, 0)
+    parts = [many(state[:, :cut].contiguous(), act[:, :cut].contiguous(), 40, 0),
+             many(state[:, cut:].contiguous(), act[:, cut:].contiguous(), 40, cut)]
+    for w, a, b in zip(whole, *parts):
+        assert torch.equal(w, torch.cat([a, b], dim=-1)), name
