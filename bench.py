@@ -67,6 +67,38 @@ WORKLOADS = {
 }
 
 
+# The reference's own published numbers (Apple M3 Pro through Metal/MLX, listed in the build's
+# baseline notes with their README.md / results/*.csv sources), keyed by the exact configuration
+# they were measured on: vs_baseline is reported only for a line whose configuration matches.
+PUBLISHED = {
+    ("acrobot_step", 262_144): (1.123e9, "Acrobot step kernel, N = 262,144, M3 Pro (README.md:403)"),
+    ("cartpole_step", 131_072): (1.133e9, "CartPole step kernel, N = 131,072, M3 Pro (README.md:307)"),
+    ("cartpole_step", 1_048_576): (1.249e9, "CartPole step kernel, N = 1,048,576, M3 Pro (README.md:310)"),
+    ("pendulum_mm", 256, 4): (4.44e6, "pendulum mass matrix K = 4, N = 256, M3 Pro (results/pendulum.csv)"),
+    ("pendulum_mm", 65_536, 4): (298e6, "pendulum mass matrix K = 4, N = 65,536, M3 Pro (README.md:1127)"),
+    ("pendulum_mm", 256, 16): (495e3, "pendulum mass matrix K = 16, N = 256, M3 Pro (results/pendulum.csv)"),
+    ("pendulum_mm", 65_536, 16): (12.1e6, "pendulum mass matrix K = 16, N = 65,536, M3 Pro (README.md:1129)"),
+    ("pendulum_coop", 256, 16): (643e3, "pendulum cooperative K = 16, N = 256, M3 Pro (README.md:1215)"),
+    ("pendulum_coop", 65_536, 16): (4.33e6, "pendulum cooperative K = 16, N = 65,536, M3 Pro (README.md:1223)"),
+    ("pendulum_aba", 256, 4): (3.48e6, "articulated body K = 4, N = 256, M3 Pro (results/aba.csv)"),
+    ("pendulum_aba", 65_536, 4): (450e6, "articulated body K = 4, N = 65,536, M3 Pro (README.md:1295)"),
+    ("pendulum_aba", 256, 16): (2.40e6, "articulated body K = 16, N = 256, M3 Pro (results/aba.csv)"),
+    ("pendulum_aba", 65_536, 16): (68.2e6, "articulated body K = 16, N = 65,536, M3 Pro (README.md:1297)"),
+    ("pendulum_aba", 256, 64): (713e3, "articulated body K = 64, N = 256, M3 Pro (results/aba.csv)"),
+    ("pendulum_aba", 65_536, 64): (3.96e6, "articulated body K = 64, N = 65,536, M3 Pro (README.md:1301)"),
+    ("legged_step", 65_536, 2, 8): (94.6e6, "legged C = 2, 8 sweeps, N = 65,536, M3 Pro (README.md:1685)"),
+    ("legged_step", 65_536, 4, 4): (26.2e6, "legged C = 4, 4 sweeps, N = 65,536, M3 Pro (README.md:1609)"),
+    ("legged_step", 65_536, 4, 8): (24.3e6, "legged C = 4, 8 sweeps, N = 65,536, M3 Pro (README.md:1610)"),
+    ("legged_step", 65_536, 4, 16): (21.2e6, "legged C = 4, 16 sweeps, N = 65,536, M3 Pro (README.md:1611)"),
+    ("legged_step", 262_144, 1, 1): (617e6, "hopper (C = 1, one sweep), N = 262,144, M3 Pro (README.md:1552)"),
+}
+
+
+def published(*key):
+    """(value, source) of the reference's number for this exact configuration, or (None, None)."""
+    return PUBLISHED.get(tuple(key), (None, None))
+
+
 def parse():
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
@@ -438,7 +470,8 @@ def run_ours(args):
     line = {
         "metric": METRIC, "value": value, "unit": "env steps/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * secs_max / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "scaling": "weak", "vs_baseline": value / published("acrobot_step", n)[0] if published("acrobot_step", n)[0]
+        else None, "vs_baseline_source": published("acrobot_step", n)[1], "dtype": "f32",
         "data": "synthetic (seeded uniform states, uniform actions in {0,1,2})",
         "config": {"workload": WORKLOAD, "n_envs_per_gpu": n, "env_steps_per_step": T,
                    "kernel": "rlenv_acrobot_step_many (state in registers, per-step rewards and dones to HBM)",
@@ -693,12 +726,16 @@ def run_workload(args):
         hbm = {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
                "bytes_per_launch": bytes_launch / T, "peak_kind": "measured (MEASURED_PEAKS.json)"}
         roof = {**hbm, "fp32": fp32} if hbm_bound else {**fp32, "hbm": hbm}
+        key = (args.workload, n) + ((args.k,) if args.workload.startswith("pendulum") else ()) + \
+            ((args.c, args.iters) if args.workload == "legged_step" else ())
+        pub, pub_src = published(*key)
         if extra.get("impulses"):
             # the last timed step's normal impulses: the share of feet in active contact
             extra["contact_active_fraction"] = float((imp[-1, 1::2] > 0).float().mean().item())
         line = {"metric": metric, "value": world * units * args.steps / secs, "unit": unit, "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * per, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "scaling": "weak", "vs_baseline": (world * units * args.steps / secs / pub) if pub else None,
+                "vs_baseline_source": pub_src, "dtype": "f32", "data": "synthetic",
                 "config": {"workload": args.workload, "config": desc, "n_envs_per_gpu": n, "env_steps_per_step": T, **extra},
                 "roofline": roof, "clocks": clocks}
         if world == 1 and not args.no_cpu_baseline:
