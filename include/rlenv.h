@@ -10,9 +10,12 @@
  *    environment i is state[r * N + i]. Every pointer is a device pointer
  *    unless its comment says otherwise.
  *  - The caller allocates every buffer. The library never allocates or frees
- *    memory and holds no state between calls.
+ *    memory and holds no state between calls; the one exception is
+ *    rlenv_es_centered_ranks_static, whose scratch is a fixed array of the
+ *    library (its address cached per device).
  *  - Work is enqueued asynchronously on `stream` (a cudaStream_t; NULL is the
- *    legacy default stream). Calls are reentrant.
+ *    legacy default stream). Calls are reentrant, except that overlapping calls of
+ *    rlenv_es_centered_ranks_static on one device share its scratch.
  *  - Inputs are never written. Outputs must not alias inputs except where a
  *    comment says so.
  *  - The return value is 0 on success, a negative RLENV_E* code for an argument

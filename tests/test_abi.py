@@ -87,3 +87,14 @@ def test_product_has_no_cpu_path():
     if not torch.cuda.is_available():
         with pytest.raises(RuntimeError):
             rlenv_lib.device()
+
+
+def test_a_c_host_compiles_links_and_calls_the_library(lib, tmp_path):
+    """include/rlenv.h is plain C: a C99 program includes it, links librlenv.so and calls it."""
+    exe = tmp_path / "c_abi_check"
+    build = subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-Werror", f"-I{ROOT / 'include'}",
+                            str(ROOT / "tests" / "c_abi_check.c"), f"-L{PKG}", "-lrlenv", f"-Wl,-rpath,{PKG}",
+                            "-o", str(exe)], capture_output=True, text=True)
+    assert build.returncode == 0, build.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert run.returncode == 0 and run.stdout.strip().endswith("ok"), run.stdout + run.stderr
