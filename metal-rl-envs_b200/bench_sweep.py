@@ -67,9 +67,9 @@ def kernel_rollout(body, n_actions, every):
 
     def run(n, iters):
         state = body.reset(n)
-        for i in range(1, iters + 1):
+        for done_steps in range(iters):
             state, _, _ = body.step(state, torch.randint(0, n_actions, (n,), device=dev, dtype=torch.int32))
-            if i % every == 0:
+            if (done_steps + 1) % every == 0:
                 _sync()
         _sync()
         return state
@@ -78,8 +78,8 @@ def kernel_rollout(body, n_actions, every):
 
 
 def chain_rollout(module, n_actions):
-    """The same loop as one launch of the T-step kernel: all T x N actions drawn on the device,
-    then every step, reward and done flag of the chain written by one kernel."""
+    """The same loop as one launch of the T-step kernel (`step_many`): all T x N actions drawn on
+    the device, then every step, reward and done flag of the chain written by one kernel."""
     dev = _rl.device()
 
     def run(n, iters):
@@ -112,6 +112,7 @@ def configs(body, eval_every, k=None, c=None, sweeps=None):
             "cuda kernel, sync every step": kernel_rollout(sel, 3, 1),
             f"cuda kernel, sync every {eval_every}": kernel_rollout(sel, 3, eval_every),
             f"cuda branchy kernel, sync every {eval_every}": kernel_rollout(br, 3, eval_every),
+            "cuda T-step kernel, one launch": chain_rollout(sel, 3),
         }
     if body == "pendulum":
         import pendulum_metal
@@ -123,6 +124,8 @@ def configs(body, eval_every, k=None, c=None, sweeps=None):
             f"cuda kernel, sync every {eval_every}": kernel_rollout(mm, 3, eval_every),
             f"cuda cooperative kernel, sync every {eval_every}": kernel_rollout(co, 3, eval_every),
             f"cuda kernel (pairwise trig), sync every {eval_every}": kernel_rollout(v9, 3, eval_every),
+            "cuda T-step kernel, one launch": chain_rollout(mm, 3),
+            "cuda cooperative T-step kernel, one launch": chain_rollout(co, 3),
         }
     if body == "aba":
         import pendulum_aba_metal
@@ -132,6 +135,7 @@ def configs(body, eval_every, k=None, c=None, sweeps=None):
         cfg = {
             "cuda articulated-body kernel, sync every step": kernel_rollout(ab, 3, 1),
             f"cuda articulated-body kernel, sync every {eval_every}": kernel_rollout(ab, 3, eval_every),
+            "cuda articulated-body T-step kernel, one launch": chain_rollout(ab, 3),
         }
         if k <= 16:
             cfg[f"cuda mass-matrix kernel, sync every {eval_every}"] = kernel_rollout(pendulum_metal.Pendulum(k), 3, eval_every)
@@ -143,20 +147,23 @@ def configs(body, eval_every, k=None, c=None, sweeps=None):
         return {
             "cuda kernel, sync every step": kernel_rollout(lg, 3**c, 1),
             f"cuda kernel, sync every {eval_every}": kernel_rollout(lg, 3**c, eval_every),
+            "cuda T-step kernel, one launch": chain_rollout(lg, 3**c),
         }
     raise ValueError(f"unknown body {body!r}; choose from {sorted(STEP_FILES)}")
 
 
 def steps_per_sec(rollout, n, iters, warmup, repeats):
-    """bench.py:74-82: warm-up untimed, median of `repeats` wall-clock runs."""
+    """The reference's timing rule (bench.py:74-82): an untimed warm-up run, then the median
+    wall-clock time of `repeats` runs of `iters` steps over N environments."""
     rollout(n, warmup)
-    seconds = []
-    for _ in range(repeats):
+
+    def timed_run():
         _sync()
-        start = time.perf_counter()
+        t0 = time.perf_counter()
         rollout(n, iters)
-        seconds.append(time.perf_counter() - start)
-    return n * iters / statistics.median(seconds)
+        return time.perf_counter() - t0
+
+    return n * iters / statistics.median(timed_run() for _ in range(repeats))
 
 
 def sweep(cfg, max_exp, iters, warmup, repeats, key=None, log=print):
@@ -182,19 +189,20 @@ def write_steps_csv(rows, path, iters, warmup, repeats, sweeps=None):
     else:
         cols = STEPS_COLUMNS
     fixed = {"iters": iters, "warmup": warmup, "repeats": repeats, "sweeps": sweeps}
-    with open(path, "w", newline="") as f:
-        w = csv.writer(f)
-        w.writerow(cols)
-        for r in rows:
-            w.writerow([r[c] if c in r else fixed[c] for c in cols])
+    with open(path, "w", newline="") as out:
+        table = csv.writer(out)
+        table.writerow(cols)
+        table.writerows([r.get(c, fixed.get(c)) for c in cols] for r in rows)
 
 
 def write_dict_csv(rows, path):
-    """bench_ppo.py:37-41: a DictWriter over the first row's keys."""
-    with open(path, "w", newline="") as f:
-        w = csv.DictWriter(f, fieldnames=list(rows[0]))
-        w.writeheader()
-        w.writerows(rows)
+    """The reference's ES writer (bench_ppo.py:37-41): a header of the first row's keys in
+    their order, then one line per row."""
+    columns = list(rows[0].keys())
+    with open(path, "w", newline="") as out:
+        writer = csv.writer(out)
+        writer.writerow(columns)
+        writer.writerows([row[c] for c in columns] for row in rows)
 
 
 def es_sweep(task, ns, seeds, lrs, sigma, time_budget, assist=0.0, start_velocity=0.0, anneal=300,
@@ -209,13 +217,14 @@ def es_sweep(task, ns, seeds, lrs, sigma, time_budget, assist=0.0, start_velocit
                 extra = {} if max_generations is None else {"max_generations": max_generations}
                 cfg = es.Config(task=task, pop=pop, lr=lr, sigma=sigma, time_budget=time_budget, assist_k0=assist,
                                 start_velocity=start_velocity, anneal_gens=anneal, **extra)
-                r = es.train(cfg, backend, seed)
-                name = backend if series == "backend" else f"lr {lr}"
-                rows.append({"backend": backend, "lr": lr, "series": name, "n": pop, "seed": seed, **vars(r),
-                             "steps_per_sec": r.env_steps / r.train_seconds})
-                status = f"solved in {r.train_seconds:6.1f}s" if r.solved else f"NOT solved, {r.train_seconds:6.1f}s"
-                log(f"{backend:6s} lr={lr:<5g} P={pop:>7d} seed={seed}  {status}  {r.generations:>4d} gens  "
-                    f"{r.env_steps:>14,} env steps  {r.env_steps / r.train_seconds / 1e6:8.1f}M steps/s  score {r.score:5.1f}")
+                result = es.train(cfg, backend, seed)
+                rate = result.env_steps / result.train_seconds
+                rows.append({"backend": backend, "lr": lr, "series": backend if series == "backend" else f"lr {lr}",
+                             "n": pop, "seed": seed, **vars(result), "steps_per_sec": rate})
+                outcome = "solved" if result.solved else "not solved"
+                log(f"{backend} lr={lr:g} P={pop} seed={seed}: {outcome} after {result.generations} generations, "
+                    f"{result.train_seconds:.1f} s, {result.env_steps:,} env steps ({rate / 1e6:.1f} M/s), "
+                    f"score {result.score:.1f}")
     return rows
 
 

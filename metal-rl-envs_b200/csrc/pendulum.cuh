@@ -154,16 +154,19 @@ __device__ __noinline__ void aba_accel_loops(const float* th, const float* om, f
     vx[i] = c * px + s * xy;
     vy[i] = -s * px + c * xy;
   }
-  float cA00 = 0.0f, cA01 = 0.0f, cA02 = 0.0f, cA11 = 0.0f, cA12 = 0.0f, cA22 = 0.0f;
-  float cp0 = 0.0f, cp1 = 0.0f, cp2 = 0.0f;
+  // Articulated inertia (symmetric 3x3, upper half) and bias force that the child link hands to
+  // its parent in the inward pass; zero below the last link.
+  float carry_I00 = 0.0f, carry_I01 = 0.0f, carry_I02 = 0.0f;
+  float carry_I11 = 0.0f, carry_I12 = 0.0f, carry_I22 = 0.0f;
+  float carry_p0 = 0.0f, carry_p1 = 0.0f, carry_p2 = 0.0f;
 #pragma unroll 8
   for (int i = K - 1; i >= 1; --i) {
     const float w = vw[i], x = vx[i], y = vy[i];
     const float qd = om[i] - om[i - 1];
     const float fy = w + y;
-    const float p0 = (x * fy - y * x) + cp0, p1 = (-w * fy) + cp1, p2 = (w * x) + cp2;
-    const float a00 = 1.0f + cA00, a01 = cA01, a02 = 1.0f + cA02;
-    const float a11 = 1.0f + cA11, a12 = cA12, a22 = 1.0f + cA22;
+    const float p0 = (x * fy - y * x) + carry_p0, p1 = (-w * fy) + carry_p1, p2 = (w * x) + carry_p2;
+    const float a00 = 1.0f + carry_I00, a01 = carry_I01, a02 = 1.0f + carry_I02;
+    const float a11 = 1.0f + carry_I11, a12 = carry_I12, a22 = 1.0f + carry_I22;
     U0[i] = a00;
     U1[i] = a01;
     U2[i] = a02;
@@ -181,22 +184,22 @@ __device__ __noinline__ void aba_accel_loops(const float* th, const float* om, f
     const float B00 = Ia00 + Ia01 * s + Ia02 * c, B01 = Ia01 * c - Ia02 * s, B02 = Ia01 * s + Ia02 * c;
     const float B10 = Ia01 + Ia11 * s + Ia12 * c, B11 = Ia11 * c - Ia12 * s, B12 = Ia11 * s + Ia12 * c;
     const float B20 = Ia02 + Ia12 * s + Ia22 * c, B21 = Ia12 * c - Ia22 * s, B22 = Ia12 * s + Ia22 * c;
-    cA00 = B00 + s * B10 + c * B20;
-    cA01 = B01 + s * B11 + c * B21;
-    cA02 = B02 + s * B12 + c * B22;
-    cA11 = c * B11 - s * B21;
-    cA12 = c * B12 - s * B22;
-    cA22 = s * B12 + c * B22;
-    cp0 = pa0 + s * pa1 + c * pa2;
-    cp1 = c * pa1 - s * pa2;
-    cp2 = s * pa1 + c * pa2;
+    carry_I00 = B00 + s * B10 + c * B20;
+    carry_I01 = B01 + s * B11 + c * B21;
+    carry_I02 = B02 + s * B12 + c * B22;
+    carry_I11 = c * B11 - s * B21;
+    carry_I12 = c * B12 - s * B22;
+    carry_I22 = s * B12 + c * B22;
+    carry_p0 = pa0 + s * pa1 + c * pa2;
+    carry_p1 = c * pa1 - s * pa2;
+    carry_p2 = s * pa1 + c * pa2;
   }
   {
     const float w = vw[0], x = vx[0], y = vy[0], fy = w + y;
-    U0[0] = 1.0f + cA00;
-    U1[0] = cA01;
-    U2[0] = 1.0f + cA02;
-    uu[0] = torque - ((x * fy - y * x) + cp0);
+    U0[0] = 1.0f + carry_I00;
+    U1[0] = carry_I01;
+    U2[0] = 1.0f + carry_I02;
+    uu[0] = torque - ((x * fy - y * x) + carry_p0);
   }
   float sn0, cs0;
   sincosf(th[0], &sn0, &cs0);
@@ -240,18 +243,21 @@ RLENV_D void aba_accel_unrolled(const float* th, const float* om, float torque, 
   });
   // inward: articulated inertia and bias force of the subtree, carried to the
   // parent as the child's contribution (cA, cp)
-  float cA00 = 0.0f, cA01 = 0.0f, cA02 = 0.0f, cA11 = 0.0f, cA12 = 0.0f, cA22 = 0.0f;
-  float cp0 = 0.0f, cp1 = 0.0f, cp2 = 0.0f;
+  // Articulated inertia (symmetric 3x3, upper half) and bias force that the child link hands to
+  // its parent in the inward pass; zero below the last link.
+  float carry_I00 = 0.0f, carry_I01 = 0.0f, carry_I02 = 0.0f;
+  float carry_I11 = 0.0f, carry_I12 = 0.0f, carry_I22 = 0.0f;
+  float carry_p0 = 0.0f, carry_p1 = 0.0f, carry_p2 = 0.0f;
   for_links<1, K, false, true>([&](int i) {
     const float w = vw[i], x = vx[i], y = vy[i];
     const float qd = om[i] - om[i - 1];
     // own bias p = v x* (I v), I of a unit mass at (1, 0) = [[1,0,1],[0,1,0],[1,0,1]]
     const float fy = w + y;
-    const float p0 = (x * fy - y * x) + cp0;
-    const float p1 = (-w * fy) + cp1;
-    const float p2 = (w * x) + cp2;
-    const float a00 = 1.0f + cA00, a01 = cA01, a02 = 1.0f + cA02;
-    const float a11 = 1.0f + cA11, a12 = cA12, a22 = 1.0f + cA22;
+    const float p0 = (x * fy - y * x) + carry_p0;
+    const float p1 = (-w * fy) + carry_p1;
+    const float p2 = (w * x) + carry_p2;
+    const float a00 = 1.0f + carry_I00, a01 = carry_I01, a02 = 1.0f + carry_I02;
+    const float a11 = 1.0f + carry_I11, a12 = carry_I12, a22 = 1.0f + carry_I22;
     U0[i] = a00;
     U1[i] = a01;
     U2[i] = a02;
@@ -270,23 +276,23 @@ RLENV_D void aba_accel_unrolled(const float* th, const float* om, float torque, 
     const float B00 = Ia00 + Ia01 * s + Ia02 * c, B01 = Ia01 * c - Ia02 * s, B02 = Ia01 * s + Ia02 * c;
     const float B10 = Ia01 + Ia11 * s + Ia12 * c, B11 = Ia11 * c - Ia12 * s, B12 = Ia11 * s + Ia12 * c;
     const float B20 = Ia02 + Ia12 * s + Ia22 * c, B21 = Ia12 * c - Ia22 * s, B22 = Ia12 * s + Ia22 * c;
-    cA00 = B00 + s * B10 + c * B20;
-    cA01 = B01 + s * B11 + c * B21;
-    cA02 = B02 + s * B12 + c * B22;
-    cA11 = c * B11 - s * B21;
-    cA12 = c * B12 - s * B22;
-    cA22 = s * B12 + c * B22;
-    cp0 = pa0 + s * pa1 + c * pa2;
-    cp1 = c * pa1 - s * pa2;
-    cp2 = s * pa1 + c * pa2;
+    carry_I00 = B00 + s * B10 + c * B20;
+    carry_I01 = B01 + s * B11 + c * B21;
+    carry_I02 = B02 + s * B12 + c * B22;
+    carry_I11 = c * B11 - s * B21;
+    carry_I12 = c * B12 - s * B22;
+    carry_I22 = s * B12 + c * B22;
+    carry_p0 = pa0 + s * pa1 + c * pa2;
+    carry_p1 = c * pa1 - s * pa2;
+    carry_p2 = s * pa1 + c * pa2;
   });
   {  // root link: its inertia and bias with the whole chain's contribution
     const float w = vw[0], x = vx[0], y = vy[0];
     const float fy = w + y;
-    U0[0] = 1.0f + cA00;
-    U1[0] = cA01;
-    U2[0] = 1.0f + cA02;
-    uu[0] = torque - ((x * fy - y * x) + cp0);
+    U0[0] = 1.0f + carry_I00;
+    U1[0] = carry_I01;
+    U2[0] = 1.0f + carry_I02;
+    uu[0] = torque - ((x * fy - y * x) + carry_p0);
   }
   // outward: accelerations, the base accelerating at -G; the absolute angular
   // accelerations are the running sum of the joint accelerations

@@ -158,7 +158,7 @@ legged_rollout_kernel(const float* __restrict__ state, const float* __restrict__
     q[i] = __ldg(state + i * p + m);
     v[i] = __ldg(state + (nq + i) * p + m);
   }
-  float total = 0.0f, taken = 0.0f;
+  float ret = 0.0f, alive_steps = 0.0f;  // return and steps survived, fall step included
   for (int step = 0; step < horizon; ++step) {
     // observation without x: (y, phi, psi.., x_dot, y_dot, phi_dot, psi_dot..)
     float hdn[H];
@@ -187,15 +187,15 @@ legged_rollout_kernel(const float* __restrict__ state, const float* __restrict__
 #pragma unroll 1
     for (int sub = 0; sub < lg::SUBSTEPS; ++sub) legged_substep<C, false>(q, v, tq, assist, iters);
     if (legged_terminated<C>(q)) {
-      taken += 1.0f;
-      total -= fall_penalty;
+      alive_steps += 1.0f;
+      ret -= fall_penalty;
       break;
     }
-    total += (q[1] >= gate ? v[0] : 0.0f) + alive_bonus;
-    taken += 1.0f;
+    ret += (q[1] >= gate ? v[0] : 0.0f) + alive_bonus;
+    alive_steps += 1.0f;
   }
-  fitness[m] = total;
-  steps[m] = taken;
+  fitness[m] = ret;
+  steps[m] = alive_steps;
 }
 
 using ClassicRollout = void (*)(const float*, const float*, int64_t, int64_t, int, float*);

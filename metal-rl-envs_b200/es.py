@@ -48,19 +48,25 @@ import legged_rollout_metal
 import rlenv_lib as _rl
 
 
+# ---- tasks -------------------------------------------------------------------------------------
+
 @dataclass(frozen=True)
 class Task:
+    """A learning problem: its bodies, the policy's shape, how states become observations and
+    logits become actions, the fused rollout, and the shaping of the fitness. The field names
+    are es.py's (es.py:48-70), so code written against the reference reads them unchanged;
+    `np` is always None here (the numpy bodies are the tests' oracle)."""
     name: str
     obs_dim: int
-    n_out: int               # policy outputs
+    n_out: int
     hidden: int
-    solved_at: float         # threshold on the greedy mean policy's mean fitness
-    np: Any                  # the numpy environment: not part of this build (see oracle/ in the tests)
-    mlx: Any                 # environment with reset(n) on the device
-    metal: Any               # the CUDA step kernel: step(state, action), reseed(seed)
-    obs: Callable            # (xp, state) -> (P, obs_dim)
-    action: Callable         # (xp, logits (P, n_out)) -> action index (P,)
-    rollout: Callable        # (state, theta_pop, hidden, horizon[, assist]) -> (fitness, steps)
+    solved_at: float
+    np: Any
+    mlx: Any
+    metal: Any
+    obs: Callable
+    action: Callable
+    rollout: Callable
     alive_bonus: float = 1.0
     fall_penalty: float = 0.0
     eval_bonus: float = 1.0
@@ -69,45 +75,51 @@ class Task:
     assistable: bool = False
 
 
-def _argmax(xp, logits):
-    return torch.argmax(logits, dim=-1)
+def _greedy(xp, logits):
+    """The index of the largest logit (the first one on ties)."""
+    return logits.argmax(dim=-1)
 
 
-def _cartpole_obs(xp, state):
-    return state.T
+def _state_as_obs(xp, state):
+    """CartPole observes its state as it is: (N, 4)."""
+    return state.t()
 
 
-def _acrobot_obs(xp, state):
-    th1, th2, dth1, dth2 = state
-    return torch.stack([torch.cos(th1), torch.sin(th1), torch.cos(th2), torch.sin(th2), dth1, dth2], dim=1)
+def _acrobot_features(xp, state):
+    """cos t1, sin t1, cos t2, sin t2, then both angular velocities: (N, 6)."""
+    c, s = torch.cos(state[:2]), torch.sin(state[:2])
+    return torch.stack((c[0], s[0], c[1], s[1], state[2], state[3]), dim=1)
 
 
-def _legged_obs(xp, state):
-    """Everything but x, so the policy is translation-invariant."""
-    return state[1:].T
+def _obs_without_x(xp, state):
+    """A legged body observes every state row except its horizontal position, so the policy
+    cannot depend on where the body is."""
+    return state[1:].t()
 
 
-def _legged_action(c):
+def _per_leg_action(c):
+    """Three logits per leg, one argmax per leg, combined as the base-3 digits of one action."""
+    place = 3 ** torch.arange(c, dtype=torch.int32)
+
     def action(xp, logits):
-        out = None
-        for k in range(c):
-            a_k = torch.argmax(logits[:, 3 * k:3 * k + 3], dim=-1).to(torch.int32) * 3**k
-            out = a_k if out is None else out + a_k
-        return out
+        digits = logits.reshape(logits.shape[0], c, 3).argmax(dim=-1).to(torch.int32)
+        return (digits * place.to(digits.device)).sum(dim=1, dtype=torch.int32)
     return action
 
 
-def _steps_fitness(kernel, sign):
-    """Steps survived (the terminating step excluded) to (fitness, steps taken): fitness has the
-    task's sign; steps taken counts the terminating step, capped at the horizon (es.py:96-103)."""
+def _survival(rollout_steps, sign):
+    """Adapt a rollout that counts the steps an episode survived (its terminating step not
+    counted) to the (fitness, steps taken) pair: fitness is the count with the task's sign,
+    steps taken include the terminating step and stop at the horizon (es.py:96-103)."""
     def rollout(state, theta_pop, hidden, horizon):
-        steps = kernel(state, theta_pop, hidden, horizon)
-        return sign * steps, torch.clamp(steps + 1, max=horizon)
+        survived = rollout_steps(state, theta_pop, hidden, horizon)
+        return sign * survived, torch.clamp(survived + 1, max=horizon)
     return rollout
 
 
 class _LeggedEnv:
-    """Legged step kernel plus a device reset around the standing pose, shared per C."""
+    """The legged body with C legs as es.py's `mlx` and `metal` slots use it: reset around the
+    standing pose, step with the torso assist."""
 
     RESET_BOUND = legged_metal.RESET_BOUND
 
@@ -126,34 +138,50 @@ class _LeggedEnv:
         self.body.reseed(seed)
 
 
-def _legged_task(c, name, alive=1.0, fall=0.0, gate=0.0):
-    env = _LeggedEnv(c)
-    return Task(f"legged{c}{name}", 5 + 2 * c, 3 * c, 16, 100.0, None, env, env,
-                _legged_obs, _legged_action(c),
-                lambda state, theta, hidden, horizon, assist=0.0: legged_rollout_metal.rollout(
-                    state, theta, hidden, horizon, c, alive, fall, gate, assist),
-                alive, fall, 0.0, gate, 3 + c, True)
+def _classic_task(name, module, rollout_module, obs_dim, n_out, solved_at, observe, sign):
+    return Task(name, obs_dim, n_out, 32, solved_at, None, module, module, observe, _greedy,
+                _survival(rollout_module.rollout_steps, sign))
 
+
+def _legged_variant(name, c, alive, fall, gate):
+    """A legged task: training fitness is forward velocity (counted only while the torso is at
+    least `gate` high) plus `alive` per step, minus `fall` on the step that falls; the score
+    that decides "solved" is the distance walked before the first fall, 100 for every variant."""
+    env = _LeggedEnv(c)
+
+    def rollout(state, theta, hidden, horizon, assist=0.0):
+        return legged_rollout_metal.rollout(state, theta, hidden, horizon, c, alive, fall, gate, assist)
+
+    return Task(name, 5 + 2 * c, 3 * c, 16, 100.0, None, env, env, _obs_without_x, _per_leg_action(c), rollout,
+                alive_bonus=alive, fall_penalty=fall, eval_bonus=0.0, height_gate=gate, xdot_row=3 + c,
+                assistable=True)
+
+
+# name -> (legs, alive bonus, fall penalty, height gate): es.py's table of legged tasks
+_LEGGED_TASKS = {
+    "legged2": (2, 1.0, 0.0, 0.0),
+    "legged4": (4, 1.0, 0.0, 0.0),
+    "legged2_distance": (2, 0.0, 0.0, 0.0),
+    "legged4_distance": (4, 0.0, 0.0, 0.0),
+    "legged2_alive10": (2, 0.1, 0.0, 0.0),
+    "legged2_fall": (2, 0.0, 20.0, 0.0),
+    "legged2_alive10_fall": (2, 0.1, 20.0, 0.0),
+    "legged4_alive10": (4, 0.1, 0.0, 0.0),
+    "legged2_gated": (2, 0.0, 0.0, 0.85),
+}
 
 TASKS = {
-    "cartpole": Task("cartpole", 4, 2, 32, 475.0, None, cartpole_metal, cartpole_metal,
-                     _cartpole_obs, _argmax, _steps_fitness(cartpole_rollout_metal.rollout_steps, 1.0)),
-    "acrobot": Task("acrobot", 6, 3, 32, -100.0, None, acrobot_metal, acrobot_metal,
-                    _acrobot_obs, _argmax, _steps_fitness(acrobot_rollout_metal.rollout_steps, -1.0)),
-    "legged2": _legged_task(2, ""),
-    "legged4": _legged_task(4, ""),
-    "legged2_distance": _legged_task(2, "_distance", alive=0.0),
-    "legged4_distance": _legged_task(4, "_distance", alive=0.0),
-    "legged2_alive10": _legged_task(2, "_alive10", alive=0.1),
-    "legged2_fall": _legged_task(2, "_fall", alive=0.0, fall=20.0),
-    "legged2_alive10_fall": _legged_task(2, "_alive10_fall", alive=0.1, fall=20.0),
-    "legged4_alive10": _legged_task(4, "_alive10", alive=0.1),
-    "legged2_gated": _legged_task(2, "_gated", alive=0.0, gate=0.85),
+    "cartpole": _classic_task("cartpole", cartpole_metal, cartpole_rollout_metal, 4, 2, 475.0, _state_as_obs, 1.0),
+    "acrobot": _classic_task("acrobot", acrobot_metal, acrobot_rollout_metal, 6, 3, -100.0, _acrobot_features, -1.0),
+    **{name: _legged_variant(name, *spec) for name, spec in _LEGGED_TASKS.items()},
 }
 
 
 @dataclass
 class Config:
+    """Hyper-parameters of a run, with es.py's names and defaults. hidden and solved_at of None
+    take the task's; assist_k0 and start_velocity are the curricula's starting values, both
+    annealed to zero over anneal_gens generations."""
     task: str = "cartpole"
     pop: int = 1024
     hidden: int | None = None
@@ -168,41 +196,47 @@ class Config:
     anneal_gens: int = 300
 
 
+# ---- the policy --------------------------------------------------------------------------------
+
 def n_params(hidden, task):
-    return task.obs_dim * hidden + hidden + hidden * task.n_out + task.n_out
+    """Parameters of an obs-H-out MLP with biases on both layers."""
+    return (task.obs_dim + 1 + task.n_out) * hidden + task.n_out
 
 
 def unflatten(theta_pop, hidden, task):
-    """(P, D) parameter rows to the four batched weight arrays of an obs-H-out MLP."""
-    P, H, I, O = theta_pop.shape[0], hidden, task.obs_dim, task.n_out
-    i = 0
-    w1 = theta_pop[:, i:i + I * H].reshape(P, I, H); i += I * H
-    b1 = theta_pop[:, i:i + H]; i += H
-    w2 = theta_pop[:, i:i + H * O].reshape(P, H, O); i += H * O
-    b2 = theta_pop[:, i:i + O]
-    return w1, b1, w2, b2
+    """Views of the (P, D) parameter rows as the MLP's weights: w1 (P, obs, H), b1 (P, H),
+    w2 (P, H, out), b2 (P, out), stored in that order (es.py:156-164)."""
+    p, i, o = theta_pop.shape[0], task.obs_dim, task.n_out
+    w1, b1, w2, b2 = torch.split(theta_pop, (i * hidden, hidden, hidden * o, o), dim=1)
+    return w1.reshape(p, i, hidden), b1, w2.reshape(p, hidden, o), b2
 
 
 def population_logits(xp, obs, params):
-    """Every environment runs its own policy: one batched contraction per layer."""
+    """Each environment evaluated by its own member's MLP: two batched matrix products."""
     w1, b1, w2, b2 = params
-    h = torch.tanh(torch.einsum("pi,pih->ph", obs, w1) + b1)
-    return torch.einsum("ph,pho->po", h, w2) + b2
+    hidden = torch.tanh(torch.bmm(obs.unsqueeze(1), w1).squeeze(1) + b1)
+    return torch.bmm(hidden.unsqueeze(1), w2).squeeze(1) + b2
 
+
+# ---- curricula ---------------------------------------------------------------------------------
 
 def push(xp, task, state, start_velocity):
-    """The starting-push curriculum: add a forward velocity to every episode's initial state."""
-    if not start_velocity or task.xdot_row is None:
-        return state
-    state = state.clone()
-    state[task.xdot_row] += start_velocity
+    """Start every episode with start_velocity added to the forward velocity (es.py:196-203);
+    the state is returned unchanged when there is no push or the task has no forward row."""
+    if start_velocity and task.xdot_row is not None:
+        state = state.clone()
+        state[task.xdot_row] += start_velocity
     return state
 
 
 def curriculum(cfg, gen):
-    """Assistance stiffness and starting push at generation `gen`, annealed linearly to zero by anneal_gens."""
-    ramp = max(0.0, 1.0 - (gen - 1) / cfg.anneal_gens) if cfg.anneal_gens > 0 else 0.0
-    return cfg.assist_k0 * ramp, cfg.start_velocity * ramp
+    """(assist stiffness, start push) of generation gen: the configured values at generation 1,
+    falling linearly to zero by generation anneal_gens + 1, zero throughout when anneal_gens is
+    not positive (es.py:206-211)."""
+    if cfg.anneal_gens <= 0:
+        return 0.0, 0.0
+    weight = 1.0 - min(1.0, (gen - 1) / cfg.anneal_gens)
+    return cfg.assist_k0 * weight, cfg.start_velocity * weight
 
 
 # Populations from this size up are ranked by the O(P log P) sort kernel, smaller ones by the
@@ -237,23 +271,32 @@ def centered_ranks(xp, values, sorted_kernel=None):
 
 
 def loop_fitness(backend, params, horizon, assist=0.0, start_velocity=0.0, state=None):
-    """(reward sum until first termination, steps taken) for each member, stepping the whole
-    population once per iteration through the CUDA step kernel (es.py:174-193)."""
+    """(fitness, steps taken) per member by the step-at-a-time loop of es.py:174-193: the
+    population's MLPs in torch, the bodies through the CUDA step kernel, every member stepped
+    each iteration and credited only until its first termination."""
     task = backend.task
-    P = params[0].shape[0]
-    state = push(torch, task, backend.reset(P) if state is None else state, start_velocity)
-    alive = torch.ones(P, dtype=torch.bool, device=state.device)
-    fit = torch.zeros(P, device=state.device)
-    steps = torch.zeros(P, device=state.device)
+    n = params[0].shape[0]
+    if state is None:
+        state = backend.reset(n)
+    state = push(torch, task, state, start_velocity)
+    dev = state.device
+    running = torch.ones(n, dtype=torch.bool, device=dev)
+    fitness = torch.zeros(n, device=dev)
+    taken = torch.zeros(n, device=dev)
     for _ in range(horizon):
         action = task.action(torch, population_logits(torch, task.obs(torch, state), params))
-        state, reward, done = backend.step(state, action, assist) if task.assistable else backend.step(state, action)
-        steps = steps + alive.float()
-        fell = alive & done
-        alive = alive & ~done
-        forward = (reward - 1.0) * (state[1] >= task.height_gate).float() if task.height_gate else reward - 1.0
-        fit = fit + (forward + task.alive_bonus) * alive.float() - task.fall_penalty * fell.float()
-    return fit, steps
+        if task.assistable:
+            state, reward, done = backend.step(state, action, assist)
+        else:
+            state, reward, done = backend.step(state, action)
+        taken += running.float()
+        fell = running & done
+        running = running & ~done
+        progress = reward - 1.0
+        if task.height_gate:
+            progress = progress * (state[1] >= task.height_gate).float()
+        fitness += (progress + task.alive_bonus) * running.float() - task.fall_penalty * fell.float()
+    return fitness, taken
 
 
 def _world():
@@ -331,9 +374,8 @@ class MetalBackend:
 
     def rollout(self, theta_pop, hidden, horizon, assist=0.0, start_velocity=0.0, gen=0, member_offset=0):
         state = push(torch, self.task, self.reset(theta_pop.shape[0], gen, member_offset), start_velocity)
-        if self.task.assistable:
-            return self.task.rollout(state, theta_pop, hidden, horizon, assist)
-        return self.task.rollout(state, theta_pop, hidden, horizon)
+        extra = (assist,) if self.task.assistable else ()
+        return self.task.rollout(state, theta_pop, hidden, horizon, *extra)
 
     def gather(self, local):
         """All ranks' shards concatenated in rank order (one collective per tensor stack)."""
@@ -362,15 +404,17 @@ BACKENDS = {"metal": MetalBackend, "cuda": MetalBackend, "mlx": MLXBackend, "loo
 
 
 def generation(backend, theta, cfg, hidden, gen=1):
-    """One ES generation: perturb, roll out, rank, update (es.py:218-227)."""
+    """One generation of es.py:218-227 on this rank's shard of the population: perturb, roll
+    out, gather every shard's (fitness, steps), rank, update. Returns (theta, fitness, steps)
+    with fitness and steps of the whole population."""
     pairs = cfg.pop // 2
-    offset, rows = backend.shard(cfg.pop)
-    theta_pop = backend.perturb(theta, cfg.sigma, gen, pairs, offset, rows)
-    assist, start_velocity = curriculum(cfg, gen)
-    fit, steps = backend.rollout(theta_pop, hidden, cfg.horizon, assist, start_velocity, gen, offset)
+    first, count = backend.shard(cfg.pop)
+    members = backend.perturb(theta, cfg.sigma, gen, pairs, first, count)
+    stiffness, velocity = curriculum(cfg, gen)
+    fit, steps = backend.rollout(members, hidden, cfg.horizon, stiffness, velocity, gen, first)
     if backend.world > 1:
-        both = backend.gather(torch.stack([fit.float(), steps.float()], dim=1))
-        fit, steps = both[:, 0].contiguous(), both[:, 1].contiguous()
+        gathered = backend.gather(torch.stack([fit.float(), steps.float()], dim=1))
+        fit, steps = gathered[:, 0].contiguous(), gathered[:, 1].contiguous()
     theta = backend.update(theta, backend.centered_ranks(fit), cfg.lr, cfg.sigma, gen, pairs)
     backend.sync(theta)
     return theta, fit, steps
@@ -401,23 +445,27 @@ def assert_ranks_agree(theta):
 
 
 def mean_policy(theta, hidden, task):
-    """The unperturbed policy as an actor on (n, obs_dim) observations, on the GPU."""
-    w1, b1, w2, b2 = (p[0] for p in unflatten(theta[None, :], hidden, task))
-    return lambda obs: torch.tanh(obs @ w1 + b1) @ w2 + b2
+    """theta (D,) as a function from (n, obs_dim) observations to (n, out) logits."""
+    w1, b1, w2, b2 = (part[0] for part in unflatten(theta.reshape(1, -1), hidden, task))
+
+    def actor(obs):
+        return torch.tanh(obs @ w1 + b1) @ w2 + b2
+    return actor
 
 
 def evaluate(task, actor, n=2048, steps=500):
-    """Canonical score of a greedy actor over n fresh episodes (es.py:308-322): the environment's
-    reward minus one plus task.eval_bonus, summed to the first termination, on the GPU."""
+    """The score that decides "solved" (es.py:308-322): n fresh episodes of the greedy actor,
+    each crediting reward - 1 + task.eval_bonus per step until its first termination (the
+    environment's own reward for CartPole and Acrobot, forward distance for legged bodies);
+    the mean over episodes. The actor and the bodies run on the GPU."""
     state = task.mlx.reset(n)
-    alive = torch.ones(n, dtype=torch.bool, device=state.device)
-    fit = torch.zeros(n, device=state.device)
+    running = torch.ones(n, dtype=torch.bool, device=state.device)
+    total = torch.zeros(n, device=state.device)
     for _ in range(steps):
-        action = task.action(torch, actor(task.obs(torch, state)))
-        state, reward, done = task.metal.step(state, action)
-        alive = alive & ~done
-        fit = fit + (reward - 1.0 + task.eval_bonus) * alive.float()
-    return fit.mean().item()
+        state, reward, done = task.metal.step(state, task.action(torch, actor(task.obs(torch, state))))
+        running &= ~done
+        total += (reward - 1.0 + task.eval_bonus) * running.float()
+    return total.mean().item()
 
 
 def evaluate_theta(task, theta, hidden, n=2048, steps=500, state=None):
@@ -434,64 +482,81 @@ def evaluate_theta(task, theta, hidden, n=2048, steps=500, state=None):
 
 @dataclass
 class Result:
+    """Outcome of `train`, with es.py's fields: env_steps counts the steps members actually
+    took (each episode ends at its first termination); train_seconds covers the generations
+    only, not the evaluations of the mean policy."""
     solved: bool
     generations: int
-    env_steps: int        # steps actually taken: a member's episode ends at its first termination
-    train_seconds: float  # training only; evaluation of the mean policy is outside the clock
+    env_steps: int
+    train_seconds: float
     score: float
 
 
 def train(cfg, backend_name, seed, log=lambda *_: None):
-    assert cfg.pop % 2 == 0
+    """Run generations until the mean policy's score reaches the threshold, the generation cap
+    or the time budget (es.py:334-354). log(gen, env_steps, train_seconds, mean fitness,
+    score) is called after every generation."""
+    if cfg.pop % 2:
+        raise ValueError(f"the population must be even (antithetic pairs); got {cfg.pop}")
     if backend_name not in BACKENDS:
         raise ValueError(f"backend {backend_name!r}: this build runs on the GPU only ({sorted(BACKENDS)}); "
                          "the numpy reference is the test oracle")
     task = TASKS[cfg.task]
-    hidden = task.hidden if cfg.hidden is None else cfg.hidden
-    solved_at = task.solved_at if cfg.solved_at is None else cfg.solved_at
-    backend = BACKENDS[backend_name](task, seed)
-    theta = backend.normal((n_params(hidden, task),)) * 0.1
+    width = task.hidden if cfg.hidden is None else cfg.hidden
+    target = task.solved_at if cfg.solved_at is None else cfg.solved_at
+    make_backend = BACKENDS[backend_name]
+    backend = make_backend(task, seed)
+    theta = backend.normal((n_params(width, task),)) * 0.1
     backend.sync(theta)
-    train_seconds, env_steps, score, gen = 0.0, 0, 0.0, 0
-    for gen in range(1, cfg.max_generations + 1):
-        start = time.perf_counter()
-        theta, fit, steps = generation(backend, theta, cfg, hidden, gen)
-        train_seconds += time.perf_counter() - start
-        env_steps += int(steps.sum().item())
+    clock, taken, score, gen = 0.0, 0, 0.0, 0
+    while gen < cfg.max_generations:
+        gen += 1
+        t0 = time.perf_counter()
+        theta, fit, steps = generation(backend, theta, cfg, width, gen)
+        clock += time.perf_counter() - t0
+        taken += int(steps.sum().item())
         if backend.world > 1 and gen % CHECK_EVERY == 0:
             assert_ranks_agree(theta)
-        score = evaluate_theta(task, theta, hidden)
-        log(gen, env_steps, train_seconds, float(fit.mean().item()), score)
-        if score >= solved_at:
-            return Result(True, gen, env_steps, train_seconds, score)
-        if train_seconds >= cfg.time_budget:
+        score = evaluate_theta(task, theta, width)
+        log(gen, taken, clock, float(fit.mean().item()), score)
+        if score >= target:
+            return Result(True, gen, taken, clock, score)
+        if clock >= cfg.time_budget:
             break
-    return Result(False, gen, env_steps, train_seconds, score)
+    return Result(False, gen, taken, clock, score)
 
 
-def main():
-    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    p.add_argument("--task", choices=TASKS, default="cartpole")
-    p.add_argument("--pop", type=int, default=1024)
-    p.add_argument("--backend", choices=BACKENDS, default="metal")
-    p.add_argument("--seed", type=int, default=0)
-    p.add_argument("--lr", type=float, default=0.1)
-    p.add_argument("--sigma", type=float, default=0.1)
-    p.add_argument("--time-budget", type=float, default=120.0)
-    p.add_argument("--max-generations", type=int, default=500)
-    p.add_argument("--assist", type=float, default=0.0, help="torso-assist spring stiffness at generation 1, annealed to zero")
-    p.add_argument("--start-velocity", type=float, default=0.0, help="forward push at episode start, annealed to zero")
-    p.add_argument("--anneal", type=int, default=300, help="generation by which both curricula reach zero")
-    args = p.parse_args()
-    cfg = Config(task=args.task, pop=args.pop, lr=args.lr, sigma=args.sigma, time_budget=args.time_budget,
-                 max_generations=args.max_generations, assist_k0=args.assist,
-                 start_velocity=args.start_velocity, anneal_gens=args.anneal)
-    result = train(
-        cfg, args.backend, args.seed,
-        log=lambda gen, es_, secs, fit, score: print(
-            f"gen {gen:4d}  env_steps {es_:>13,}  train {secs:7.2f}s  pop fitness {fit:8.1f}  score {score:8.1f}", flush=True),
-    )
-    print(result)
+# es.py's command line: flag -> (type, default, help)
+_FLAGS = {
+    "--task": (str, "cartpole", "the task to learn"),
+    "--pop": (int, 1024, "population size (even: antithetic pairs)"),
+    "--backend": (str, "metal", "metal (alias cuda): the fused kernels; mlx (alias loop): the step loop"),
+    "--seed": (int, 0, "seed of parameters, noise and initial states"),
+    "--lr": (float, 0.1, "learning rate"),
+    "--sigma": (float, 0.1, "perturbation scale"),
+    "--time-budget": (float, 120.0, "seconds of training after which the run stops"),
+    "--max-generations": (int, 500, "generation cap"),
+    "--assist": (float, 0.0, "curriculum: torso-assist stiffness at generation 1, annealed to zero"),
+    "--start-velocity": (float, 0.0, "curriculum: forward push at the start of every episode, annealed to zero"),
+    "--anneal": (int, 300, "generation by which both curricula have reached zero"),
+}
+
+
+def main(argv=None):
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    for flag, (kind, default, text) in _FLAGS.items():
+        choices = {"--task": TASKS, "--backend": BACKENDS}.get(flag)
+        parser.add_argument(flag, type=kind, default=default, help=text, choices=choices)
+    args = parser.parse_args(argv)
+    renamed = {"assist": "assist_k0", "anneal": "anneal_gens"}  # flags whose Config field is named otherwise
+    cfg = Config(**{renamed.get(k, k): v for k, v in vars(args).items() if k not in ("backend", "seed")})
+
+    def report(gen, env_steps, seconds, fitness, score):
+        print(f"generation {gen:4d} | {env_steps:>14,} env steps | {seconds:8.2f} s | population fitness "
+              f"{fitness:8.1f} | score {score:8.1f}", flush=True)
+
+    print(train(cfg, args.backend, args.seed, log=report))
+    return 0
 
 
 if __name__ == "__main__":

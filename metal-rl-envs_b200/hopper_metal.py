@@ -14,7 +14,8 @@ import numpy as np
 import rlenv_lib as _rl
 from legged_metal import FALL_ANGLE, FALL_HEIGHT, L, RESET_BOUND, _OnDevice  # noqa: F401
 
-STAND = np.array([0.0, L, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0], dtype=np.float32)
+STAND = np.zeros(8, dtype=np.float32)
+STAND[1] = L  # upright at rest, the hip one leg length above the floor
 
 
 class Hopper(_rl.StepBody):

@@ -31,22 +31,27 @@ ITERS = 8
 
 
 def leg_angles(c):
-    """Resting leg angles, spread symmetrically so the inner feet touch the floor."""
-    return np.linspace(-0.25 * (c - 1), 0.25 * (c - 1), c) if c > 1 else np.zeros(1)
+    """Resting leg angles, 0.5 rad apart and symmetric about the vertical."""
+    return (2.0 * np.arange(c) - (c - 1)) * 0.25
+
+
+def _at_rest(angles):
+    """State (2(3+C),) at rest with the given leg angles, the hip as high as the innermost leg."""
+    angles = np.asarray(angles, dtype=np.float64)
+    q = np.zeros(3 + angles.size)
+    q[1] = L * np.cos(np.min(np.abs(angles)))
+    q[3:] = angles
+    return np.pad(q, (0, q.size)).astype(np.float32)
 
 
 def stand_pose(c):
     """The reset pose (2(3+C),): hip at the height of the innermost feet, at rest."""
-    a = leg_angles(c)
-    q = np.concatenate([[0.0, L * np.cos(np.abs(a).min()), 0.0], a])
-    return np.concatenate([q, np.zeros_like(q)]).astype(np.float32)
+    return _at_rest(leg_angles(c))
 
 
 def static_pose(c):
-    """A true equilibrium with every foot on the floor, legs at +-0.25 rad."""
-    a = np.array([-0.25, 0.25] * (c // 2)) if c > 1 else np.zeros(1)
-    q = np.concatenate([[0.0, L * np.cos(np.abs(a).min()), 0.0], np.sort(a)])
-    return np.concatenate([q, np.zeros_like(q)]).astype(np.float32)
+    """A true equilibrium with every foot on the floor, legs at +-0.25 rad (C even)."""
+    return _at_rest(np.where(np.arange(c) < c // 2, -0.25, 0.25) if c > 1 else [0.0])
 
 
 class _OnDevice:

@@ -76,7 +76,8 @@ def _acrobot_derivative(th1, th2, w1, w2, torque):
 
 def wrap_angle(x):
     """To [-pi, pi) without branches (acrobot_np.py:88-90)."""
-    return x - 2 * np.pi * np.floor((x + np.pi) / (2 * np.pi))
+    period = 2 * np.pi
+    return x - period * np.floor((x + np.pi) / period)
 
 
 def acrobot_physics(state, action):
@@ -95,7 +96,7 @@ def acrobot_physics(state, action):
 
 def acrobot_terminated(state):
     """Tip above height 1: -cos t1 - cos(t1 + t2) > 1 (acrobot_np.py:92-93)."""
-    return -np.cos(state[0]) - np.cos(state[1] + state[0]) > 1.0
+    return np.cos(state[0]) + np.cos(state[0] + state[1]) < -1.0
 
 
 def acrobot_reward(done):

@@ -56,15 +56,15 @@ TASKS = {
 
 
 def n_params(hidden, task):
-    return task.obs_dim * hidden + hidden + hidden * task.n_out + task.n_out
+    """Weights and biases of both layers of the obs-H-out MLP (es.py:152-153)."""
+    return (task.obs_dim + 1 + task.n_out) * hidden + task.n_out
 
 
 def unflatten(theta_pop, hidden, task):
-    """(P, D) rows to w1 (P, I, H), b1 (P, H), w2 (P, H, O), b2 (P, O) (es.py:156-164)."""
-    P, H, I, O = theta_pop.shape[0], hidden, task.obs_dim, task.n_out
-    cuts = np.cumsum([I * H, H, H * O])
-    w1, b1, w2, b2 = np.split(theta_pop, cuts, axis=1)
-    return w1.reshape(P, I, H), b1, w2.reshape(P, H, O), b2
+    """(P, D) rows to w1 (P, obs, H), b1 (P, H), w2 (P, H, out), b2 (P, out) (es.py:156-164)."""
+    rows, n_in, n_out = theta_pop.shape[0], task.obs_dim, task.n_out
+    w1, b1, w2, b2 = np.split(theta_pop, np.cumsum([n_in * hidden, hidden, hidden * n_out]), axis=1)
+    return w1.reshape(rows, n_in, hidden), b1, w2.reshape(rows, hidden, n_out), b2
 
 
 def population_logits(obs, params):
@@ -122,11 +122,11 @@ def env_step(task, state, action, rng, assist=0.0):
 
 
 def push(task, state, start_velocity):
-    if not start_velocity or task.xdot_row is None:
-        return state
-    out = state.copy()
-    out[task.xdot_row] += start_velocity
-    return out
+    """Initial states with start_velocity added to the forward velocity row (es.py:196-203)."""
+    if start_velocity and task.xdot_row is not None:
+        state = state.copy()
+        state[task.xdot_row] += start_velocity
+    return state
 
 
 # ---- learner -------------------------------------------------------------------
@@ -149,8 +149,10 @@ class Config:
 
 
 def curriculum(cfg, gen):
-    ramp = max(0.0, 1.0 - (gen - 1) / cfg.anneal_gens) if cfg.anneal_gens > 0 else 0.0
-    return cfg.assist_k0 * ramp, cfg.start_velocity * ramp
+    """(assist, push) at generation gen: linear from the configured values at generation 1 to
+    zero at generation anneal_gens + 1; zero when anneal_gens is not positive (es.py:206-211)."""
+    weight = 1.0 - min(1.0, (gen - 1) / cfg.anneal_gens) if cfg.anneal_gens > 0 else 0.0
+    return cfg.assist_k0 * weight, cfg.start_velocity * weight
 
 
 def loop_fitness(task, params, horizon, rng, state=None, assist=0.0, start_velocity=0.0):
@@ -164,7 +166,7 @@ def loop_fitness(task, params, horizon, rng, state=None, assist=0.0, start_veloc
     for _ in range(horizon):
         a = act(task, population_logits(observe(task, s), params))
         s, r, done = env_step(task, s, a, rng, assist)
-        steps = steps + alive.astype(steps.dtype)
+        steps += alive
         fell = alive & done
         alive = alive & ~done
         fwd = (r - 1.0) * (s[1] >= task.height_gate).astype(fit.dtype) if task.height_gate else r - 1.0
@@ -209,22 +211,28 @@ class Result:
 
 
 def train(cfg, seed, log=lambda *_: None):
-    assert cfg.pop % 2 == 0
+    """es.py:334-354 with the numpy backend and the numpy evaluation above: generations until
+    the mean policy's score reaches the threshold, the generation cap or the time budget. One
+    numpy Generator seeded with `seed` draws theta, then each generation's noise and initial
+    states, then each evaluation's episodes, in that order."""
+    if cfg.pop % 2:
+        raise ValueError("the population must be even")
     task = TASKS[cfg.task]
-    hidden = task.hidden if cfg.hidden is None else cfg.hidden
-    solved_at = task.solved_at if cfg.solved_at is None else cfg.solved_at
+    width = cfg.hidden if cfg.hidden is not None else task.hidden
+    target = cfg.solved_at if cfg.solved_at is not None else task.solved_at
     rng = np.random.default_rng(seed)
-    theta = rng.normal(size=(n_params(hidden, task),)).astype(np.float32) * 0.1
-    secs, env_steps, score, gen = 0.0, 0, 0.0, 0
-    for gen in range(1, cfg.max_generations + 1):
-        t0 = time.perf_counter()
-        theta, fit, steps = generation(task, theta, cfg, hidden, rng, gen)
-        secs += time.perf_counter() - t0
-        env_steps += int(steps.sum())
-        score = evaluate(task, theta, hidden, rng)
-        log(gen, env_steps, secs, float(fit.mean()), score)
-        if score >= solved_at:
-            return Result(True, gen, env_steps, secs, score)
-        if secs >= cfg.time_budget:
+    theta = rng.normal(size=(n_params(width, task),)).astype(np.float32) * 0.1
+    clock, taken, score, gen = 0.0, 0, 0.0, 0
+    while gen < cfg.max_generations:
+        gen += 1
+        start = time.perf_counter()
+        theta, fit, steps = generation(task, theta, cfg, width, rng, gen)
+        clock += time.perf_counter() - start
+        taken += int(steps.sum())
+        score = evaluate(task, theta, width, rng)
+        log(gen, taken, clock, float(fit.mean()), score)
+        if score >= target:
+            return Result(True, gen, taken, clock, score)
+        if clock >= cfg.time_budget:
             break
-    return Result(False, gen, env_steps, secs, score)
+    return Result(False, gen, taken, clock, score)

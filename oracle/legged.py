@@ -28,22 +28,27 @@ HOPPER_STAND = np.array([0.0, LG_L, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0], dtype=np.floa
 
 
 def leg_angles(c):
-    """Resting leg angles, spread symmetrically (legged_np.py:28-30)."""
-    return np.linspace(-0.25 * (c - 1), 0.25 * (c - 1), c) if c > 1 else np.zeros(1)
+    """Resting leg angles, spread symmetrically 0.5 rad apart (legged_np.py:28-30)."""
+    return 0.5 * (np.arange(c) - 0.5 * (c - 1))
+
+
+def _pose(angles):
+    """Zero-velocity state with the hip at the height where the innermost foot touches."""
+    c = len(angles)
+    s = np.zeros(2 * (3 + c), dtype=np.float32)
+    s[1] = LG_L * np.cos(np.abs(angles).min())
+    s[3:3 + c] = angles
+    return s
 
 
 def stand_pose(c):
     """Reset pose: hip at the height where the innermost feet touch the floor (legged_np.py:43-46)."""
-    a = leg_angles(c)
-    q = np.concatenate([[0.0, LG_L * np.cos(np.abs(a).min()), 0.0], a])
-    return np.concatenate([q, np.zeros_like(q)]).astype(np.float32)
+    return _pose(leg_angles(c))
 
 
 def static_pose(c):
     """Every foot on the floor with legs at +-0.25 rad: a true equilibrium (legged_np.py:33-40)."""
-    a = np.array([-0.25, 0.25] * (c // 2)) if c > 1 else np.zeros(1)
-    q = np.concatenate([[0.0, LG_L * np.cos(np.abs(a).min()), 0.0], np.sort(a)])
-    return np.concatenate([q, np.zeros_like(q)]).astype(np.float32)
+    return _pose(np.repeat([-0.25, 0.25], c // 2) if c > 1 else np.zeros(1))
 
 
 def torques(action, c):
@@ -83,15 +88,19 @@ def substep(q, v, tq, c, iters=LG_ITERS, mu=LG_MU, assist=0.0, return_impulses=F
     n = 3 + c
     z = np.zeros_like(q[0])
     one = z + 1.0
-    Jt, Jn, drift, depth = [], [], [], []
-    for k in range(c):
-        a = q[2] + q[3 + k]
-        ca, sa = np.cos(a), np.sin(a)
-        ad = v[2] + v[3 + k]
-        Jt.append([one, z, LG_L * ca] + [LG_L * ca if j == k else z for j in range(c)])
-        Jn.append([z, one, LG_L * sa] + [LG_L * sa if j == k else z for j in range(c)])
-        drift.append((-LG_L * sa * ad * ad, LG_L * ca * ad * ad))
-        depth.append(-(q[1] - LG_L * ca))
+
+    def foot(k):
+        # Rows of the foot's tangential and normal Jacobians, the velocity-product term of its
+        # acceleration, and its penetration below the floor.
+        ang = q[2] + q[3 + k]
+        ca, sa = np.cos(ang), np.sin(ang)
+        rate = v[2] + v[3 + k]
+        leg_t = [LG_L * ca if j == k else z for j in range(c)]
+        leg_n = [LG_L * sa if j == k else z for j in range(c)]
+        return ([one, z, LG_L * ca, *leg_t], [z, one, LG_L * sa, *leg_n],
+                (-LG_L * sa * rate * rate, LG_L * ca * rate * rate), -(q[1] - LG_L * ca))
+
+    Jt, Jn, drift, depth = (list(col) for col in zip(*(foot(k) for k in range(c))))
     base = [[0.0] * n for _ in range(n)]  # Python floats: weak scalars in float32 expressions
     base[0][0] = base[1][1] = LG_M_T
     base[2][2] = LG_I_T
@@ -113,11 +122,15 @@ def substep(q, v, tq, c, iters=LG_ITERS, mu=LG_MU, assist=0.0, return_impulses=F
          for k in range(c)]
     w0 = [(dot(Jt[k], vfree), dot(Jn[k], vfree)) for k in range(c)]
     lt, ln = [z] * c, [z] * c
+
+    def coupled(k, row):
+        # Velocity that the other contacts' current impulses add along row 0 (tangent) or 1 (normal).
+        return sum(A[k][l][2 * row] * lt[l] + A[k][l][2 * row + 1] * ln[l] for l in range(c) if l != k)
+
     for _ in range(iters):
         for k in range(c):
-            wt = w0[k][0] + sum(A[k][l][0] * lt[l] + A[k][l][1] * ln[l] for l in range(c) if l != k)
-            wn = w0[k][1] + sum(A[k][l][2] * lt[l] + A[k][l][3] * ln[l] for l in range(c) if l != k)
-            lt[k], ln[k] = contact_impulse(A[k][k][0], A[k][k][1], A[k][k][3], wt, wn, depth[k], mu)
+            rel_t, rel_n = w0[k][0] + coupled(k, 0), w0[k][1] + coupled(k, 1)
+            lt[k], ln[k] = contact_impulse(A[k][k][0], A[k][k][1], A[k][k][3], rel_t, rel_n, depth[k], mu)
     vnew = np.stack([vfree[i] + sum(MiJt[k][i] * lt[k] + MiJn[k][i] * ln[k] for k in range(c)) for i in range(n)])
     out = q + LG_H * vnew, vnew
     return out + (np.stack(lt), np.stack(ln)) if return_impulses else out
@@ -131,7 +144,7 @@ def physics(state, action, c, iters=LG_ITERS, assist=0.0):
     tq = torques(action, c)
     for _ in range(LG_SUBSTEPS):
         q, v = substep(q, v, tq, c, iters, assist=assist)
-    return np.concatenate([q, v])
+    return np.r_[q, v]
 
 
 def step_impulses(state, action, c, iters=LG_ITERS, assist=0.0):

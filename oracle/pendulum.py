@@ -71,8 +71,8 @@ def aba_accel(th, om, torque, k):
     accelerating at -g, then a prefix sum from joint to absolute accelerations.
     Planar motion vectors (w, vx, vy); inertias as (00, 01, 02, 11, 12, 22)."""
     z = np.zeros_like(th[0])
-    q = [th[0]] + [th[i] - th[i - 1] for i in range(1, k)]
-    qd = [om[0]] + [om[i] - om[i - 1] for i in range(1, k)]
+    q = [th[0], *np.diff(th[:k], axis=0)]  # joint angle: each link relative to its parent
+    qd = [om[0], *np.diff(om[:k], axis=0)]
     cs = [np.cos(qi) for qi in q]
     sn = [np.sin(qi) for qi in q]
     vel, bias_c, p, inertia = [], [], [], []
@@ -88,7 +88,7 @@ def aba_accel(th, om, torque, k):
         p.append([v[1] * fy - v[2] * fx, -v[0] * fy, v[0] * fx])
         inertia.append([z + 1.0, z, z + 1.0, z + 1.0, z, z + 1.0])
         prev = v
-    U, D, u = [None] * k, [None] * k, [None] * k
+    U, D, u = {}, {}, {}
     for i in range(k - 1, -1, -1):
         a00, a01, a02, a11, a12, a22 = inertia[i]
         U[i] = (a00, a01, a02)
@@ -170,8 +170,7 @@ def reward(done):
 
 def energy(state, k):
     """Kinetic plus potential energy per env, unit masses and rods (pendulum_np.py:114-120)."""
-    th, om = state[:k], state[k:]
-    vx = np.cumsum(om * np.cos(th), axis=0)
-    vy = np.cumsum(om * np.sin(th), axis=0)
-    height = np.cumsum(-np.cos(th), axis=0)
-    return 0.5 * (vx**2 + vy**2).sum(axis=0) + PD_GRAVITY * height.sum(axis=0)
+    th, om = state[:k], state[k:2 * k]
+    joint_vel = np.cumsum(np.stack([om * np.cos(th), om * np.sin(th)]), axis=1)  # (2, K, N)
+    kinetic = 0.5 * np.square(joint_vel).sum(axis=0).sum(axis=0)
+    return kinetic + PD_GRAVITY * np.cumsum(-np.cos(th), axis=0).sum(axis=0)

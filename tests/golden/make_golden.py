@@ -114,7 +114,8 @@ def main():
     # random SPD Delassus blocks (test_hopper.py:268-281)
     rng = np.random.default_rng(0)
     n = 500
-    q = np.stack([rng.uniform(-1, 1, n), rng.uniform(0.7, 1.3, n), rng.uniform(-0.6, 0.6, n), rng.uniform(-0.8, 0.8, n)])
+    ranges = ((-1.0, 1.0), (0.7, 1.3), (-0.6, 0.6), (-0.8, 0.8))  # x, y, phi, psi; drawn in this order
+    q = np.stack([rng.uniform(lo, hi, n) for lo, hi in ranges])
     state = np.concatenate([q, rng.uniform(-2, 2, (4, n))]).astype(np.float32)
     action = rng.integers(0, 3, n)
     h = hopper_np.Hopper()

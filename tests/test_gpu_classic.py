@@ -73,7 +73,7 @@ def test_resets_are_uniform_bounded_and_vary(cuda, name):
     m = mod()
     m.reseed(0)
     n = 16384
-    terminal = np.zeros((4, n), dtype=np.float32)
+    terminal = np.zeros((4, n), np.float32)
     if name == "cartpole":
         terminal[:] = 3.0
     else:

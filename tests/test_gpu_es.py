@@ -119,11 +119,11 @@ def test_update_matches_float64(cuda):
 def test_generation_uses_antithetic_pairs_and_moves_theta(cuda):
     import es
 
-    cfg = es.Config(pop=8, horizon=5)
+    pop, horizon, width = 8, 5, 4
     backend = es.MetalBackend(es.TASKS["cartpole"], 0)
-    theta = torch.zeros(es.n_params(4, es.TASKS["cartpole"]), device=cuda)
-    new, fit, steps = es.generation(backend, theta, cfg, 4)
-    assert fit.shape == (8,) and float(steps.max()) <= 5
+    theta = torch.zeros(es.n_params(width, es.TASKS["cartpole"]), device=cuda)
+    new, fit, steps = es.generation(backend, theta, es.Config(pop=pop, horizon=horizon), width)
+    assert tuple(fit.shape) == (pop,) and steps.max().item() <= horizon
     assert not torch.allclose(new, torch.zeros_like(new))
 
 
@@ -157,9 +157,12 @@ def test_fused_kernel_matches_step_loop(cuda, name, scale):
     fk, sk = task.rollout(state, theta, task.hidden, horizon)
     fl, sl = es.loop_fitness(backend, es.unflatten(theta, task.hidden, task), horizon, state=state)
     fk, fl, sk, sl = to_np(fk), to_np(fl), to_np(sk), to_np(sl)
-    close = np.abs(fk - fl) <= 1e-3 * np.maximum(np.abs(fl), 1.0) + 1e-2
-    record(f"es_kernel_vs_loop_{name}", fitness_agree=float(close.mean()), steps_agree=float((sk == sl).mean()))
-    assert close.mean() > 0.95 and (sk == sl).mean() > 0.95, (close.mean(), (sk == sl).mean())
+    # the reference's criterion (test_es.py): fitness within 1e-3 relative (floor 1) plus 1e-2,
+    # and equal step counts, for more than 95% of the members
+    fitness_agree = float(np.mean(np.isclose(fk, fl, rtol=0.0, atol=1e-2 + 1e-3 * np.maximum(np.abs(fl), 1.0))))
+    steps_agree = float(np.mean(sk == sl))
+    record(f"es_kernel_vs_loop_{name}", fitness_agree=fitness_agree, steps_agree=steps_agree)
+    assert min(fitness_agree, steps_agree) > 0.95, (fitness_agree, steps_agree)
     if name.startswith("legged"):
         assert 5 < sl.mean() < 200
 
@@ -196,16 +199,22 @@ def test_es_learns_cartpole(cuda):
 def test_es_learns_acrobot(cuda):
     import es
 
-    r = es.train(es.Config(task="acrobot", pop=4096, time_budget=60.0, solved_at=-250.0), "metal", seed=0)
-    record("es_acrobot_p4096", solved=r.solved, generations=r.generations, score=r.score, seconds=r.train_seconds)
-    assert r.score >= -250.0, r
+    goal = -250.0  # the reference's learning check for Acrobot at P = 4,096
+    result = es.train(es.Config(task="acrobot", pop=4096, time_budget=60.0, solved_at=goal), "metal", seed=0)
+    record("es_acrobot_p4096", solved=result.solved, generations=result.generations, score=result.score,
+           seconds=result.train_seconds)
+    assert result.score >= goal, result
 
 
 def test_es_biped_learns_to_stay_up(cuda):
     import es
 
-    last = []
-    es.train(es.Config(task="legged2", pop=1024, time_budget=30.0, max_generations=60), "metal", seed=0,
-             log=lambda gen, steps, secs, fit, score: last.append(fit))
-    record("es_legged2_p1024_60gens", final_fitness=last[-1], generations=len(last))
-    assert last[-1] >= 300.0, last[-1]
+    fitness_by_generation = []
+
+    def keep(*entry):  # (gen, env_steps, seconds, mean training fitness, score)
+        fitness_by_generation.append(entry[3])
+
+    es.train(es.Config(task="legged2", pop=1024, time_budget=30.0, max_generations=60), "metal", seed=0, log=keep)
+    final = fitness_by_generation[-1]
+    record("es_legged2_p1024_60gens", final_fitness=final, generations=len(fitness_by_generation))
+    assert final >= 300.0, final  # the biped stands for most of its 500-step episodes

@@ -14,7 +14,8 @@ pytestmark = pytest.mark.gpu
 
 def _agree(name, fk, fl, sk=None, sl=None):
     fk, fl = np.asarray(fk, np.float64), np.asarray(fl, np.float64)
-    close = np.abs(fk - fl) <= 1e-3 * np.maximum(np.abs(fl), 1.0) + 1e-2
+    tol = 1e-2 + 1e-3 * np.maximum(np.abs(fl), 1.0)
+    close = np.abs(fk - fl) <= tol
     same = (np.asarray(sk) == np.asarray(sl)).mean() if sk is not None else close.mean()
     record(name, fitness_agree=float(close.mean()), steps_agree=float(same), members=int(fk.size))
     return close.mean(), same
@@ -90,7 +91,7 @@ def test_legged_rollout_long_horizon_matches_oracle(cuda, c, alive, fall, gate, 
     assert s_ok > 0.95 and f_ok > 0.7
     assert abs(fk.mean() - fl.mean()) <= 0.03 * np.abs(fl).mean() + 0.05
     if fall:
-        assert (fk < 0).any(), "some random bipeds fall and pay the penalty"
+        assert fk.min() < 0, "a random biped that falls pays the penalty"
 
 
 def test_shared_theta_row_equals_broadcast_rows(cuda):

@@ -152,10 +152,10 @@ def _run(q, v, tau, n, mu=legged.LG_MU):
 
 
 def _col(*vals):
-    return np.array(vals, dtype=np.float32)[:, None]
+    return np.asarray(vals, np.float32).reshape(-1, 1)
 
 
-def test_free_flight_is_a_parabola():
+def test_airborne_body_follows_a_ballistic_arc():
     q, v = _run(_col(0.0, 10.0, 0.0, 0.0), _col(0.3, 0.0, 0.0, 0.0), np.zeros(1, np.float32), 100)
     assert abs(q[1, 0] - (10.0 - 0.5 * 9.8 * 1.0)) < 0.06 and abs(q[0, 0] - 0.3) < 1e-4
 
@@ -195,7 +195,7 @@ def test_contact_impulse_complementarity():
     lt, ln = legged.contact_impulse(att, atn, ann, wt, wn, depth)
     target = 20.0 * np.maximum(depth, 0.0)
     wt2, wn2 = wt + att * lt + atn * ln, wn + atn * lt + ann * ln
-    assert (ln >= 0).all() and (ln[depth < 0] == 0).all()
+    assert ln.min() >= 0 and not ln[depth < 0].any()
     ok = ann > legged.LG_MU * np.abs(atn)
     push_ = ok & (ln > 0)
     np.testing.assert_allclose(wn2[push_], target[push_], atol=1e-3)
@@ -217,13 +217,13 @@ def _standing_drift(c, iters, substeps=400):
     q, v = pose[:d].astype(np.float32)[:, None], np.zeros((d, 1), np.float32)
     for _ in range(substeps):
         q, v = legged.substep(q, v, [np.zeros(1, np.float32)] * c, c, iters=iters)
-    return float(np.abs(q[:, 0] - pose[:d]).max())
+    return float(np.max(np.abs(q[:, 0] - pose[:d])))
 
 
 def test_two_leg_stand_converges_with_sweeps():
     drifts = [_standing_drift(2, k) for k in (1, 4, 8, 32, 256)]
-    assert all(a > b for a, b in zip(drifts, drifts[1:])), drifts
-    assert drifts[-1] < 1e-6 and drifts[2] < 1e-2, drifts
+    assert np.all(np.diff(drifts) < 0), drifts  # more sweeps, less drift
+    assert drifts[2] < 1e-2 and drifts[4] < 1e-6, drifts
 
 
 @pytest.mark.parametrize("c", [1, 2, 4])
