@@ -22,12 +22,15 @@ namespace {
 // next first RK4 stage needs). kVec is the number of consecutive environments
 // a thread owns: 4 (16-byte accesses) where the step is light enough to be
 // bound by memory, 1 where it is bound by instruction issue and the
-// occupancy of one environment per thread hides latency better. kMinBlocks is
-// the launch bound on resident 256-thread blocks per SM.
+// occupancy of one environment per thread hides latency better. kBlock is the
+// block size and kMinBlocks the launch bound on resident blocks per SM.
 struct CartPoleEnv {
   using S = CartPole;
   struct Aux {};
   static constexpr int kVec = 4;
+  // 128 threads: 131,072 environments make 1,024 blocks, 6.9 per SM, against 3.5 (so
+  // 4 on some SMs, 3 on others) with 256 threads: 145 against 133 B env-steps/s on a B200
+  static constexpr int kBlock = 128;
   static constexpr int kMinBlocks = 1;
   RLENV_D static S from(const float (&r)[4]) { return S{r[0], r[1], r[2], r[3]}; }
   RLENV_D static void to(const S& s, float (&r)[4]) {
@@ -52,6 +55,7 @@ struct AcrobotEnv {
   static constexpr int kVec = 1;
   // 8 resident blocks of 256 threads (at most 32 registers): the whole batch of a
   // 262,144-environment launch is resident at once instead of 1.15 waves
+  static constexpr int kBlock = 256;
   static constexpr int kMinBlocks = 8;
   RLENV_D static S from(const float (&r)[4]) { return S{r[0], r[1], r[2], r[3]}; }
   RLENV_D static void to(const S& s, float (&r)[4]) {
@@ -164,9 +168,11 @@ RLENV_D void store_states(float* __restrict__ s, int64_t n, int64_t i, const typ
 }
 
 // SUMS selects the instance that also accumulates per-environment reward sums
-// and termination counts; the plain chain keeps those registers free.
-template <typename Env, typename A, int V, bool SUMS>
-__global__ void __launch_bounds__(kThreads, Env::kMinBlocks)
+// and termination counts; the plain chain keeps those registers free. SEQ is set
+// when both per-step sequences are written: the loop then has no per-step test
+// of their pointers (3.5% of the Acrobot kernel's time on a B200).
+template <typename Env, typename A, int V, bool SUMS, bool SEQ>
+__global__ void __launch_bounds__(Env::kBlock, Env::kMinBlocks)
 step_many_kernel(const float* __restrict__ state_in, const A* __restrict__ actions, uint32_t seed0,
                  int64_t T, int64_t n, int64_t off, float* __restrict__ state_out,
                  float* __restrict__ reward_seq, uint8_t* __restrict__ done_seq,
@@ -195,8 +201,8 @@ step_many_kernel(const float* __restrict__ state_in, const A* __restrict__ actio
       d[u] = Env::step(st[u], aux[u], act[u], env_hash(seed0 + uint32_t(t), off + i + u), rw[u]);
 #pragma unroll
     for (int u = 0; u < V; ++u) act[u] = nxt[u];
-    if (reward_seq) store_vec<V>(reward_seq, t * n + i, rw);
-    if (done_seq) store_flags<V>(done_seq, t * n + i, d);
+    if (SEQ || reward_seq) store_vec<V>(reward_seq, t * n + i, rw);
+    if (SEQ || done_seq) store_flags<V>(done_seq, t * n + i, d);
     if constexpr (SUMS) {
 #pragma unroll
       for (int u = 0; u < V; ++u) {
@@ -215,11 +221,11 @@ step_many_kernel(const float* __restrict__ state_in, const A* __restrict__ actio
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Four environments per thread (16-byte state accesses, one load of four actions) pay off
-// only when the batch still fills the GPU at a quarter of the threads: from about four
-// resident 256-thread blocks per SM on the 148 SMs of a B200. Below that one environment
-// per thread is faster (measured with T = 1,000 on a B200: at N = 131,072, 134 against 80 B
-// env-steps/s; at N = 1,048,576, 178 against 196 B).
-constexpr int64_t kVecMinEnvs = int64_t(4) * kThreads * 4 * 148;
+// only when the batch still fills the GPU at a quarter of the threads: from about 32
+// resident warps per SM on the 148 SMs of a B200. Below that one environment per thread
+// is faster (measured with T = 1,000 on a B200: at N = 131,072, 145 against 80 B
+// env-steps/s; at N = 1,048,576, 188 against 201 B).
+constexpr int64_t kVecMinEnvs = int64_t(4) * 32 * 32 * 148;
 
 template <typename Env>
 int launch_step_many(const float* state_in, const void* actions, int dtype, uint32_t seed0,
@@ -239,20 +245,23 @@ int launch_step_many(const float* state_in, const void* actions, int dtype, uint
   return with_action_type(dtype, [&](auto tag) {
     using A = std::remove_const_t<std::remove_pointer_t<decltype(tag)>>;
     const A* a = static_cast<const A*>(actions);
-    auto go = [&](auto sums) {
-      constexpr bool S = decltype(sums)::value;
+    auto go = [&](auto sums, auto seq) {
+      constexpr bool S = decltype(sums)::value, Q = decltype(seq)::value;
+      constexpr int B = Env::kBlock;
       if constexpr (Env::kVec == 4) {
         if (vec) {
-          step_many_kernel<Env, A, 4, S><<<grid_for(n / 4), kThreads, 0, s>>>(
+          step_many_kernel<Env, A, 4, S, Q><<<grid_for(n / 4, B), B, 0, s>>>(
               state_in, a, seed0, T, n, off, state_out, reward_seq, done_seq, reward_sum, done_count);
           return launch_status();
         }
       }
-      step_many_kernel<Env, A, 1, S><<<grid_for(n), kThreads, 0, s>>>(
+      step_many_kernel<Env, A, 1, S, Q><<<grid_for(n, B), B, 0, s>>>(
           state_in, a, seed0, T, n, off, state_out, reward_seq, done_seq, reward_sum, done_count);
       return launch_status();
     };
-    return (reward_sum || done_count) ? go(std::true_type{}) : go(std::false_type{});
+    const bool sums = reward_sum || done_count, seq = reward_seq && done_seq;
+    if (sums) return seq ? go(std::true_type{}, std::true_type{}) : go(std::true_type{}, std::false_type{});
+    return seq ? go(std::false_type{}, std::true_type{}) : go(std::false_type{}, std::false_type{});
   });
 }
 

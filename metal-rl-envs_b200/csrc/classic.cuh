@@ -31,7 +31,7 @@ struct CartPole {
 // One Euler step for a push of `force` (cartpole_np.py:58-77).
 RLENV_D CartPole cartpole_physics(CartPole s, float force) {
   float sn, c;
-  sincosf(s.th, &sn, &c);
+  sincos_fast(s.th, &sn, &c);
   float temp = (force + cp::POLE_MASS_LENGTH * (s.thd * s.thd) * sn) / cp::TOTAL_MASS;
   float th_acc = (cp::G * sn - c * temp) /
                  (cp::HALF_POLE * (cp::FOUR_THIRDS - cp::POLE_MASS * (c * c) / cp::TOTAL_MASS));
@@ -87,8 +87,8 @@ struct AcrobotTrig {
 
 RLENV_D AcrobotTrig acrobot_trig(const Acrobot& s) {
   AcrobotTrig t;
-  sincosf(s.th1, &t.s1, &t.c1);
-  sincosf(s.th2, &t.s2, &t.c2);
+  sincos_fast(s.th1, &t.s1, &t.c1);
+  sincos_fast(s.th2, &t.s2, &t.c2);
   return t;
 }
 
@@ -114,7 +114,6 @@ RLENV_D Acrobot acrobot_dsdt(const Acrobot& s, const AcrobotTrig& t, float torqu
   return Acrobot{s.dth1, s.dth2, dd1, dd2};
 }
 
-// Angle to [-pi, pi) without branches (acrobot_np.py:88-90).
 // Angle to [-pi, pi) (acrobot_np.py:87-89).
 RLENV_D float wrap_angle(float x) { return wrap_to_pi(x); }
 

@@ -140,6 +140,82 @@ RLENV_D float wrap_to_pi(float x) {
   return x - kTwoPi * f;
 }
 
+// ---------------------------------------------------------------------------
+// Sine and cosine of one angle, for the physics kernels (every angle a step
+// forms is within a few tens of radians of zero).
+// - Reduction by pi/2 after Cody & Waite (1980): k = rint(2x/pi) by the 1.5 * 2^23
+//   rounding constant, whose low mantissa bits are then k mod 4; r = x - k pi/2 with
+//   pi/2 in three float32 parts. With fused multiply-adds the first part's step is
+//   exact, so r carries at most half an ulp of rounding.
+// - sin r = r + r^3 P(r^2) and cos r = 1 + r^2 (-1/2 + r^2 Q(r^2)), P and Q quadratics
+//   fitted for least maximum relative error on |r| <= 1.02 pi/4 (trig_coeffs.py
+//   derives every constant below; a test checks they match).
+// - Both results are within 1.6 ulp of the exact values for |x| <= 1024 (float32
+//   numpy's own sin and cos are within 1.5). Beyond that, and for NaN and infinities,
+//   sincosf answers.
+namespace trig {
+constexpr float kTwoOverPi = 6.3661975e-01f;
+constexpr float kPio2Hi = 1.5707964e+00f;
+constexpr float kPio2Mid = -4.371139e-08f;
+constexpr float kPio2Lo = -1.7151245e-15f;
+constexpr float kSin1 = -1.6666654e-01f;
+constexpr float kSin2 = 8.332063e-03f;
+constexpr float kSin3 = -1.9502117e-04f;
+constexpr float kCos1 = 4.166664e-02f;
+constexpr float kCos2 = -1.3887185e-03f;
+constexpr float kCos3 = 2.441811e-05f;
+constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+constexpr float kFastLimit = 1024.0f;
+}  // namespace trig
+
+// Where the rare branch finds sincosf. kShared: one out-of-line copy per kernel,
+// the smaller code (on a B200 the Acrobot T-step kernel runs 5% faster with it).
+// kInline: a copy at every call site, for kernels at a register limit (the call's
+// preserved registers take the legged C = 4 kernel from 128 to 133 registers, and
+// from four resident blocks per SM to three).
+enum class TrigFar { kShared, kInline };
+
+static __device__ __noinline__ float2 sincos_far(float x) {
+  float2 sc;
+  sincosf(x, &sc.x, &sc.y);
+  return sc;
+}
+
+template <TrigFar kFar = TrigFar::kShared>
+RLENV_D void sincos_fast(float x, float* s, float* c) {
+  if (!(fabsf(x) <= trig::kFastLimit)) {
+    if constexpr (kFar == TrigFar::kShared) {
+      const float2 sc = sincos_far(x);
+      *s = sc.x;
+      *c = sc.y;
+    } else {
+      sincosf(x, s, c);
+    }
+    return;
+  }
+  const float j = fmaf(x, trig::kTwoOverPi, trig::kRound);
+  const float k = j - trig::kRound;
+  const uint32_t quadrant = __float_as_uint(j);
+  float r = fmaf(-k, trig::kPio2Hi, x);
+  r = fmaf(-k, trig::kPio2Mid, r);
+  r = fmaf(-k, trig::kPio2Lo, r);
+  const float r2 = r * r;
+  const float ps = fmaf(fmaf(r2, trig::kSin3, trig::kSin2), r2, trig::kSin1);
+  const float sr = fmaf(r * r2, ps, r);
+  const float pc = fmaf(fmaf(r2, trig::kCos3, trig::kCos2), r2, trig::kCos1);
+  const float cr = fmaf(r2, fmaf(r2, pc, -0.5f), 1.0f);
+  const bool odd = quadrant & 1u;
+  const float a = odd ? cr : sr, b = odd ? sr : cr;
+  *s = __uint_as_float(__float_as_uint(a) ^ ((quadrant & 2u) << 30));
+  *c = __uint_as_float(__float_as_uint(b) ^ (((quadrant + 1u) & 2u) << 30));
+}
+
+RLENV_D float cos_fast(float x) {
+  float s, c;
+  sincos_fast(x, &s, &c);
+  return c;
+}
+
 // Index of element (i, j), j <= i, of a lower triangle stored row by row.
 RLENV_HD constexpr int tri(int i, int j) { return i * (i + 1) / 2 + j; }
 

@@ -154,7 +154,7 @@ RLENV_D void legged_substep(float (&q)[3 + C], float (&v)[3 + C], const float (&
 #pragma unroll
   for (int k = 0; k < C; ++k) {
     float sa, ca;
-    sincosf(q[2] + q[3 + k], &sa, &ca);
+    sincos_fast<TrigFar::kInline>(q[2] + q[3 + k], &sa, &ca);
     const float ad = v[2] + v[3 + k];
     mi.lca[k] = lg::L * ca;
     mi.lsa[k] = lg::L * sa;

@@ -54,7 +54,7 @@ template <int K, bool PAIRWISE>
 RLENV_D void mm_accel(const float (&th)[K], const float (&om)[K], float torque, float (&acc)[K]) {
   float c[K], s[K];
 #pragma unroll
-  for (int i = 0; i < K; ++i) sincosf(th[i], &s[i], &c[i]);
+  for (int i = 0; i < K; ++i) sincos_fast(th[i], &s[i], &c[i]);
   float L[K * (K + 1) / 2];
   float rhs[K];
 #pragma unroll
@@ -65,7 +65,7 @@ RLENV_D void mm_accel(const float (&th)[K], const float (&om)[K], float torque, 
       const float mu = float(K - (i > j ? i : j));
       float cd, sd;
       if (PAIRWISE) {
-        sincosf(th[i] - th[j], &sd, &cd);
+        sincos_fast(th[i] - th[j], &sd, &cd);
       } else {
         cd = c[i] * c[j] + s[i] * s[j];
         sd = s[i] * c[j] - c[i] * s[j];
@@ -146,7 +146,7 @@ __device__ __noinline__ void aba_accel_loops(const float* th, const float* om, f
   for (int i = 1; i < K; ++i) {
     const float qd = om[i] - om[i - 1];
     float s, c;
-    sincosf(th[i] - th[i - 1], &s, &c);
+    sincos_fast(th[i] - th[i - 1], &s, &c);
     sn[i] = s;
     cs[i] = c;
     const float pw = vw[i - 1], px = vx[i - 1], xy = vy[i - 1] + pw;
@@ -202,7 +202,7 @@ __device__ __noinline__ void aba_accel_loops(const float* th, const float* om, f
     uu[0] = torque - ((x * fy - y * x) + carry_p0);
   }
   float sn0, cs0;
-  sincosf(th[0], &sn0, &cs0);
+  sincos_fast(th[0], &sn0, &cs0);
   float ax = cs0 * -pd::G + om[0] * vy[0];
   float ay = -sn0 * -pd::G - om[0] * vx[0];
   const float qdd = (uu[0] - (U0[0] * 0.0f + U1[0] * ax + U2[0] * ay)) / U0[0];
@@ -235,7 +235,7 @@ RLENV_D void aba_accel_unrolled(const float* th, const float* om, float torque, 
   vy[0] = 0.0f;
   for_links<1, K, true, true>([&](int i) {
     const float qd = om[i] - om[i - 1];
-    sincosf(th[i] - th[i - 1], &sn[i], &cs[i]);
+    sincos_fast(th[i] - th[i - 1], &sn[i], &cs[i]);
     const float pw = vw[i - 1], px = vx[i - 1], xy = vy[i - 1] + pw;  // joint at (1, 0)
     vw[i] = pw + qd;
     vx[i] = cs[i] * px + sn[i] * xy;
@@ -297,7 +297,7 @@ RLENV_D void aba_accel_unrolled(const float* th, const float* om, float torque, 
   // outward: accelerations, the base accelerating at -G; the absolute angular
   // accelerations are the running sum of the joint accelerations
   float sn0, cs0;
-  sincosf(th[0], &sn0, &cs0);
+  sincos_fast(th[0], &sn0, &cs0);
   const float qd0 = om[0];
   // root: X_0 maps the base acceleration (0, -G, 0); r = 0
   float ax = cs0 * -pd::G + qd0 * vy[0];
@@ -367,7 +367,7 @@ RLENV_D void pendulum_rk4(float (&th)[K], float (&om)[K], float torque, Accel ac
 template <int K, bool UNROLL>
 RLENV_D bool pendulum_terminated(const float (&th)[K]) {
   float h = 0.0f;
-  for_range<K, UNROLL>([&](int j) { h += cosf(th[j]); });
+  for_range<K, UNROLL>([&](int j) { h += cos_fast(th[j]); });
   return -h > float(K) * 0.5f;
 }
 

@@ -90,7 +90,7 @@ RLENV_D float seg_sum(float v) {
 template <int K>
 RLENV_D float coop_accel(float th_j, float om_j, float torque, int j) {
   float sj, cj;
-  sincosf(th_j, &sj, &cj);
+  sincos_fast(th_j, &sj, &cj);
   float Lr[K];
   float r = 0.0f;
 #pragma unroll
@@ -166,7 +166,7 @@ pendulum_coop_kernel(const float* __restrict__ state, const void* __restrict__ a
     const float a4 = coop_accel<K>(ts, os, torque, j);
     th = pd_wrap(th + pd::SIXTH_DT * (dth + os));
     om = fminf(fmaxf(om + pd::SIXTH_DT * (dom + a4), -pd::MAX_VEL), pd::MAX_VEL);
-    const bool d = -seg_sum<K>(cosf(th)) > float(K) * 0.5f;
+    const bool d = -seg_sum<K>(cos_fast(th)) > float(K) * 0.5f;
     if (d) {
       const uint32_t h = env_hash(seed0 + uint32_t(t), off + e);
       th = uniform_pm(pcg_hash(h + uint32_t(j) * kRowStride), pd::RESET_BOUND);

@@ -75,7 +75,7 @@ def _acrobot_derivative(th1, th2, w1, w2, torque):
 
 
 def wrap_angle(x):
-    """To [-pi, pi) without branches (acrobot_np.py:88-90)."""
+    """To [-pi, pi) without branches (acrobot_np.py:87-89)."""
     period = 2 * np.pi
     return x - period * np.floor((x + np.pi) / period)
 

@@ -1,0 +1,83 @@
+"""The kernels' sine and cosine (sincos_fast, csrc/common.cuh) on the device.
+
+Every physics kernel takes its trigonometry from sincos_fast. This checks its error against
+float64 sin and cos, in float32 ulps of the exact value, next to CUDA's sincosf and float32
+numpy on the same inputs. The probe is compiled here from tests/trig_probe.cu.
+"""
+
+import ctypes
+import subprocess
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import PKG, ROOT
+
+pytestmark = pytest.mark.gpu
+
+ULP_BOUND = 1.6  # both results, |x| <= 1024
+
+
+@pytest.fixture(scope="module")
+def probe(tmp_path_factory):
+    import rlenv_build
+
+    so = tmp_path_factory.mktemp("trig") / "trig_probe.so"
+    cmd = [rlenv_build.nvcc(), *rlenv_build.ARCH, "-O3", "-std=c++17", "--expt-relaxed-constexpr",
+           "-shared", "-Xcompiler", "-fPIC", f"-I{ROOT / 'include'}", f"-I{PKG / 'csrc'}",
+           str(ROOT / "tests" / "trig_probe.cu"), "-o", str(so)]
+    subprocess.run(cmd, check=True, capture_output=True)
+    lib = ctypes.CDLL(str(so))
+    lib.trig_probe.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int64]
+
+    def run(x):
+        xd = torch.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()
+        outs = [torch.empty_like(xd) for _ in range(4)]
+        assert lib.trig_probe(xd.data_ptr(), *(o.data_ptr() for o in outs), xd.numel()) == 0
+        return [o.cpu().numpy() for o in outs]
+
+    return run
+
+
+def _ulps(got, exact):
+    spacing = np.spacing(np.abs(exact).astype(np.float32)).astype(np.float64)
+    return np.abs(got.astype(np.float64) - exact) / spacing
+
+
+def _inputs(limit, seed=0):
+    r = np.random.default_rng(seed)
+    near_quadrants = np.arange(-int(limit / (np.pi / 2)), int(limit / (np.pi / 2)) + 1) * (np.pi / 2)
+    near = (near_quadrants[:, None] + np.linspace(-1e-5, 1e-5, 41)[None, :]).ravel()
+    x = np.concatenate([r.uniform(-limit, limit, 4_000_000), np.linspace(-limit, limit, 1_000_001), near])
+    x = x.astype(np.float32)
+    return x[np.abs(x) <= limit]
+
+
+@pytest.mark.parametrize("limit", [np.pi, 40.0, 1024.0])
+def test_sincos_fast_error_in_ulps(probe, limit):
+    x = _inputs(limit)
+    s, c, s_lib, c_lib = probe(x)
+    xs = x.astype(np.float64)
+    es, ec = _ulps(s, np.sin(xs)), _ulps(c, np.cos(xs))
+    lib_s, lib_c = _ulps(s_lib, np.sin(xs)), _ulps(c_lib, np.cos(xs))
+    np_s, np_c = _ulps(np.sin(x), np.sin(xs)), _ulps(np.cos(x), np.cos(xs))
+    print(f"|x| <= {limit}: sin {es.max():.3f} cos {ec.max():.3f} ulp; sincosf {lib_s.max():.3f} "
+          f"{lib_c.max():.3f}; numpy float32 {np_s.max():.3f} {np_c.max():.3f}")
+    assert es.max() <= ULP_BOUND and ec.max() <= ULP_BOUND
+
+
+def test_sincos_fast_outside_the_fast_range_is_sincosf(probe):
+    x = np.array([1024.5, -2000.0, 1e5, -3e7, 1e30, np.inf, -np.inf, np.nan], np.float32)
+    s, c, s_lib, c_lib = probe(x)
+    np.testing.assert_array_equal(s, s_lib)
+    np.testing.assert_array_equal(c, c_lib)
+    assert np.isnan(s[-3:]).all() and np.isnan(c[-3:]).all()
+
+
+def test_sincos_fast_exact_points(probe):
+    x = np.array([0.0, 1e-30, -1e-30, 1e-7], np.float32)
+    s, c, _, _ = probe(x)
+    np.testing.assert_array_equal(s[1:], x[1:])  # sin x = x below half an ulp of x^3/6
+    np.testing.assert_array_equal(c, np.ones(4, np.float32))
+    assert s[0] == 0.0
