@@ -327,14 +327,34 @@ def hbm_peak_gbs():
     return 6650.0, "fallback"
 
 
-def profiled_traffic():
-    """DRAM bytes per launch of the step kernel from the committed ncu summary, if present."""
+def profiled(key):
+    """A figure of the step kernel's committed ncu summary (`key: value` line), if present:
+    traffic_bytes_per_launch (DRAM bytes per full-size launch) or inst_per_env_step
+    (executed thread instructions per environment-step)."""
     f = ROOT / "profiles" / "acrobot_step_many_n262144_t1000.md"
     if f.exists():
         for line in f.read_text().splitlines():
-            if line.startswith("traffic_bytes_per_launch:"):
+            if line.startswith(key + ":"):
                 return float(line.split(":", 1)[1].strip().split()[0])
     return None
+
+
+def profiled_traffic():
+    return profiled("traffic_bytes_per_launch")
+
+
+def issue_view(env_steps_per_s_per_gpu, sm_mhz, sms):
+    """The step kernel against instruction issue, its actual limit: executed thread
+    instructions per second (ncu's count per env-step times the measured rate) over one
+    warp instruction per SM sub-partition per cycle at the sampled SM clock."""
+    inst = profiled("inst_per_env_step")
+    if not inst or not sm_mhz:
+        return None
+    achieved = env_steps_per_s_per_gpu * inst / 1e9
+    peak = sms * 4 * 32 * sm_mhz * 1e6 / 1e9
+    return {"achieved": achieved, "peak": peak, "unit": "G thread-inst/s", "frac": achieved / peak,
+            "inst_per_env_step": inst, "peak_kind": f"{sms} SMs x 4 schedulers x 32 lanes x sampled SM clock",
+            "source": "ncu smsp__inst_executed, profiles/acrobot_step_many_n262144_t1000.md"}
 
 
 def run_ours(args):
@@ -467,6 +487,7 @@ def run_ours(args):
         cpu = {"value": v, "unit": "env steps/s", "cores": cores, "kind": "port",
                "sample": sample + " (single thread, as the reference reports numpy)"}
     achieved = flops / per_launch / 1e12
+    clock_summary = clocks.summary()
     line = {
         "metric": METRIC, "value": value, "unit": "env steps/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * secs_max / args.steps, "higher_is_better": True,
@@ -485,13 +506,15 @@ def run_ours(args):
                      "traffic": traffic, "algorithmic_bytes_per_launch": bytes_per_launch,
                      "hbm": {"achieved": bytes_per_launch / per_launch / 1e9, "peak": hbm, "unit": "GB/s",
                              "frac": bytes_per_launch / per_launch / 1e9 / hbm, "peak_kind": hbm_kind},
+                     "issue": issue_view(n * T / per_launch, clock_summary.get("sm_mhz"),
+                                         torch.cuda.get_device_properties(dev).multi_processor_count),
                      "launch_ms": per_launch * 1e3},
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": "env steps/s", "h2d_bytes_per_step": 4 * 4 * n + T * n,
                 "d2h_bytes_per_step": 4 * 4 * n + 8 * n, "api": "acrobot_metal.step_many", "steps": e2e_steps,
                 "pipelined": "copy stream and compute stream, two steps in flight"},
         "gpu_launches": args.steps,
-        "clocks": clocks.summary(),
+        "clocks": clock_summary,
     }
     print(json.dumps(line), flush=True)
 
