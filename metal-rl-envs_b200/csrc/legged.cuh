@@ -31,44 +31,49 @@ constexpr float ASSIST_DAMPING = 0.1f;
 // friction (stick inside the cone, else slide on its edge), nothing for a
 // contact above the floor, one that would pull, or one already separating.
 // inv_det, inv_dp and inv_dm are 1 / det, 1 / (Ann + mu Atn) and
-// 1 / (Ann - mu Atn), which depend on the block only and so are computed once
-// per substep; a sliding direction whose denominator is not positive has a
-// zero reciprocal, so its normal impulse is zero (the reference's Painleve
-// guard). BRANCHY skips the solve of an airborne contact with a branch (the
-// variant of hopper_metal.py:110) instead of computing it and selecting zero.
+// 1 / (Ann - mu Atn), and slip is Att mu + Atn: they depend on the block only
+// and so are computed once per substep. A sliding direction whose denominator is
+// not positive has a zero reciprocal, so its normal impulse is zero (the
+// reference's Painleve guard). target is the Baumgarte velocity
+// (0.2 / H) max(depth, 0) of a touching foot and -infinity for one above the
+// floor, so that "touching and wn < target" is one comparison. The reference
+// clamps the sliding normal impulses at zero; here they are not clamped, which
+// changes nothing: a result counts only when target - wn > 0, and then both are
+// already non-negative. BRANCHY skips the solve of an airborne contact with a
+// branch (the variant of hopper_metal.py:110) instead of computing it and
+// selecting zero.
 struct ContactConsts {
-  float inv_det, inv_dp, inv_dm;
+  float inv_det, inv_dp, inv_dm, slip, target;
 };
 
-RLENV_D ContactConsts contact_consts(float Att, float Atn, float Ann) {
+RLENV_D ContactConsts contact_consts(float Att, float Atn, float Ann, float depth) {
   const float den_p = Ann + lg::MU * Atn, den_m = Ann - lg::MU * Atn;
   return ContactConsts{1.0f / (Att * Ann - Atn * Atn), den_p > 0.0f ? 1.0f / den_p : 0.0f,
-                       den_m > 0.0f ? 1.0f / den_m : 0.0f};
+                       den_m > 0.0f ? 1.0f / den_m : 0.0f, Att * lg::MU + Atn,
+                       depth >= 0.0f ? lg::BAUMGARTE_OVER_H * depth : -INFINITY};
 }
 
 template <bool BRANCHY>
 RLENV_D void contact_impulse(float Att, float Atn, float Ann, const ContactConsts& k, float wt,
-                             float wn, float depth, float& lt, float& ln) {
-  const bool touching = depth >= 0.0f;
-  if (BRANCHY && !touching) {
+                             float wn, float& lt, float& ln) {
+  if (BRANCHY && k.target == -INFINITY) {
     lt = 0.0f;
     ln = 0.0f;
     return;
   }
-  const float target = lg::BAUMGARTE_OVER_H * fmaxf(depth, 0.0f);
-  const float gap = target - wn;
+  const float gap = k.target - wn;
   const float ln_stick = (Att * gap + Atn * wt) * k.inv_det;
   const float lt_stick = (-Ann * wt - Atn * gap) * k.inv_det;
   const bool sticks = fabsf(lt_stick) <= lg::MU * ln_stick;
-  const float ln_p = fmaxf(gap * k.inv_dp, 0.0f);
-  const float ln_m = fmaxf(gap * k.inv_dm, 0.0f);
-  const float slip_p = wt + (Att * lg::MU + Atn) * ln_p;
+  const float ln_p = gap * k.inv_dp;
+  const float ln_m = gap * k.inv_dm;
+  const float slip_p = wt + k.slip * ln_p;
   const float sgn = slip_p <= 0.0f ? 1.0f : -1.0f;
   const float ln_slide = slip_p <= 0.0f ? ln_p : ln_m;
   const float lt_slide = (lg::MU * sgn) * ln_slide;
   const float l_n = sticks ? ln_stick : ln_slide;
   const float l_t = sticks ? lt_stick : lt_slide;
-  const bool active = touching && l_n > 0.0f && wn < target;
+  const bool active = gap > 0.0f && l_n > 0.0f;
   ln = active ? l_n : 0.0f;
   lt = active ? l_t : 0.0f;
 }
@@ -229,7 +234,7 @@ RLENV_D void legged_substep(float (&q)[3 + C], float (&v)[3 + C], const float (&
     }
     w0t[k] = wt;
     w0n[k] = wn;
-    cc[k] = contact_consts(att[tri(k, k)], atn[k][k], ann[tri(k, k)]);
+    cc[k] = contact_consts(att[tri(k, k)], atn[k][k], ann[tri(k, k)], depth[k]);
   }
   // block projected Gauss-Seidel: each contact solved exactly given the others
   float lt[C], ln[C];
@@ -241,17 +246,21 @@ RLENV_D void legged_substep(float (&q)[3 + C], float (&v)[3 + C], const float (&
   for (int it = 0; it < iters; ++it) {
 #pragma unroll
     for (int k = 0; k < C; ++k) {
-      // the other contacts' contribution first, then the free velocity (legged_np.py:91-94)
-      float st = 0.0f, sn = 0.0f;
+      // the free velocity plus the other contacts' contribution (legged_np.py:91-94), in
+      // two interleaved sums so that the dependency chain is half as long
+      float st0 = w0t[k], sn0 = w0n[k], st1 = 0.0f, sn1 = 0.0f;
 #pragma unroll
-      for (int l = 0; l < C; ++l) {
+      for (int l = 0, j = 0; l < C; ++l) {
         if (l == k) continue;
         const int kl = k > l ? tri(k, l) : tri(l, k);
+        float& st = (j & 1) ? st1 : st0;
+        float& sn = (j & 1) ? sn1 : sn0;
         st += att[kl] * lt[l] + atn[k][l] * ln[l];
         sn += atn[l][k] * lt[l] + ann[kl] * ln[l];
+        ++j;
       }
-      contact_impulse<BRANCHY>(att[tri(k, k)], atn[k][k], ann[tri(k, k)], cc[k], w0t[k] + st,
-                               w0n[k] + sn, depth[k], lt[k], ln[k]);
+      contact_impulse<BRANCHY>(att[tri(k, k)], atn[k][k], ann[tri(k, k)], cc[k], st0 + st1,
+                               sn0 + sn1, lt[k], ln[k]);
     }
   }
   // v = v_free + M^-1 J^T lambda
