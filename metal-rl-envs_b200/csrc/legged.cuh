@@ -195,10 +195,14 @@ RLENV_D void legged_substep(float (&q)[3 + C], float (&v)[3 + C], const float (&
   // and G[k][l] = g_k . S^-1 g_l (S's upper block), the blocks of contacts k, l are
   //   Att = lsa_k lsa_l G + [k = l] lca_k^2 / D,  Atn = -lsa_k lca_l G + [k = l] lca_k lsa_k / D,
   //   Ann = lca_k lca_l G + [k = l] lsa_k^2 / D   (Atn[k][l] pairs k's tangent with l's normal).
-  // Att and Ann are kept as packed lower triangles over the contacts, Atn in full.
+  // Off the diagonal a block is rank one: contact l's impulse (lt_l, ln_l) adds
+  // (lsa_k, -lca_k) G[k][l] P_l to contact k's relative velocity, where
+  // P_l = lsa_l lt_l - lca_l ln_l. So the sweeps keep G below the diagonal (packed,
+  // G[k][l] at tri(k - 1, l)), the running P_l and the diagonal blocks.
   constexpr float kInvD = 1.0f / (lg::M_F * lg::L * lg::L);
   constexpr float kInvL2 = 1.0f / (lg::L * lg::L);
-  float att[C * (C + 1) / 2], ann[C * (C + 1) / 2], atn[C][C];
+  float gkl[C * (C - 1) / 2 + 1];
+  float dtt[C], dtn[C], dnn[C];
   {
     float h0[C], h1[C];  // S^-1 g_l
 #pragma unroll
@@ -211,12 +215,14 @@ RLENV_D void legged_substep(float (&q)[3 + C], float (&v)[3 + C], const float (&
     for (int k = 0; k < C; ++k) {
       const float g0 = lsa[k] * kInvL2, g1 = -lca[k] * kInvL2;
 #pragma unroll
-      for (int l = 0; l < C; ++l) {
+      for (int l = 0; l <= k; ++l) {
         const float gam = g0 * h0[l] + g1 * h1[l];
-        atn[k][l] = -lsa[k] * lca[l] * gam + (k == l ? lca[k] * lsa[k] * kInvD : 0.0f);
-        if (l <= k) {
-          att[tri(k, l)] = lsa[k] * lsa[l] * gam + (k == l ? lca[k] * lca[k] * kInvD : 0.0f);
-          ann[tri(k, l)] = lca[k] * lca[l] * gam + (k == l ? lsa[k] * lsa[k] * kInvD : 0.0f);
+        if (l < k) {
+          gkl[tri(k - 1, l)] = gam;
+        } else {
+          dtt[k] = lsa[k] * lsa[k] * gam + lca[k] * lca[k] * kInvD;
+          dtn[k] = -lsa[k] * lca[k] * gam + lca[k] * lsa[k] * kInvD;
+          dnn[k] = lca[k] * lca[k] * gam + lsa[k] * lsa[k] * kInvD;
         }
       }
     }
@@ -234,33 +240,32 @@ RLENV_D void legged_substep(float (&q)[3 + C], float (&v)[3 + C], const float (&
     }
     w0t[k] = wt;
     w0n[k] = wn;
-    cc[k] = contact_consts(att[tri(k, k)], atn[k][k], ann[tri(k, k)], depth[k]);
+    cc[k] = contact_consts(dtt[k], dtn[k], dnn[k], depth[k]);
   }
   // block projected Gauss-Seidel: each contact solved exactly given the others
-  float lt[C], ln[C];
+  float lt[C], ln[C], pl[C];
 #pragma unroll
   for (int k = 0; k < C; ++k) {
     lt[k] = 0.0f;
     ln[k] = 0.0f;
+    pl[k] = 0.0f;
   }
   for (int it = 0; it < iters; ++it) {
 #pragma unroll
     for (int k = 0; k < C; ++k) {
-      // the free velocity plus the other contacts' contribution (legged_np.py:91-94), in
-      // two interleaved sums so that the dependency chain is half as long
-      float st0 = w0t[k], sn0 = w0n[k], st1 = 0.0f, sn1 = 0.0f;
+      // the free velocity plus the other contacts' contribution (legged_np.py:91-94)
+      float wt = w0t[k], wn = w0n[k];
+      if constexpr (C > 1) {
+        float sum = 0.0f;
 #pragma unroll
-      for (int l = 0, j = 0; l < C; ++l) {
-        if (l == k) continue;
-        const int kl = k > l ? tri(k, l) : tri(l, k);
-        float& st = (j & 1) ? st1 : st0;
-        float& sn = (j & 1) ? sn1 : sn0;
-        st += att[kl] * lt[l] + atn[k][l] * ln[l];
-        sn += atn[l][k] * lt[l] + ann[kl] * ln[l];
-        ++j;
+        for (int l = 0; l < C; ++l) {
+          if (l != k) sum += gkl[k > l ? tri(k - 1, l) : tri(l - 1, k)] * pl[l];
+        }
+        wt = fmaf(lsa[k], sum, wt);
+        wn = fmaf(-lca[k], sum, wn);
       }
-      contact_impulse<BRANCHY>(att[tri(k, k)], atn[k][k], ann[tri(k, k)], cc[k], st0 + st1,
-                               sn0 + sn1, lt[k], ln[k]);
+      contact_impulse<BRANCHY>(dtt[k], dtn[k], dnn[k], cc[k], wt, wn, lt[k], ln[k]);
+      if constexpr (C > 1) pl[k] = lsa[k] * lt[k] - lca[k] * ln[k];
     }
   }
   // v = v_free + M^-1 J^T lambda

@@ -48,24 +48,33 @@ def aba_flops(k):
 
 
 def legged_flops(c, iters=8):
-    """Per step of the legged body (4 substeps) as csrc/legged.cuh computes it: the mass matrix
-    solved in closed form (arrowhead structure: legs eliminated first, a 2x2 Schur block), the
-    Delassus matrix from the same closed form. Per substep with n = 3 + C: leg kinematics 12C;
-    Schur block 6C + 12; generalised forces 15C + 12; two mass solves 2 (14C + 7); free velocity
-    and update 5n; Delassus 9C^2 + 19C; free relative velocities 10C; per-contact constants 10C;
-    per sweep and contact the other contacts' contribution 8(C - 1) and the exact impulse about
-    40 (the same count as legged_reference_flops: it is the same code); J^T lambda 9C.
+    """Per step of the legged body (4 substeps) as csrc/legged.cuh computes it.
+    - The mass matrix is solved in closed form: an arrowhead structure, with the legs
+      eliminated first and then a 2x2 Schur block.
+    - The Delassus blocks come from the same closed form. Off the diagonal they are rank
+      one, so the sweeps carry G[k][l] and one scalar P_l per contact instead of the full
+      2x2 blocks.
+    Per substep, with n = 3 + C:
+    - leg kinematics 12C; Schur block 6C + 12; generalised forces 15C + 12;
+    - two mass solves 2 (14C + 7); free velocity and update 5n;
+    - Delassus, the diagonal blocks in full and G below the diagonal, 1.5C^2 + 24.5C;
+    - free relative velocities 10C; per-contact constants (three reciprocals, the slip
+      coefficient, the Baumgarte target) 14C;
+    - per sweep and contact: the other contacts' contribution 2(C - 1) + 4, the exact impulse
+      about 38 and the contact's P 3;
+    - J^T lambda 9C.
     Transcendentals: C sines and cosines, 3C + 1 reciprocals."""
     n = 3 + c
-    sub = (12 * c + 6 * c + 12 + 15 * c + 12 + 2 * (14 * c + 7) + 5 * n + 9 * c * c + 19 * c + 10 * c + 10 * c
-           + iters * c * (8 * (c - 1) + 40) + 9 * c)
+    sub = (12 * c + 6 * c + 12 + 15 * c + 12 + 2 * (14 * c + 7) + 5 * n + 1.5 * c * c + 24.5 * c + 10 * c
+           + 14 * c + iters * c * (2 * (c - 1) + 4 + 38 + 3) + 9 * c)
     return dict(flops=round(4 * sub), transcendentals=4 * (2 * c + 3 * c + 1))
 
 
 def legged_reference_flops(c, iters=8):
     """The same step as the reference computes it (legged_np.py:57-97): the dense (3+C)^2 mass
     matrix, its Cholesky factor and 2C + 1 dense solves, the Delassus blocks from the solves;
-    the Gauss-Seidel sweeps as above. For comparison only: the kernel does the closed form."""
+    the Gauss-Seidel sweeps over the full 2x2 blocks, 8(C - 1) + 40 per sweep and contact.
+    For comparison only: the kernel does the closed form."""
     n = 3 + c
     sub = (10 * c + (n * (n + 1) // 2) * 2 * c + 8 * n * c + n ** 3 / 3 + (2 * c + 1) * 2 * n * n
            + 24 * c * c + 12 * c + iters * c * (8 * (c - 1) + 40) + 4 * n * c + 4 * n)
