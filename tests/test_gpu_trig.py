@@ -75,6 +75,15 @@ def test_sincos_fast_outside_the_fast_range_is_sincosf(probe):
     assert np.isnan(s[-3:]).all() and np.isnan(c[-3:]).all()
 
 
+def test_sincos_fast_branch_placements_agree(probe):
+    """The out-of-line (kShared) and inline (kInline) placements of sincosf's branch give the
+    same bits on both sides of 1,024 rad (the probe turns a mismatch into NaN)."""
+    r = np.random.default_rng(1)
+    x = np.concatenate([r.uniform(-2048, 2048, 1_000_000), r.uniform(-1e6, 1e6, 10_000)]).astype(np.float32)
+    s, _, _, _ = probe(x)
+    assert not np.isnan(s).any()
+
+
 def test_sincos_fast_exact_points(probe):
     x = np.array([0.0, 1e-30, -1e-30, 1e-7], np.float32)
     s, c, _, _ = probe(x)
