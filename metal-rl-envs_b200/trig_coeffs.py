@@ -1,4 +1,4 @@
-"""Constants of the kernels' sine/cosine (``sincos_fast`` in csrc/common.cuh).
+"""Constants of the kernels' sine/cosine (``sincos_fast`` and ``sincos_sfu`` in csrc/common.cuh).
 
 Run as a script, this prints the C++ constants. tests/test_trig_coeffs.py checks that the
 header holds exactly these values.
@@ -38,6 +38,14 @@ def pio2_parts():
     return parts
 
 
+def two_pi_parts():
+    """2 pi as hi + lo, two float32s, for the reduction before the special function unit."""
+    with mp.workdps(60):
+        hi = np.float32(float(2 * mp.pi))
+        lo = np.float32(float(2 * mp.pi - mp.mpf(float(hi))))
+    return hi, lo
+
+
 def _lawson(target, powers, weight, xs):
     basis = np.array([[x ** p for p in powers] for x in xs])
     y = np.array([target(x) for x in xs])
@@ -69,6 +77,8 @@ def constants():
     out = {"kTwoOverPi": np.float32(2.0 / np.pi), "kPio2Hi": hi, "kPio2Mid": mid, "kPio2Lo": lo}
     out.update({f"kSin{i}": v for i, v in enumerate(p, 1)})
     out.update({f"kCos{i}": v for i, v in enumerate(q, 1)})
+    hi2, lo2 = two_pi_parts()
+    out.update({"kInvTwoPi": np.float32(1.0 / (2.0 * np.pi)), "kTwoPiHi": hi2, "kTwoPiLo": lo2})
     return out
 
 
