@@ -43,6 +43,13 @@ RLENV_D void for_range(F&& f) {
 // K-link arrays stay in registers (fully unrolled loops) up to this size.
 constexpr int kUnrollLinks = 16;
 
+// Every acceleration evaluation (the four RK4 stages) takes its sines and cosines from
+// the special function unit (sincos_sfu, within 5.9e-7 absolute); the derivatives enter
+// the step weighted by dt / 6 and dt / 3. Termination, which the done flags must get
+// exactly right, uses cos_fast (within 1.6 ulp). The reference's Metal kernels call
+// Metal's default fast-math sin and cos (pendulum_metal.py:27, 98-102;
+// pendulum_aba_metal.py:34, 61, 74).
+
 // ---- mass-matrix accelerations (pendulum_np.py:68-111) ---------------------
 // M_ij = mu_ij cos(t_i - t_j), mu_ij = K - max(i, j); rhs_i = -sum_j mu_ij
 // sin(t_i - t_j) w_j^2 - G mu_ii sin t_i (+ torque at the root); M acc = rhs by
@@ -54,7 +61,7 @@ template <int K, bool PAIRWISE>
 RLENV_D void mm_accel(const float (&th)[K], const float (&om)[K], float torque, float (&acc)[K]) {
   float c[K], s[K];
 #pragma unroll
-  for (int i = 0; i < K; ++i) sincos_fast(th[i], &s[i], &c[i]);
+  for (int i = 0; i < K; ++i) sincos_sfu(th[i], &s[i], &c[i]);
   float L[K * (K + 1) / 2];
   float rhs[K];
 #pragma unroll
@@ -65,7 +72,7 @@ RLENV_D void mm_accel(const float (&th)[K], const float (&om)[K], float torque, 
       const float mu = float(K - (i > j ? i : j));
       float cd, sd;
       if (PAIRWISE) {
-        sincos_fast(th[i] - th[j], &sd, &cd);
+        sincos_sfu(th[i] - th[j], &sd, &cd);
       } else {
         cd = c[i] * c[j] + s[i] * s[j];
         sd = s[i] * c[j] - c[i] * s[j];
@@ -146,7 +153,7 @@ __device__ __noinline__ void aba_accel_loops(const float* th, const float* om, f
   for (int i = 1; i < K; ++i) {
     const float qd = om[i] - om[i - 1];
     float s, c;
-    sincos_fast(th[i] - th[i - 1], &s, &c);
+    sincos_sfu(th[i] - th[i - 1], &s, &c);
     sn[i] = s;
     cs[i] = c;
     const float pw = vw[i - 1], px = vx[i - 1], xy = vy[i - 1] + pw;
@@ -202,7 +209,7 @@ __device__ __noinline__ void aba_accel_loops(const float* th, const float* om, f
     uu[0] = torque - ((x * fy - y * x) + carry_p0);
   }
   float sn0, cs0;
-  sincos_fast(th[0], &sn0, &cs0);
+  sincos_sfu(th[0], &sn0, &cs0);
   float ax = cs0 * -pd::G + om[0] * vy[0];
   float ay = -sn0 * -pd::G - om[0] * vx[0];
   const float qdd = (uu[0] - (U0[0] * 0.0f + U1[0] * ax + U2[0] * ay)) / U0[0];
@@ -235,7 +242,7 @@ RLENV_D void aba_accel_unrolled(const float* th, const float* om, float torque, 
   vy[0] = 0.0f;
   for_links<1, K, true, true>([&](int i) {
     const float qd = om[i] - om[i - 1];
-    sincos_fast(th[i] - th[i - 1], &sn[i], &cs[i]);
+    sincos_sfu(th[i] - th[i - 1], &sn[i], &cs[i]);
     const float pw = vw[i - 1], px = vx[i - 1], xy = vy[i - 1] + pw;  // joint at (1, 0)
     vw[i] = pw + qd;
     vx[i] = cs[i] * px + sn[i] * xy;
@@ -297,7 +304,7 @@ RLENV_D void aba_accel_unrolled(const float* th, const float* om, float torque, 
   // outward: accelerations, the base accelerating at -G; the absolute angular
   // accelerations are the running sum of the joint accelerations
   float sn0, cs0;
-  sincos_fast(th[0], &sn0, &cs0);
+  sincos_sfu(th[0], &sn0, &cs0);
   const float qd0 = om[0];
   // root: X_0 maps the base acceleration (0, -G, 0); r = 0
   float ax = cs0 * -pd::G + qd0 * vy[0];
