@@ -199,6 +199,7 @@ def write_dict_csv(rows, path):
     """The reference's ES writer (bench_ppo.py:37-41): a header of the first row's keys in
     their order, then one line per row."""
     columns = list(rows[0].keys())
+    Path(path).parent.mkdir(parents=True, exist_ok=True)
     with open(path, "w", newline="") as out:
         writer = csv.writer(out)
         writer.writerow(columns)
