@@ -257,10 +257,15 @@ RLENV_API int rlenv_es_centered_ranks_sorted(const float* fitness, int64_t p, fl
                                              void* scratch, int64_t scratch_bytes, void* stream);
 
 /* rlenv_es_centered_ranks_sorted for callers that cannot allocate device
- * memory: no counterpart in the reference, which has no such caller. It
- * allocates nothing; its scratch is a fixed 1 MiB array inside the library
- * (per device), so 2 <= p <= 65,536 and larger p is rejected with
- * RLENV_EINVAL. Nothing in the array needs to start at zero. Calls on one
+ * memory: no counterpart in the reference, which has no such caller. Such
+ * callers include code running inside a memory pool or allocator that forbids
+ * further allocation, a framework that hands out only its own buffers, and
+ * steps that must not add allocation latency or fragmentation. It allocates
+ * nothing; its scratch is a fixed 1 MiB array inside the library (per device,
+ * held until the process exits), so 2 <= p <= 65,536 and larger p is rejected
+ * with RLENV_EINVAL. The first call on each device, with that device current,
+ * looks up the array's device address once; make that first call before any
+ * stream capture. Nothing in the array needs to start at zero. Calls on one
  * device whose executions overlap (different streams or host threads) share
  * the array and race; issue them on one stream. Same ranks, bit for bit, as
  * the other two rank entry points. */
