@@ -145,7 +145,10 @@ RLENV_D void for_links(F&& f) {
 template <int K>
 __device__ __noinline__ void aba_accel_loops(const float* th, const float* om, float torque,
                                              float* acc) {
-  float vw[K], vx[K], vy[K], sn[K], cs[K], U0[K], U1[K], U2[K], uu[K], iD[K];
+  // Seven per-link arrays in local memory. The inward pass overwrites what the last pass no
+  // longer needs: vw becomes u / D, vx and vy the velocity-product terms -qd vx and qd vy,
+  // and U1r, U2r hold U1 / D and U2 / D (U0 / D is 1: D = U0).
+  float vw[K], vx[K], vy[K], sn[K], cs[K], U1r[K], U2r[K];
   vw[0] = om[0];
   vx[0] = 0.0f;
   vy[0] = 0.0f;
@@ -174,16 +177,16 @@ __device__ __noinline__ void aba_accel_loops(const float* th, const float* om, f
     const float p0 = (x * fy - y * x) + carry_p0, p1 = (-w * fy) + carry_p1, p2 = (w * x) + carry_p2;
     const float a00 = 1.0f + carry_I00, a01 = carry_I01, a02 = 1.0f + carry_I02;
     const float a11 = 1.0f + carry_I11, a12 = carry_I12, a22 = 1.0f + carry_I22;
-    U0[i] = a00;
-    U1[i] = a01;
-    U2[i] = a02;
-    uu[i] = -p0;
     const float r = 1.0f / a00;
-    iD[i] = r;
     const float Ia00 = a00 - a00 * a00 * r, Ia01 = a01 - a00 * a01 * r, Ia02 = a02 - a00 * a02 * r;
     const float Ia11 = a11 - a01 * a01 * r, Ia12 = a12 - a01 * a02 * r, Ia22 = a22 - a02 * a02 * r;
     const float c1 = qd * y, c2 = -qd * x;
-    const float g = uu[i] * r;
+    const float g = -p0 * r;
+    vw[i] = g;
+    vx[i] = c2;
+    vy[i] = c1;
+    U1r[i] = a01 * r;
+    U2r[i] = a02 * r;
     const float pa0 = p0 + (Ia01 * c1 + Ia02 * c2) + a00 * g;
     const float pa1 = p1 + (Ia11 * c1 + Ia12 * c2) + a01 * g;
     const float pa2 = p2 + (Ia12 * c1 + Ia22 * c2) + a02 * g;
@@ -201,27 +204,22 @@ __device__ __noinline__ void aba_accel_loops(const float* th, const float* om, f
     carry_p1 = c * pa1 - s * pa2;
     carry_p2 = s * pa1 + c * pa2;
   }
-  {
-    const float w = vw[0], x = vx[0], y = vy[0], fy = w + y;
-    U0[0] = 1.0f + carry_I00;
-    U1[0] = carry_I01;
-    U2[0] = 1.0f + carry_I02;
-    uu[0] = torque - ((x * fy - y * x) + carry_p0);
-  }
+  const float w0 = vw[0], x0 = vx[0], y0 = vy[0], fy0 = w0 + y0;
+  const float U0_0 = 1.0f + carry_I00, U1_0 = carry_I01, U2_0 = 1.0f + carry_I02;
+  const float uu0 = torque - ((x0 * fy0 - y0 * x0) + carry_p0);
   float sn0, cs0;
   sincos_sfu(th[0], &sn0, &cs0);
-  float ax = cs0 * -pd::G + om[0] * vy[0];
-  float ay = -sn0 * -pd::G - om[0] * vx[0];
-  const float qdd = (uu[0] - (U0[0] * 0.0f + U1[0] * ax + U2[0] * ay)) / U0[0];
+  float ax = cs0 * -pd::G + om[0] * y0;
+  float ay = -sn0 * -pd::G - om[0] * x0;
+  const float qdd = (uu0 - (U0_0 * 0.0f + U1_0 * ax + U2_0 * ay)) / U0_0;
   float aw = 0.0f + qdd, run = qdd;
   acc[0] = run;
 #pragma unroll 8
   for (int i = 1; i < K; ++i) {
-    const float qd = om[i] - om[i - 1];
     const float xy = ay + aw;
-    const float ap1 = cs[i] * ax + sn[i] * xy + qd * vy[i];
-    const float ap2 = -sn[i] * ax + cs[i] * xy - qd * vx[i];
-    const float q2 = (uu[i] - (U0[i] * aw + U1[i] * ap1 + U2[i] * ap2)) * iD[i];
+    const float ap1 = cs[i] * ax + sn[i] * xy + vy[i];
+    const float ap2 = -sn[i] * ax + cs[i] * xy + vx[i];
+    const float q2 = vw[i] - aw - U1r[i] * ap1 - U2r[i] * ap2;
     aw = aw + q2;
     ax = ap1;
     ay = ap2;
