@@ -232,8 +232,10 @@ __device__ __noinline__ void aba_accel_loops(const float* th, const float* om, f
 template <int K>
 RLENV_D void aba_accel_unrolled(const float* th, const float* om, float torque, float* acc) {
   // per link: velocity, the joint rotation's sine and cosine (evaluated once, used by all three
-  // passes), U = I^A S, u and 1 / D
-  float vw[K], vx[K], vy[K], sn[K], cs[K], U0[K], U1[K], U2[K], uu[K], iD[K];
+  // passes); the inward pass then overwrites the velocity with what the last pass needs
+  // (u / D and the velocity-product terms c2 = -qd vx, c1 = qd vy) and keeps U1 / D, U2 / D
+  // (U0 / D is 1: D = U0)
+  float vw[K], vx[K], vy[K], sn[K], cs[K], U1r[K], U2r[K];
   // outward: link velocities v_i = X_i v_{i-1} + S qd_i; the root has v_0 = (qd_0, 0, 0)
   vw[0] = om[0];
   vx[0] = 0.0f;
@@ -246,10 +248,8 @@ RLENV_D void aba_accel_unrolled(const float* th, const float* om, float torque, 
     vx[i] = cs[i] * px + sn[i] * xy;
     vy[i] = -sn[i] * px + cs[i] * xy;
   });
-  // inward: articulated inertia and bias force of the subtree, carried to the
-  // parent as the child's contribution (cA, cp)
-  // Articulated inertia (symmetric 3x3, upper half) and bias force that the child link hands to
-  // its parent in the inward pass; zero below the last link.
+  // inward: articulated inertia (symmetric 3x3, upper half) and bias force of the subtree,
+  // carried to the parent as the child's contribution; zero below the last link
   float carry_I00 = 0.0f, carry_I01 = 0.0f, carry_I02 = 0.0f;
   float carry_I11 = 0.0f, carry_I12 = 0.0f, carry_I22 = 0.0f;
   float carry_p0 = 0.0f, carry_p1 = 0.0f, carry_p2 = 0.0f;
@@ -263,16 +263,16 @@ RLENV_D void aba_accel_unrolled(const float* th, const float* om, float torque, 
     const float p2 = (w * x) + carry_p2;
     const float a00 = 1.0f + carry_I00, a01 = carry_I01, a02 = 1.0f + carry_I02;
     const float a11 = 1.0f + carry_I11, a12 = carry_I12, a22 = 1.0f + carry_I22;
-    U0[i] = a00;
-    U1[i] = a01;
-    U2[i] = a02;
-    uu[i] = -p0;
     const float r = 1.0f / a00;  // D = a00
-    iD[i] = r;
     const float Ia00 = a00 - a00 * a00 * r, Ia01 = a01 - a00 * a01 * r, Ia02 = a02 - a00 * a02 * r;
     const float Ia11 = a11 - a01 * a01 * r, Ia12 = a12 - a01 * a02 * r, Ia22 = a22 - a02 * a02 * r;
     const float c1 = qd * y, c2 = -qd * x;  // c_i = v_i x S qd
-    const float g = uu[i] * r;
+    const float g = -p0 * r;                 // u / D, u = -p0
+    vw[i] = g;
+    vx[i] = c2;
+    vy[i] = c1;
+    U1r[i] = a01 * r;
+    U2r[i] = a02 * r;
     const float pa0 = p0 + (Ia01 * c1 + Ia02 * c2) + a00 * g;
     const float pa1 = p1 + (Ia11 * c1 + Ia12 * c2) + a01 * g;
     const float pa2 = p2 + (Ia12 * c1 + Ia22 * c2) + a02 * g;
@@ -291,32 +291,27 @@ RLENV_D void aba_accel_unrolled(const float* th, const float* om, float torque, 
     carry_p1 = c * pa1 - s * pa2;
     carry_p2 = s * pa1 + c * pa2;
   });
-  {  // root link: its inertia and bias with the whole chain's contribution
-    const float w = vw[0], x = vx[0], y = vy[0];
-    const float fy = w + y;
-    U0[0] = 1.0f + carry_I00;
-    U1[0] = carry_I01;
-    U2[0] = 1.0f + carry_I02;
-    uu[0] = torque - ((x * fy - y * x) + carry_p0);
-  }
+  // root link: its inertia and bias with the whole chain's contribution
+  const float w0 = vw[0], x0 = vx[0], y0 = vy[0], fy0 = w0 + y0;
+  const float U0_0 = 1.0f + carry_I00, U1_0 = carry_I01, U2_0 = 1.0f + carry_I02;
+  const float uu0 = torque - ((x0 * fy0 - y0 * x0) + carry_p0);
   // outward: accelerations, the base accelerating at -G; the absolute angular
   // accelerations are the running sum of the joint accelerations
   float sn0, cs0;
   sincos_sfu(th[0], &sn0, &cs0);
   const float qd0 = om[0];
   // root: X_0 maps the base acceleration (0, -G, 0); r = 0
-  float ax = cs0 * -pd::G + qd0 * vy[0];
-  float ay = -sn0 * -pd::G - qd0 * vx[0];
-  float qdd = (uu[0] - (U0[0] * 0.0f + U1[0] * ax + U2[0] * ay)) / U0[0];
+  float ax = cs0 * -pd::G + qd0 * y0;
+  float ay = -sn0 * -pd::G - qd0 * x0;
+  const float qdd = (uu0 - (U0_0 * 0.0f + U1_0 * ax + U2_0 * ay)) / U0_0;
   float aw = 0.0f + qdd;
   float run = qdd;
   acc[0] = run;
   for_links<1, K, true, true>([&](int i) {
-    const float qd = om[i] - om[i - 1];
     const float xy = ay + aw;
-    const float ap1 = cs[i] * ax + sn[i] * xy + qd * vy[i];
-    const float ap2 = -sn[i] * ax + cs[i] * xy - qd * vx[i];
-    const float q2 = (uu[i] - (U0[i] * aw + U1[i] * ap1 + U2[i] * ap2)) * iD[i];
+    const float ap1 = cs[i] * ax + sn[i] * xy + vy[i];
+    const float ap2 = -sn[i] * ax + cs[i] * xy + vx[i];
+    const float q2 = vw[i] - aw - U1r[i] * ap1 - U2r[i] * ap2;
     aw = aw + q2;
     ax = ap1;
     ay = ap2;
