@@ -57,13 +57,15 @@ def torques(action, c):
     return [((a // 3**k) % 3 - 1).astype(np.float32) * LG_TORQUE for k in range(c)]
 
 
-def contact_impulse(att, atn, ann, wt, wn, depth, mu=LG_MU):
+def contact_impulse(att, atn, ann, wt, wn, depth, mu=LG_MU, f32=False):
     """Exact single-contact impulse (lt, ln), branch-free (hopper_np.py:80-109): stick when
     the sticking impulse lies in the friction cone, else slide on the cone's edge in the
     direction that opposes the residual slip; nothing above the floor, when pulling, or when
     the free motion already separates. A sliding direction with a non-positive denominator
     (the Painleve regime) contributes nothing. As in the reference, the sliding sign is a
-    float64 array, so lt (and every state it touches afterwards) is float64."""
+    float64 array, so lt (and every state it touches afterwards) is float64. With f32 the sign
+    is float32 and every value stays float32, as in the reference's Metal kernels and its MLX
+    step loop (legged_metal.py:53-71), which its rollout test compares (test_es.py:46-68)."""
     touching = depth >= 0.0
     target = LG_BAUMGARTE / LG_H * np.maximum(depth, 0.0)
     det = att * ann - atn * atn
@@ -74,7 +76,8 @@ def contact_impulse(att, atn, ann, wt, wn, depth, mu=LG_MU):
     ln_p = np.where(dp > 0.0, np.maximum((target - wn) / np.where(dp > 0.0, dp, 1.0), 0.0), 0.0)
     ln_m = np.where(dm > 0.0, np.maximum((target - wn) / np.where(dm > 0.0, dm, 1.0), 0.0), 0.0)
     slip = wt + (att * mu + atn) * ln_p
-    direction = np.where(slip <= 0.0, 1.0, -1.0)
+    one = np.float32(1.0) if f32 else 1.0
+    direction = np.where(slip <= 0.0, one, -one)
     ln_sl = np.where(slip <= 0.0, ln_p, ln_m)
     lt_sl = mu * direction * ln_sl
     ln = np.where(stick, ln_st, ln_sl)
@@ -83,8 +86,9 @@ def contact_impulse(att, atn, ann, wt, wn, depth, mu=LG_MU):
     return np.where(on, lt, 0.0), np.where(on, ln, 0.0)
 
 
-def substep(q, v, tq, c, iters=LG_ITERS, mu=LG_MU, assist=0.0, return_impulses=False):
-    """One substep of 0.01 for C legs (legged_np.py:57-97). q, v: (3+C, N); tq: C arrays."""
+def substep(q, v, tq, c, iters=LG_ITERS, mu=LG_MU, assist=0.0, return_impulses=False, f32=False):
+    """One substep of 0.01 for C legs (legged_np.py:57-97). q, v: (3+C, N); tq: C arrays.
+    f32 keeps every value float32 (see contact_impulse)."""
     n = 3 + c
     z = np.zeros_like(q[0])
     one = z + 1.0
@@ -130,20 +134,21 @@ def substep(q, v, tq, c, iters=LG_ITERS, mu=LG_MU, assist=0.0, return_impulses=F
     for _ in range(iters):
         for k in range(c):
             rel_t, rel_n = w0[k][0] + coupled(k, 0), w0[k][1] + coupled(k, 1)
-            lt[k], ln[k] = contact_impulse(A[k][k][0], A[k][k][1], A[k][k][3], rel_t, rel_n, depth[k], mu)
+            lt[k], ln[k] = contact_impulse(A[k][k][0], A[k][k][1], A[k][k][3], rel_t, rel_n, depth[k], mu, f32)
     vnew = np.stack([vfree[i] + sum(MiJt[k][i] * lt[k] + MiJn[k][i] * ln[k] for k in range(c)) for i in range(n)])
     out = q + LG_H * vnew, vnew
     return out + (np.stack(lt), np.stack(ln)) if return_impulses else out
 
 
-def physics(state, action, c, iters=LG_ITERS, assist=0.0):
-    """Four substeps from state (2(3+C), N) under the decoded per-leg torques (legged_np.py:121-128)."""
+def physics(state, action, c, iters=LG_ITERS, assist=0.0, f32=False):
+    """Four substeps from state (2(3+C), N) under the decoded per-leg torques (legged_np.py:121-128).
+    f32 keeps every value float32 (see contact_impulse)."""
     s = np.asarray(state)
     d = 3 + c
     q, v = s[:d], s[d:]
     tq = torques(action, c)
     for _ in range(LG_SUBSTEPS):
-        q, v = substep(q, v, tq, c, iters, assist=assist)
+        q, v = substep(q, v, tq, c, iters, assist=assist, f32=f32)
     return np.r_[q, v]
 
 

@@ -87,7 +87,9 @@ def legged_action(logits, c):
 
 
 def legged_rollout(state, theta, hidden, horizon, c, alive_bonus=1.0, fall_penalty=0.0, height_gate=0.0,
-                   assist=0.0, iters=legged.LG_ITERS):
+                   assist=0.0, iters=legged.LG_ITERS, f32=False):
+    """f32 runs the physics in float32 throughout (legged.contact_impulse); by default it
+    follows the reference numpy's float64 promotion."""
     s = np.array(state)
     P = s.shape[1]
     theta = _theta_rows(theta, P)
@@ -98,7 +100,7 @@ def legged_rollout(state, theta, hidden, horizon, c, alive_bonus=1.0, fall_penal
         if not alive.any():
             break
         act = legged_action(policy_logits(s[1:].T, theta, hidden, 5 + 2 * c, 3 * c), c)
-        nxt = legged.physics(s, act, c, iters, assist)
+        nxt = legged.physics(s, act, c, iters, assist, f32=f32)
         fell = legged.terminated(nxt)
         steps += alive
         forward = np.where(nxt[1] >= height_gate, nxt[3 + c], 0.0)
