@@ -217,6 +217,19 @@ RLENV_API int rlenv_legged_rollout(int c, int hidden, int horizon, int iters, fl
                          int64_t theta_stride, int64_t p, float* fitness, float* steps,
                          void* stream);
 
+/* The same rollout with the lanes per member chosen by the caller: 1, 2 or 4,
+ * dividing both c and hidden (2 and 4 need c even), or 0 for the library's
+ * choice, which rlenv_legged_rollout uses. Lane l of a member's group owns its
+ * contacts [l c / lanes, (l + 1) c / lanes) and hidden units
+ * [l hidden / lanes, ...); every width gives the same bits, and the same bits as
+ * stepping the body with rlenv_legged_step. The reference runs one thread per
+ * member (legged_rollout_metal.py:19-83); this entry point is for tuning and for
+ * tests of that equality. */
+RLENV_API int rlenv_legged_rollout_lanes(int lanes, int c, int hidden, int horizon, int iters,
+                               float alive, float fall, float gate, float assist,
+                               const float* state, const float* theta, int64_t theta_stride,
+                               int64_t p, float* fitness, float* steps, void* stream);
+
 /* ---- ES generation pieces (es.py:214-227) ------------------------------------
  * Noise: half (rows, d) of standard normals for antithetic pairs
  * [row_offset, row_offset + rows), element (pair, j) a function of

@@ -44,11 +44,17 @@ legged_kernel(const float* __restrict__ state, const void* __restrict__ actions,
   constexpr int nq = 3 + C;
   const int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (e >= n) return;
-  float q[nq], v[nq];
+  float qt[3], vt[3], ql[C], vl[C];  // torso (x, y, phi) and legs (psi_k), with their rates
 #pragma unroll
   for (int i = 0; i < nq; ++i) {
-    q[i] = __ldg(state + i * n + e);
-    v[i] = __ldg(state + (nq + i) * n + e);
+    const float qi = __ldg(state + i * n + e), vi = __ldg(state + (nq + i) * n + e);
+    if (i < 3) {
+      qt[i] = qi;
+      vt[i] = vi;
+    } else {
+      ql[i - 3] = qi;
+      vl[i - 3] = vi;
+    }
   }
   const float k_assist = assist_ptr ? __ldg(assist_ptr) : assist;
   int act = T > 0 ? action_at(actions, dtype, e) : 0;  // loaded one step ahead
@@ -60,22 +66,23 @@ legged_kernel(const float* __restrict__ state, const void* __restrict__ actions,
 #pragma unroll
     for (int k = 0; k < 2 * C; ++k) imp[k] = 0.0f;
 #pragma unroll 1
-    for (int sub = 0; sub < lg::SUBSTEPS; ++sub)
-      legged_substep<C, BRANCHY, IMPULSES>(q, v, tq, k_assist, iters, imp);
+    for (int ss = 0; ss < lg::SUBSTEPS; ++ss)
+      legged_substep<C, 1, BRANCHY, IMPULSES>(qt, vt, ql, vl, tq, k_assist, iters, nullptr, 0, true, imp);
     if constexpr (IMPULSES) {
 #pragma unroll
       for (int k = 0; k < 2 * C; ++k) impulse_seq[(t * 2 * C + k) * n + e] = imp[k];
     }
-    const bool d = legged_terminated<C>(q);
-    const float rw = d ? 0.0f : v[0] + 1.0f;
+    const bool d = legged_terminated(qt);
+    const float rw = d ? 0.0f : vt[0] + 1.0f;
     if (d) {
       const uint32_t h = env_hash(seed0 + uint32_t(t), off + e);
 #pragma unroll
       for (int i = 0; i < 2 * nq; ++i) {
         const float fresh =
             __fadd_rn(__ldg(stand + i), uniform_pm(pcg_hash(h + uint32_t(i) * kRowStride), lg::RESET_BOUND));
-        if (i < nq) q[i] = fresh;
-        else v[i - nq] = fresh;
+        const int j = i < nq ? i : i - nq;
+        float& slot = i < nq ? (j < 3 ? qt[j] : ql[j - 3]) : (j < 3 ? vt[j] : vl[j - 3]);
+        slot = fresh;
       }
     }
     if (reward_seq) reward_seq[t * n + e] = rw;
@@ -83,8 +90,8 @@ legged_kernel(const float* __restrict__ state, const void* __restrict__ actions,
   }
 #pragma unroll
   for (int i = 0; i < nq; ++i) {
-    next[i * n + e] = q[i];
-    next[(nq + i) * n + e] = v[i];
+    next[i * n + e] = i < 3 ? qt[i] : ql[i - 3];
+    next[(nq + i) * n + e] = i < 3 ? vt[i] : vl[i - 3];
   }
 }
 

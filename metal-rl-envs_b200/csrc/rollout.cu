@@ -13,8 +13,8 @@
 // physics on the same inputs, so control flow stays uniform in the group, and
 // the group stops at its member's first termination.
 //
-// Legged: one thread per member; the hidden layer is formed from weights read
-// through the read-only cache, then four substeps of the contact dynamics.
+// Legged: a group of 1, 2 or 4 lanes per member, the policy staged once per block in
+// shared memory, then four substeps of the contact dynamics per step.
 #include "classic.cuh"
 #include "legged.cuh"
 
@@ -141,61 +141,191 @@ acrobot_rollout_kernel(const float* __restrict__ state, const float* __restrict_
   if (valid && lane == 0) fitness[m] = survived;
 }
 
-template <int C, int H>
-__global__ void __launch_bounds__(128)
+// Shared-memory image of a legged member's policy for one lane of its group of G lanes.
+// es.unflatten's row (w1 (OBS, H), b1 (H), w2 (H, OUT), b2 (OUT)) is cut into the slices the
+// lanes use: lane gl forms hidden units [gl U, (gl + 1) U) and the logits of legs
+// [gl CL, (gl + 1) CL), so its slice holds those columns of w1 and b1 ((OBS, U) and U),
+// those outputs' rows of w2, transposed ((3 CL, H)), and their biases. A lane reads only its
+// own slice. The slice stride SL keeps a warp's loads conflict-free: with 128-bit loads a
+// quarter-warp's eight slices start SL / 4 (odd) chunks of 16 bytes apart, eight distinct
+// chunks modulo eight; with scalar loads only, SL is odd. The group's exchange areas
+// (legged.cuh) follow the slices.
+template <int C, int H, int G>
+struct LeggedSlice {
+  static constexpr int OBS = 5 + 2 * C, OUT = 3 * C;
+  static constexpr int B1g = OBS * H, W2g = B1g + H, B2g = W2g + H * OUT;  // in the global row
+  static constexpr int U = H / G, CL = C / G, NO = 3 * CL;
+  static constexpr bool kVec1 = U % 4 == 0, kVec2 = H % 4 == 0;
+  static constexpr int W1 = 0, B1 = OBS * U, W2 = (B1 + U + 3) / 4 * 4, B2 = W2 + NO * H;
+  static constexpr int SL0 = B2 + NO;
+  static constexpr int SL4 = (SL0 + 3) / 4 * 4;
+  static constexpr int SL = (kVec1 || kVec2) ? ((SL4 / 4) % 2 ? SL4 : SL4 + 4) : (SL0 % 2 ? SL0 : SL0 + 1);
+  static constexpr int kMembers = 32 / G;  // one warp per block
+  static constexpr int XS = G > 1 ? lgx::xch_floats<C, H>() : 0;  // exchange floats per member
+  static constexpr size_t kSmem = (size_t(32) * SL + size_t(kMembers) * XS) * sizeof(float);
+};
+
+// A group of G lanes per member (G divides C and H): lane gl owns C / G contacts and legs
+// (legged_substep) and H / G hidden units. A block is one warp of 32 / G members whose
+// policy slices are staged once into shared memory (LeggedSlice), so that the per-step
+// weight reads are conflict-free shared loads rather than 32-row gathers through L1. Each
+// step: the MLP on the state without x (legged_rollout_metal.py:36-51: bias first, then the
+// inputs in order; each lane forms its hidden units whole and its legs' logits whole from
+// the gathered hidden layer, so no sum depends on G), one three-way head per leg with the
+// first index winning ties, four contact substeps, termination, and the shaped reward
+// (legged_rollout_metal.py:52-55). Every lane stays in the loop until the last member of its
+// warp has fallen (finished members keep stepping, unrecorded), so the exchanges and the
+// warp-wide votes of the substep's contact skipping always see 32 lanes.
+template <int C, int H, int G>
+__global__ void __launch_bounds__(32)
 legged_rollout_kernel(const float* __restrict__ state, const float* __restrict__ theta,
                       int64_t stride, int64_t p, int horizon, int iters, float alive_bonus,
                       float fall_penalty, float gate, float assist, float* __restrict__ fitness,
                       float* __restrict__ steps) {
-  constexpr int nq = 3 + C, OBS = 5 + 2 * C, OUT = 3 * C;
-  constexpr int B1 = OBS * H, W2 = B1 + H, B2 = W2 + H * OUT;
-  const int64_t m = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (m >= p) return;
-  const float* __restrict__ row = theta + m * stride;
-  float q[nq], v[nq];
+  using R = LeggedSlice<C, H, G>;
+  using namespace lgx;
+  constexpr int nq = 3 + C, OBS = R::OBS, U = R::U, CL = R::CL, NO = R::NO;
+  extern __shared__ float4 smem4[];
+  float* __restrict__ my = reinterpret_cast<float*>(smem4) + threadIdx.x * R::SL;
+  const int lane = int(threadIdx.x), gl = lane % G;
+  float* xch = G > 1 ? reinterpret_cast<float*>(smem4) + 32 * R::SL + (lane / G) * R::XS : nullptr;
+  const int64_t m_raw = int64_t(blockIdx.x) * R::kMembers + lane / G;
+  const bool valid = m_raw < p;
+  const int64_t m = valid ? m_raw : p - 1;  // lanes past p shadow the last member, unrecorded
+  {
+    const float* __restrict__ row = theta + m * stride;
+#pragma unroll 1
+    for (int k = 0; k < OBS; ++k) {
 #pragma unroll
-  for (int i = 0; i < nq; ++i) {
-    q[i] = __ldg(state + i * p + m);
-    v[i] = __ldg(state + (nq + i) * p + m);
-  }
-  float ret = 0.0f, alive_steps = 0.0f;  // return and steps survived, fall step included
-  for (int step = 0; step < horizon; ++step) {
-    // observation without x: (y, phi, psi.., x_dot, y_dot, phi_dot, psi_dot..)
-    float hdn[H];
-#pragma unroll
-    for (int j = 0; j < H; ++j) {
-      float s = __ldg(row + B1 + j);
-#pragma unroll
-      for (int k = 1; k < nq; ++k) s += q[k] * __ldg(row + (k - 1) * H + j);
-#pragma unroll
-      for (int k = 0; k < nq; ++k) s += v[k] * __ldg(row + (nq - 1 + k) * H + j);
-      hdn[j] = tanhf(s);
+      for (int u = 0; u < U; ++u) my[R::W1 + k * U + u] = __ldg(row + k * H + gl * U + u);
     }
-    float tq[C];
 #pragma unroll
-    for (int leg = 0; leg < C; ++leg) {
+    for (int u = 0; u < U; ++u) my[R::B1 + u] = __ldg(row + R::B1g + gl * U + u);
+#pragma unroll 1
+    for (int j = 0; j < H; ++j) {
+#pragma unroll
+      for (int o = 0; o < NO; ++o) my[R::W2 + o * H + j] = __ldg(row + R::W2g + j * R::OUT + gl * NO + o);
+    }
+#pragma unroll
+    for (int o = 0; o < NO; ++o) my[R::B2 + o] = __ldg(row + R::B2g + gl * NO + o);
+  }
+  float qt[3], vt[3], ql[CL], vl[CL];
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    qt[i] = __ldg(state + i * p + m);
+    vt[i] = __ldg(state + (nq + i) * p + m);
+  }
+#pragma unroll
+  for (int c = 0; c < CL; ++c) {
+    ql[c] = __ldg(state + (3 + gl * CL + c) * p + m);
+    vl[c] = __ldg(state + (nq + 3 + gl * CL + c) * p + m);
+  }
+  bool alive = valid;
+  float ret = 0.0f, taken = 0.0f;  // return and steps taken, fall step included
+  for (int step = 0; step < horizon; ++step) {
+    if (!__any_sync(kFull, alive)) break;
+    // The weights do not change inside the loop, and without this barrier the compiler hoists
+    // all of their loads out of it, into far more registers than a thread has.
+    asm volatile("" ::: "memory");
+    // observation without x: (y, phi, psi.., x_dot, y_dot, phi_dot, psi_dot..)
+    float obs[OBS];
+    {
+      float own[2][CL], all[2][C];
+#pragma unroll
+      for (int c = 0; c < CL; ++c) {
+        own[0][c] = ql[c];
+        own[1][c] = vl[c];
+      }
+      contact_exchange<C, G, 2>(own, all, xch + kXchObs * C, gl);
+      obs[0] = qt[1];
+      obs[1] = qt[2];
+#pragma unroll
+      for (int k = 0; k < C; ++k) obs[2 + k] = all[0][k];
+#pragma unroll
+      for (int i = 0; i < 3; ++i) obs[2 + C + i] = vt[i];
+#pragma unroll
+      for (int k = 0; k < C; ++k) obs[5 + C + k] = all[1][k];
+    }
+    float hown[U];
+    if constexpr (R::kVec1) {
+#pragma unroll
+      for (int u = 0; u < U; u += 4) {
+        const float4 b = *reinterpret_cast<const float4*>(my + R::B1 + u);
+        float acc[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int k = 0; k < OBS; ++k) {
+          const float4 w = *reinterpret_cast<const float4*>(my + R::W1 + k * U + u);
+          acc[0] = fmaf(obs[k], w.x, acc[0]);
+          acc[1] = fmaf(obs[k], w.y, acc[1]);
+          acc[2] = fmaf(obs[k], w.z, acc[2]);
+          acc[3] = fmaf(obs[k], w.w, acc[3]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) hown[u + i] = tanhf(acc[i]);
+      }
+    } else {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        float acc = my[R::B1 + u];
+#pragma unroll
+        for (int k = 0; k < OBS; ++k) acc = fmaf(obs[k], my[R::W1 + k * U + u], acc);
+        hown[u] = tanhf(acc);
+      }
+    }
+    float hdn[H];
+    if constexpr (G == 1) {
+#pragma unroll
+      for (int j = 0; j < H; ++j) hdn[j] = hown[j];
+    } else {
+      float* hx = xch + xch_hidden<C>();
+#pragma unroll
+      for (int u = 0; u < U; ++u) hx[gl * U + u] = hown[u];
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < H; ++j) hdn[j] = hx[j];
+    }
+    float tq[CL];
+#pragma unroll
+    for (int c = 0; c < CL; ++c) {
       float l[3];
 #pragma unroll
       for (int o = 0; o < 3; ++o) {
-        float s = __ldg(row + B2 + 3 * leg + o);
+        const float* __restrict__ w2 = my + R::W2 + (3 * c + o) * H;
+        float acc = my[R::B2 + 3 * c + o];
+        if constexpr (R::kVec2) {
 #pragma unroll
-        for (int j = 0; j < H; ++j) s += hdn[j] * __ldg(row + W2 + j * OUT + 3 * leg + o);
-        l[o] = s;
+          for (int j = 0; j < H; j += 4) {
+            const float4 w = *reinterpret_cast<const float4*>(w2 + j);
+            acc = fmaf(hdn[j], w.x, acc);
+            acc = fmaf(hdn[j + 1], w.y, acc);
+            acc = fmaf(hdn[j + 2], w.z, acc);
+            acc = fmaf(hdn[j + 3], w.w, acc);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < H; ++j) acc = fmaf(hdn[j], w2[j], acc);
+        }
+        l[o] = acc;
       }
-      tq[leg] = float(argmax3(l[0], l[1], l[2]) - 1) * lg::TORQUE;
+      tq[c] = float(argmax3(l[0], l[1], l[2]) - 1) * lg::TORQUE;
     }
 #pragma unroll 1
-    for (int sub = 0; sub < lg::SUBSTEPS; ++sub) legged_substep<C, false>(q, v, tq, assist, iters);
-    if (legged_terminated<C>(q)) {
-      alive_steps += 1.0f;
-      ret -= fall_penalty;
-      break;
+    for (int ss = 0; ss < lg::SUBSTEPS; ++ss)
+      legged_substep<C, G, false, false, true>(qt, vt, ql, vl, tq, assist, iters, xch, gl, alive);
+    if (alive) {
+      taken += 1.0f;
+      if (legged_terminated(qt)) {
+        ret = sub(ret, fall_penalty);
+        alive = false;
+      } else {
+        ret = add(ret, add(qt[1] >= gate ? vt[0] : 0.0f, alive_bonus));
+      }
     }
-    ret += (q[1] >= gate ? v[0] : 0.0f) + alive_bonus;
-    alive_steps += 1.0f;
   }
-  fitness[m] = ret;
-  steps[m] = alive_steps;
+  if (valid && gl == 0) {
+    fitness[m] = ret;
+    steps[m] = taken;
+  }
 }
 
 using ClassicRollout = void (*)(const float*, const float*, int64_t, int64_t, int, float*);
@@ -261,27 +391,81 @@ struct AcrobotRollout {
 using LeggedRollout = void (*)(const float*, const float*, int64_t, int64_t, int, int, float, float,
                                float, float, float*, float*);
 
-template <int C>
-LeggedRollout pick_legged_h(int h) {
-  switch (h) {
-    case 1: return &legged_rollout_kernel<C, 1>;
-    case 2: return &legged_rollout_kernel<C, 2>;
-    case 4: return &legged_rollout_kernel<C, 4>;
-    case 8: return &legged_rollout_kernel<C, 8>;
-    case 16: return &legged_rollout_kernel<C, 16>;
-    case 32: return &legged_rollout_kernel<C, 32>;
-    default: return nullptr;
+struct LeggedLaunch {
+  LeggedRollout fn;
+  size_t smem;
+  int lanes;
+};
+
+template <int C, int H, int G>
+LeggedLaunch legged_instance() {
+  if constexpr (C % G == 0 && H % G == 0 && (G == 1 || C % 2 == 0))
+    return LeggedLaunch{&legged_rollout_kernel<C, H, G>, LeggedSlice<C, H, G>::kSmem, G};
+  else
+    return LeggedLaunch{nullptr, 0, G};
+}
+
+template <int C, int H>
+LeggedLaunch pick_legged_g(int g) {
+  switch (g) {
+    case 1: return legged_instance<C, H, 1>();
+    case 2: return legged_instance<C, H, 2>();
+    case 4: return legged_instance<C, H, 4>();
+    default: return LeggedLaunch{nullptr, 0, g};
   }
 }
 
-LeggedRollout pick_legged(int c, int h) {
-  switch (c) {
-    case 1: return pick_legged_h<1>(h);
-    case 2: return pick_legged_h<2>(h);
-    case 3: return pick_legged_h<3>(h);
-    case 4: return pick_legged_h<4>(h);
-    default: return nullptr;
+template <int C>
+LeggedLaunch pick_legged_h(int h, int g) {
+  switch (h) {
+    case 1: return pick_legged_g<C, 1>(g);
+    case 2: return pick_legged_g<C, 2>(g);
+    case 4: return pick_legged_g<C, 4>(g);
+    case 8: return pick_legged_g<C, 8>(g);
+    case 16: return pick_legged_g<C, 16>(g);
+    case 32: return pick_legged_g<C, 32>(g);
+    default: return LeggedLaunch{nullptr, 0, g};
   }
+}
+
+LeggedLaunch pick_legged(int c, int h, int g) {
+  switch (c) {
+    case 1: return pick_legged_h<1>(h, g);
+    case 2: return pick_legged_h<2>(h, g);
+    case 3: return pick_legged_h<3>(h, g);
+    case 4: return pick_legged_h<4>(h, g);
+    default: return LeggedLaunch{nullptr, 0, g};
+  }
+}
+
+// Opt a kernel in to its dynamic shared memory on the current device. The attribute is per
+// function and device, and setting it again is harmless, so each launch sets it (a few
+// microseconds against a rollout of milliseconds) instead of caching it per device.
+int prepare_smem(const void* fn, size_t smem) {
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             int(cudaSharedmemCarveoutMaxShared));
+  return e == cudaSuccess ? RLENV_OK : int(e);
+}
+
+// Lanes per legged member when the caller leaves it open: the widest G (dividing C and H)
+// whose launch keeps every member resident at once. Members run for as long as they stay
+// up, so a launch that needs a second wave runs its longest-lived members one after another.
+int legged_lanes(int c, int h, int64_t p) {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+    return 1;
+  for (int g = 4; g > 1; g /= 2) {
+    const LeggedLaunch L = pick_legged(c, h, g);
+    if (!L.fn) continue;
+    if (prepare_smem(reinterpret_cast<const void*>(L.fn), L.smem) != RLENV_OK) continue;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, L.fn, 32, L.smem) != cudaSuccess) continue;
+    if (int64_t(per_sm) * sms * (32 / g) >= p) return g;
+  }
+  return 1;
 }
 
 int launch_classic(ClassicRollout fn, int g, const float* state, const float* theta,
@@ -316,19 +500,34 @@ int rlenv_acrobot_rollout(const float* state, const float* theta, int64_t theta_
                         horizon, fitness, stream);
 }
 
+int rlenv_legged_rollout_lanes(int lanes, int c, int hidden, int horizon, int iters, float alive,
+                               float fall, float gate, float assist, const float* state,
+                               const float* theta, int64_t theta_stride, int64_t p, float* fitness,
+                               float* steps, void* stream) {
+  using namespace rlenv;
+  if (p < 0 || horizon < 0 || theta_stride < 0 || iters < 1) return RLENV_EINVAL;
+  if (pick_legged(c, hidden, 1).fn == nullptr) return RLENV_EUNSUPPORTED;
+  if (lanes == 0) lanes = legged_lanes(c, hidden, p);
+  const LeggedLaunch L = pick_legged(c, hidden, lanes);
+  if (!L.fn) return RLENV_EUNSUPPORTED;
+  if (p == 0) return RLENV_OK;
+  if (!state || !theta || !fitness || !steps) return RLENV_EINVAL;
+  const int st = prepare_smem(reinterpret_cast<const void*>(L.fn), L.smem);
+  if (st != RLENV_OK) return st;
+  const int64_t members = 32 / L.lanes;
+  const int64_t blocks = (p + members - 1) / members;
+  if (blocks > int64_t(0x7fffffff)) return RLENV_EINVAL;
+  L.fn<<<int(blocks), 32, L.smem, as_stream(stream)>>>(state, theta, theta_stride, p, horizon, iters,
+                                                       alive, fall, gate, assist, fitness, steps);
+  return launch_status();
+}
+
 int rlenv_legged_rollout(int c, int hidden, int horizon, int iters, float alive, float fall,
                          float gate, float assist, const float* state, const float* theta,
                          int64_t theta_stride, int64_t p, float* fitness, float* steps,
                          void* stream) {
-  using namespace rlenv;
-  if (p < 0 || horizon < 0 || theta_stride < 0 || iters < 1) return RLENV_EINVAL;
-  LeggedRollout fn = pick_legged(c, hidden);
-  if (!fn) return RLENV_EUNSUPPORTED;
-  if (p == 0) return RLENV_OK;
-  if (!state || !theta || !fitness || !steps) return RLENV_EINVAL;
-  fn<<<grid_for(p, 128), 128, 0, as_stream(stream)>>>(state, theta, theta_stride, p, horizon, iters,
-                                                      alive, fall, gate, assist, fitness, steps);
-  return launch_status();
+  return rlenv_legged_rollout_lanes(0, c, hidden, horizon, iters, alive, fall, gate, assist, state,
+                                    theta, theta_stride, p, fitness, steps, stream);
 }
 
 }  // extern "C"

@@ -48,6 +48,8 @@ _SIGNATURES = {
     "rlenv_acrobot_rollout": [c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_void_p, c_void_p],
     "rlenv_legged_rollout": [c_int, c_int, c_int, c_int, c_float, c_float, c_float, c_float, c_void_p, c_void_p,
                              c_int64, c_int64, c_void_p, c_void_p, c_void_p],
+    "rlenv_legged_rollout_lanes": [c_int, c_int, c_int, c_int, c_int, c_float, c_float, c_float, c_float, c_void_p,
+                                   c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p],
     "rlenv_pendulum_mm_step_many": [c_int, c_int, c_void_p, c_void_p, c_int, c_uint32, c_int64, c_int64, c_int64,
                                     c_void_p, c_void_p, c_void_p, c_void_p],
     "rlenv_pendulum_coop_step_many": [c_int, c_void_p, c_void_p, c_int, c_uint32, c_int64, c_int64, c_int64,
