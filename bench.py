@@ -225,28 +225,89 @@ def cpu_workload_baseline(workload, args, n, budget_s=10.0):
                       f"after 1 warm-up, numpy {np.__version__}, 1 thread"}
 
 
+def default_config(n, T, world):
+    """The default line's workload, printed identically by both arms."""
+    return {"workload": WORKLOAD, "n_envs_per_gpu": n, "env_steps_per_step": T,
+            "actions": "uniform over {0, 1, 2}, seeded", "state0": "uniform in +-0.1, seeded",
+            "parallelism": f"env-sharded x{world}, no data-path collective"}
+
+
+def _ref_step_fn():
+    """(step(state, action, rng) -> (next, reward, done), kind): the reference's own
+    acrobot_np.step where an install of the reference is importable (baseline/_ref), else the
+    oracle's restatement of it."""
+    ref = ROOT / "baseline" / "_ref"
+    if (ref / "acrobot_np.py").exists():
+        sys.path.insert(0, str(ref))
+        try:
+            import acrobot_np
+
+            return acrobot_np.step, "reference"
+        except Exception:
+            pass
+    sys.path.insert(0, str(ROOT))
+    from oracle import classic
+
+    def step(state, action, rng):
+        stepped = classic.acrobot_physics(state, action)
+        done = classic.acrobot_terminated(stepped)
+        fresh = rng.uniform(-0.1, 0.1, size=state.shape).astype(np.float32)
+        return np.where(done[None, :], fresh, stepped), classic.acrobot_reward(done), done
+    return step, "port"
+
+
+def _ref_worker(args):
+    """Step a shard of n environments of the numpy Acrobot `steps` times (the shape of the
+    reference's bench loop: actions drawn inside the loop); returns the elapsed seconds."""
+    n, steps, seed = args
+    os.environ.setdefault("OMP_NUM_THREADS", "1")
+    step, _ = _ref_step_fn()
+    rng = np.random.default_rng(seed)
+    state = rng.uniform(-0.1, 0.1, size=(4, n)).astype(np.float32)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        state, _, _ = step(state, rng.integers(0, 3, size=n), rng)
+    return time.perf_counter() - t0
+
+
 def run_reference(args):
+    """The reference's CPU implementation of the path on every host core: the batch sharded over
+    one process per core, each bench step a bounded sample of the workload (the same N, fewer
+    environment steps), K timed steps after W warm-up steps, sized to finish in about
+    --cpu-seconds."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    import multiprocessing as mp
+
     cores = len(os.sched_getaffinity(0))
-    vals = []
-    for _ in range(args.warmup):
-        cpu_throughput(args.n, 2.0, cores)
-    sample = ""
-    for _ in range(args.steps if args.steps <= 5 else 3):
-        v, sample, _ = cpu_throughput(args.n, args.cpu_seconds / 3, cores)
-        vals.append(v)
-    value = statistics.median(vals)
+    n = args.n
+    per = max(1, n // cores)
+    _, kind = _ref_step_fn()
+    probe = _ref_worker((per, 2, 0)) / 2  # seconds per step of one shard
+    budget = max(args.cpu_seconds, 5.0) / max(1, args.steps + args.warmup)
+    sample_steps = int(max(1, min(args.t, budget / max(probe, 1e-6))))
+    secs = []
+    with mp.get_context("spawn").Pool(cores) as pool:
+        for k in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            pool.map(_ref_worker, [(per, sample_steps, 1000 * k + r) for r in range(cores)])
+            if k >= args.warmup:
+                secs.append(time.perf_counter() - t0)
+    total = per * cores * sample_steps
+    value = total * len(secs) / sum(secs)
+    sample = (f"{'acrobot_np.step (the reference, baseline/_ref)' if kind == 'reference' else 'acrobot_np.step restated in oracle/'}: "
+              f"N={per * cores} environments in {cores} shards, {sample_steps} environment steps per bench step, "
+              f"numpy {np.__version__}, one process per core")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "env steps/s", "n_gpus": args.gpus,
-            "steps": len(vals), "warmup": args.warmup, "ms_per_step": 1e3 * args.n * args.t / value,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * n * args.t / value,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded uniform states and actions)",
-            "config": {"workload": WORKLOAD, "n_envs": args.n, "env_steps_per_step": args.t,
-                       "note": "the reference's numpy step (acrobot_np.step) restated in oracle/; each step a "
-                               "bounded sample of the workload"},
-            "cpu_baseline": {"value": value, "unit": "env steps/s", "cores": cores, "kind": "port", "sample": sample},
-            "e2e": {"value": value, "unit": "env steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "config": default_config(n, args.t, args.gpus),
+            "cpu_baseline": {"value": value, "unit": "env steps/s", "cores": cores, "kind": kind, "sample": sample},
+            "e2e": {"value": value, "unit": "env steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "timing": "wall clock over the K timed bench steps; ms_per_step is the time of a full step "
+                      "(N x env_steps_per_step) at the measured rate"}
     print(json.dumps(line), flush=True)
 
 
@@ -327,34 +388,136 @@ def hbm_peak_gbs():
     return 6650.0, "fallback"
 
 
-def profiled(key):
-    """A figure of the step kernel's committed ncu summary (`key: value` line), if present:
-    traffic_bytes_per_launch (DRAM bytes per full-size launch) or inst_per_env_step
-    (executed thread instructions per environment-step)."""
-    f = ROOT / "profiles" / "acrobot_step_many_n262144_t1000.md"
-    if f.exists():
-        for line in f.read_text().splitlines():
-            if line.startswith(key + ":"):
-                return float(line.split(":", 1)[1].strip().split()[0])
-    return None
+def north_star_records(torch, dist, world, rank, local, dev, sgemm):
+    """Sub-records of the default run: the north star's other figures, each timed here with CUDA
+    events over its own region (warm-up untimed, max over ranks). Every rank runs every record in
+    the same order (the ES record's all-gather and the barriers are collectives).
+    - cartpole_fused_n1m: CartPole, N = 1,048,576 per GPU, 1,000 steps per launch (T-step kernel,
+      per-step rewards and done flags to HBM); target 1e9 env-steps/s per GPU.
+    - cartpole_single_n16m: the drop-in single step at N = 2^24 per GPU, 20 launches per CUDA graph,
+      41 B per env-step streamed (int32 actions): against measured HBM bandwidth.
+    - acrobot_single_like_reference: the reference's published configuration (README.md:403):
+      N = 262,144, one step kernel launch per step, actions drawn on the device every step, 32
+      steps per CUDA graph (the reference evaluates every 32); vs_baseline against its 1.123e9.
+    - legged4_step: C = 4, 8 sweeps, N = 262,144 per GPU, 50 steps per launch, states, rewards,
+      fall flags and contact impulses out: against the FP32 rate.
+    - es_legged4: one ES generation (perturb, rollout, ranks, update), P = 16,384 split over the
+      ranks (strong scaling), horizon 1,000, H = 16, sigma 0.1, lr 0.03; with more than one rank
+      also es_legged4_weak, P = 16,384 per rank."""
+    import es
+    import legged_metal
+    import rlenv_flops
+    import rlenv_lib as rl
 
+    lib = rl.load()
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    g = torch.Generator(device=dev).manual_seed(777 + rank)
+    hbm, hbm_kind = hbm_peak_gbs()
+    out = {}
 
-def profiled_traffic():
-    return profiled("traffic_bytes_per_launch")
+    def timed(fn, steps, warmup):
+        return _timed(torch, dist, world, stream, fn, steps, warmup, local)
 
+    def fp32(flops_per_s):
+        return {"achieved_tflops": flops_per_s / 1e12, "peak_tflops": sgemm,
+                "frac": flops_per_s / 1e12 / sgemm if sgemm else None, "peak_kind": "cuBLAS SGEMM, TF32 off, this run"}
 
-def issue_view(env_steps_per_s_per_gpu, sm_mhz, sms):
-    """The step kernel against instruction issue, its actual limit: executed thread
-    instructions per second (ncu's count per env-step times the measured rate) over one
-    warp instruction per SM sub-partition per cycle at the sampled SM clock."""
-    inst = profiled("inst_per_env_step")
-    if not inst or not sm_mhz:
-        return None
-    achieved = env_steps_per_s_per_gpu * inst / 1e9
-    peak = sms * 4 * 32 * sm_mhz * 1e6 / 1e9
-    return {"achieved": achieved, "peak": peak, "unit": "G thread-inst/s", "frac": achieved / peak,
-            "inst_per_env_step": inst, "peak_kind": f"{sms} SMs x 4 schedulers x 32 lanes x sampled SM clock",
-            "source": "ncu smsp__inst_executed, profiles/acrobot_step_many_n262144_t1000.md"}
+    # CartPole fused
+    n, T = 1 << 20, 1000
+    acts = torch.randint(0, 2, (T, n), device=dev, generator=g).to(torch.uint8)
+    s0 = rl.reset_uniform(4, n, 0.05, seed=7, index_offset=rank * n, dev=dev)
+    s1 = torch.empty_like(s0)
+    rew, dn = torch.empty((T, n), device=dev), torch.empty((T, n), device=dev, dtype=torch.bool)
+    secs, clk = timed(lambda: rl.check(lib.cartpole_step_many(s0.data_ptr(), acts.data_ptr(), rl.U8, 1, T, n, rank * n,
+                                                              s1.data_ptr(), rew.data_ptr(), dn.data_ptr(), 0, 0, sp)), 5, 3)
+    v = n * T * 5 / secs
+    out["cartpole_fused_n1m"] = {"value": v * world, "unit": "env steps/s", "per_gpu": v, "target_per_gpu": 1e9,
+                                 "n_envs_per_gpu": n, "env_steps_per_launch": T, "launches": 5, "ms_per_launch": 1e3 * secs / 5,
+                                 "fp32": fp32(v * rlenv_flops.CARTPOLE["flops"]), "sm_mhz": clk["sm_mhz"]}
+    del acts, s0, s1, rew, dn
+
+    # CartPole and Acrobot single steps
+    def singles(env, n, T, dtype, sample_on_device):
+        n_act = 2 if env == "cartpole" else 3
+        abi = getattr(lib, f"{env}_step")
+        acts = (torch.empty((T, n), device=dev, dtype=torch.int32) if sample_on_device else
+                torch.randint(0, n_act, (T, n), device=dev, generator=g, dtype=torch.int32))
+        sa = rl.reset_uniform(4, n, 0.05 if env == "cartpole" else 0.1, seed=7, index_offset=rank * n, dev=dev)
+        sb = torch.empty_like(sa)
+        rew, dn = torch.empty((T, n), device=dev), torch.empty((T, n), device=dev, dtype=torch.bool)
+
+        def one(t):
+            if sample_on_device:
+                acts[t].random_(0, n_act)
+            src, dst = (sa, sb) if t % 2 == 0 else (sb, sa)
+            rl.check(abi(src.data_ptr(), acts[t].data_ptr(), rl.I32, 1 + t, n, rank * n, dst.data_ptr(),
+                         rew[t].data_ptr(), dn[t].data_ptr(), torch.cuda.current_stream().cuda_stream))
+        graph = _graph_steps(torch, one, T)
+        secs, clk = timed(graph.replay, 3, 3)
+        del graph
+        return n * T * 3 / secs, secs / 3, clk
+
+    v, per, clk = singles("cartpole", 1 << 24, 20, torch.int32, False)
+    gbs = v * rlenv_flops.step_bytes(4, 4) / 1e9
+    out["cartpole_single_n16m"] = {"value": v * world, "unit": "env steps/s", "per_gpu": v, "n_envs_per_gpu": 1 << 24,
+                                   "launches_per_graph": 20, "bytes_per_env_step": rlenv_flops.step_bytes(4, 4),
+                                   "hbm": {"achieved_gbs": gbs, "peak_gbs": hbm, "frac": gbs / hbm, "peak_kind": hbm_kind},
+                                   "sm_mhz": clk["sm_mhz"]}
+    v, per, clk = singles("acrobot", 262_144, 32, torch.int32, True)
+    pub, src = published("acrobot_step", 262_144)
+    out["acrobot_single_like_reference"] = {
+        "value": v * world, "unit": "env steps/s", "per_gpu": v, "n_envs_per_gpu": 262_144, "launches_per_graph": 32,
+        "actions": "drawn on the device every step (torch random_, inside the graph), as the reference's bench does",
+        "vs_baseline": v / pub, "vs_baseline_source": src, "sm_mhz": clk["sm_mhz"],
+        "gpu_launches_per_step": 1}
+
+    # legged4 step with contact impulses
+    c, iters, n, T = 4, 8, 262_144, 50
+    stand = torch.from_numpy(legged_metal.stand_pose(c)).to(dev)
+    la = rl.reset_uniform(2 * (3 + c), n, 0.05, center=stand, seed=3, index_offset=rank * n, dev=dev)
+    lb = torch.empty_like(la)
+    acts = torch.randint(0, 3 ** c, (T, n), device=dev, generator=g).to(torch.uint8)
+    rew, dn = torch.empty((T, n), device=dev), torch.empty((T, n), device=dev, dtype=torch.bool)
+    imp = torch.empty((T, 2 * c, n), device=dev)
+    secs, clk = timed(lambda: rl.check(lib.legged_step_many(c, iters, la.data_ptr(), acts.data_ptr(), rl.U8, 1,
+                                                            stand.data_ptr(), 0.0, None, T, n, rank * n, lb.data_ptr(),
+                                                            rew.data_ptr(), dn.data_ptr(), imp.data_ptr(), sp)), 5, 3)
+    v = n * T * 5 / secs
+    fl = rlenv_flops.legged_flops(c, iters)["flops"]
+    out["legged4_step"] = {"value": v * world, "unit": "env steps/s", "per_gpu": v, "legs": c, "sweeps": iters,
+                           "n_envs_per_gpu": n, "env_steps_per_launch": T, "impulses": True,
+                           "flops_per_env_step": fl, "fp32": fp32(v * fl),
+                           "flops_per_env_step_reference_algorithm": rlenv_flops.legged_reference_flops(c, iters)["flops"],
+                           "sm_mhz": clk["sm_mhz"]}
+    del la, lb, acts, rew, dn, imp
+
+    # legged4 ES generation
+    def es_record(pop):
+        task = es.TASKS["legged4"]
+        cfg = es.Config(task="legged4", pop=pop, horizon=1000, sigma=0.1, lr=0.03)
+        backend = es.MetalBackend(task, 0)
+        st = {"theta": backend.normal((es.n_params(task.hidden, task),)) * 0.1, "gen": 0, "taken": 0.0}
+
+        def gen():
+            st["gen"] += 1
+            st["theta"], _, steps = es.generation(backend, st["theta"], cfg, task.hidden, st["gen"])
+            st["taken"] += float(steps.sum().item())
+        for _ in range(3):
+            gen()
+        st["taken"] = 0.0
+        secs, clk = timed(gen, 5, 0)
+        taken = st["taken"] / 5 * world  # every rank's shard takes about as many steps as rank 0's
+        fl = rlenv_flops.es_member_step_flops("legged4")["flops"]
+        return {"value": 1e3 * secs / 5, "unit": "ms per generation", "higher_is_better": False, "population": pop,
+                "horizon": 1000, "hidden": task.hidden, "generations": 5, "after_generations": 3,
+                "member_steps_taken_per_generation": taken, "member_steps_nominal": pop * 1000,
+                "env_steps_per_s": taken / (secs / 5), "fp32_steps_taken": fp32(taken / (secs / 5) * fl),
+                "sm_mhz": clk["sm_mhz"]}
+    out["es_legged4"] = {**es_record(16_384), "scaling": "strong (P split over the ranks, one all-gather per generation)"}
+    if world > 1:
+        out["es_legged4_weak"] = {**es_record(16_384 * world), "scaling": "weak (P = 16,384 per rank)"}
+    return out
 
 
 def run_ours(args):
@@ -454,7 +617,7 @@ def run_ours(args):
     e2e_run(max(2, args.warmup // 2))
     torch.cuda.synchronize()
     barrier()
-    e2e_steps = max(4, args.steps // 10)
+    e2e_steps = max(20, args.steps // 10)
     torch.cuda.synchronize()
     t_e2e = time.perf_counter()
     s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -474,7 +637,8 @@ def run_ours(args):
     sgemm = measured_sgemm_tflops(torch) if rank == 0 else None
     bytes_per_launch = rlenv_flops.step_many_bytes(4, n, T, 1, True)
     hbm, hbm_kind = hbm_peak_gbs()
-    traffic = profiled_traffic()
+    clock_summary = clocks.summary()
+    subs = north_star_records(torch, dist, world, rank, local, dev, sgemm)
 
     if world > 1:
         dist.barrier()
@@ -487,27 +651,26 @@ def run_ours(args):
         cpu = {"value": v, "unit": "env steps/s", "cores": cores, "kind": "port",
                "sample": sample + " (single thread, as the reference reports numpy)"}
     achieved = flops / per_launch / 1e12
-    clock_summary = clocks.summary()
     line = {
         "metric": METRIC, "value": value, "unit": "env steps/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * secs_max / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": value / published("acrobot_step", n)[0] if published("acrobot_step", n)[0]
-        else None, "vs_baseline_source": published("acrobot_step", n)[1], "dtype": "f32",
-        "data": "synthetic (seeded uniform states, uniform actions in {0,1,2})",
-        "config": {"workload": WORKLOAD, "n_envs_per_gpu": n, "env_steps_per_step": T,
-                   "kernel": "rlenv_acrobot_step_many (state in registers, per-step rewards and dones to HBM)",
-                   "l2": "inputs and outputs larger than L2 (actions 262 MB, rewards+dones 1.3 GB per step)",
-                   "parallelism": f"env-sharded x{world}, no data-path collective"},
+        "scaling": "weak", "vs_baseline": None,
+        "vs_baseline_note": "the reference publishes no fused multi-step figure; its single-step kernel figure "
+                            "is compared on north_star.acrobot_single_like_reference",
+        "dtype": "f32", "data": "synthetic (seeded uniform states, uniform actions in {0,1,2})",
+        "config": default_config(n, T, world),
+        "kernel": "rlenv_acrobot_step_many: T steps per launch, state in registers, uint8 actions resident in "
+                  "HBM, per-step rewards and done flags written to HBM",
+        "l2": "inputs and outputs larger than L2 (actions 262 MB, rewards and done flags 1.3 GB per step)",
         "roofline": {"bound": "fp32", "achieved": achieved, "peak": sgemm, "unit": "TFLOP/s",
                      "frac": achieved / sgemm if sgemm else None,
                      "peak_kind": "cuBLAS SGEMM (TF32 off) measured in this run; nominal FP32 FMA 74.4 TFLOP/s",
                      "flops_per_env_step": rlenv_flops.ACROBOT["flops"],
                      "transcendentals_per_env_step": rlenv_flops.ACROBOT["transcendentals"],
-                     "traffic": traffic, "algorithmic_bytes_per_launch": bytes_per_launch,
+                     "traffic": None, "algorithmic_bytes_per_launch": bytes_per_launch,
+                     "traffic_note": "DRAM bytes per launch are an ncu figure, kept in profiles/ (not read here)",
                      "hbm": {"achieved": bytes_per_launch / per_launch / 1e9, "peak": hbm, "unit": "GB/s",
                              "frac": bytes_per_launch / per_launch / 1e9 / hbm, "peak_kind": hbm_kind},
-                     "issue": issue_view(n * T / per_launch, clock_summary.get("sm_mhz"),
-                                         torch.cuda.get_device_properties(dev).multi_processor_count),
                      "launch_ms": per_launch * 1e3},
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": "env steps/s", "h2d_bytes_per_step": 4 * 4 * n + T * n,
@@ -515,6 +678,7 @@ def run_ours(args):
                 "pipelined": "copy stream and compute stream, two steps in flight"},
         "gpu_launches": args.steps,
         "clocks": clock_summary,
+        "north_star": subs,
     }
     print(json.dumps(line), flush=True)
 

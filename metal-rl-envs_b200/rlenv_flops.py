@@ -52,21 +52,25 @@ def legged_flops(c, iters=8):
     - The mass matrix is solved in closed form: an arrowhead structure, with the legs
       eliminated first and then a 2x2 Schur block.
     - The Delassus blocks come from the same closed form. Off the diagonal they are rank
-      one, so the sweeps carry G[k][l] and one scalar P_l per contact instead of the full
-      2x2 blocks.
+      one, so a contact sees the others through one scalar coupling s.
+    - Each contact's exact block solve is affine in s in each of its regimes, so its
+      coefficients are formed once per substep and a Gauss-Seidel solve is the coupling, seven
+      multiply-adds and three comparisons; the exact impulse is solved once at the end.
     Per substep, with n = 3 + C:
     - leg kinematics 12C; Schur block 6C + 12; generalised forces 15C + 12;
     - two mass solves 2 (14C + 7); free velocity and update 5n;
     - Delassus, the diagonal blocks in full and G below the diagonal, 1.5C^2 + 24.5C;
     - free relative velocities 10C; per-contact constants (three reciprocals, the slip
       coefficient, the Baumgarte target) 14C;
-    - per sweep and contact: the other contacts' contribution 2(C - 1) + 4, the exact impulse
-      about 38 and the contact's P 3;
+    - (C > 1) the affine coefficients 41C; per sweep and contact 2(C - 1) + 17; the final exact
+      impulse 42C; (C = 1) one exact impulse, 42;
     - J^T lambda 9C.
-    Transcendentals: C sines and cosines, 3C + 1 reciprocals."""
+    Every sweep is counted (the rollout's skipping of contacts no live member touches only
+    removes zero terms). Transcendentals: C sines and cosines, 3C + 1 reciprocals."""
     n = 3 + c
+    solve = (41 * c + iters * c * (2 * (c - 1) + 17) + 42 * c) if c > 1 else 42
     sub = (12 * c + 6 * c + 12 + 15 * c + 12 + 2 * (14 * c + 7) + 5 * n + 1.5 * c * c + 24.5 * c + 10 * c
-           + 14 * c + iters * c * (2 * (c - 1) + 4 + 38 + 3) + 9 * c)
+           + 14 * c + solve + 9 * c)
     return dict(flops=round(4 * sub), transcendentals=4 * (2 * c + 3 * c + 1))
 
 
@@ -74,7 +78,7 @@ def legged_reference_flops(c, iters=8):
     """The same step as the reference computes it (legged_np.py:57-97): the dense (3+C)^2 mass
     matrix, its Cholesky factor and 2C + 1 dense solves, the Delassus blocks from the solves;
     the Gauss-Seidel sweeps over the full 2x2 blocks, 8(C - 1) + 40 per sweep and contact.
-    For comparison only: the kernel does the closed form."""
+    For comparison only: the kernel does the closed form with affine sweeps."""
     n = 3 + c
     sub = (10 * c + (n * (n + 1) // 2) * 2 * c + 8 * n * c + n ** 3 / 3 + (2 * c + 1) * 2 * n * n
            + 24 * c * c + 12 * c + iters * c * (8 * (c - 1) + 40) + 4 * n * c + 4 * n)
