@@ -42,3 +42,26 @@ def check_step(name, out, ref_stepped, ref_done, oracle_next, rtol, atol, ref_re
     np.testing.assert_array_equal(nxt[:, ~live], oracle_next[:, ~live], err_msg=f"{name}: reset columns")
     if ref_reward is not None:
         np.testing.assert_allclose(reward, ref_reward, rtol=rtol, atol=atol, err_msg=f"{name}: reward")
+
+
+# The legged rollout cases pinned at the reference's horizon (test_es.py:46-104): (legs, alive
+# bonus, fall penalty, height gate, assist). Plain reward for both bodies; the shaped and
+# assisted variants of the reference's legged2 tasks.
+LEGGED_ROLLOUT_CASES = [(2, 1.0, 0.0, 0.0, 0.0), (2, 0.1, 20.0, 0.0, 0.0), (2, 0.0, 0.0, 0.85, 0.0),
+                        (2, 0.0, 0.0, 0.0, 20.0), (4, 1.0, 0.0, 0.0, 0.0), (4, 0.1, 20.0, 0.0, 0.0)]
+LEGGED_ROLLOUT_P, LEGGED_ROLLOUT_HORIZON, LEGGED_ROLLOUT_HIDDEN = 1024, 200, 16
+
+
+def legged_rollout_inputs(index):
+    """(initial states (2(3+C), P), parameter rows (P, D)) of case `index`: the reset pose plus
+    uniform +-0.05 on every row, and normal parameters scaled by 0.3 (the reference test's
+    scale), from numpy's default generator seeded with 100 + index."""
+    from oracle import legged
+
+    c = LEGGED_ROLLOUT_CASES[index][0]
+    h, p = LEGGED_ROLLOUT_HIDDEN, LEGGED_ROLLOUT_P
+    rng = np.random.default_rng(100 + index)
+    state = (legged.stand_pose(c)[:, None] + rng.uniform(-0.05, 0.05, (2 * (3 + c), p))).astype(np.float32)
+    d = (5 + 2 * c) * h + h + h * 3 * c + 3 * c
+    theta = (rng.normal(size=(p, d)) * 0.3).astype(np.float32)
+    return state, theta

@@ -178,7 +178,9 @@ def test_trajectory_matches_oracle_kernel_semantics(cuda, name):
         worst = max(worst, float(np.abs(to_np(s_gpu) - s_np).max()))
     record(f"{name}_traj100", done_flips=flips, max_abs=worst, n=int(s_np.shape[1]))
     assert flips == 0
-    assert worst < (1e-3 if name == "cartpole" else 1e-2), worst
+    # about ten times the measured worst (8.2e-6 CartPole, 2.3e-5 Acrobot), so a change that
+    # degrades the arithmetic shows here before it shows anywhere else
+    assert worst < (1e-4 if name == "cartpole" else 3e-4), worst
 
 
 def test_reference_pure_physics_trajectory(cuda):

@@ -6,8 +6,9 @@ import numpy as np
 import pytest
 import torch
 
+from conftest import golden
 from oracle import legged, rollout
-from parity import record, to_np
+from parity import LEGGED_ROLLOUT_CASES, LEGGED_ROLLOUT_HIDDEN, LEGGED_ROLLOUT_HORIZON, legged_rollout_inputs, record, to_np
 
 pytestmark = pytest.mark.gpu
 
@@ -80,18 +81,66 @@ def test_legged_rollout_short_horizon_matches_oracle(cuda, c, alive, fall, gate,
     assert f_ok > 0.98 and s_ok > 0.98
 
 
-@pytest.mark.parametrize("c,alive,fall,gate,assist", LEGGED_CASES)
-def test_legged_rollout_long_horizon_matches_oracle(cuda, c, alive, fall, gate, assist):
-    """Over 60 steps the contact dynamics amplify float32 rounding: the oracle's own float32 run
-    agrees with its float64-promoted run (the reference numpy's dtype) on only 91-96% of members'
-    fitness at this tolerance. The fall step (steps taken) stays robust, and the population's mean
-    fitness, which is what the ES update consumes through the ranks, agrees closely."""
-    fk, fl, sk, sl = _legged_case(cuda, c, alive, fall, gate, assist, horizon=60)
-    f_ok, s_ok = _agree(f"legged{c}_rollout60_a{alive}_f{fall}_g{gate}_as{assist}", fk, fl, sk, sl)
-    assert s_ok > 0.95 and f_ok > 0.7
-    assert abs(fk.mean() - fl.mean()) <= 0.03 * np.abs(fl).mean() + 0.05
+@pytest.mark.parametrize("index", range(len(LEGGED_ROLLOUT_CASES)))
+def test_legged_rollout_at_the_reference_horizon(cuda, index):
+    """The reference's rollout criterion (test_es.py:46-104: 1,024 members, horizon 200,
+    parameters at scale 0.3; fitness within 1e-3 relative (floor 1) plus 1e-2, and equal step
+    counts) against the float32 oracle (tests/golden/legged_rollout.npz).
+
+    Contact dynamics amplify rounding: over 200 steps the oracle's own float32 run and its
+    float64-promoted run (the reference numpy's arithmetic) agree on fewer than 95% of members
+    in several cases, nearly all of them members that stand the whole horizon and differ in
+    their summed velocity by about 0.2% of it. So the gate is the reference's 95% where float32
+    rounding alone allows it, and otherwise the oracle's own float32-float64 agreement, less 3
+    points. The population's mean fitness, which the ranks consume, must agree closely."""
+    import legged_rollout_metal
+
+    c, alive, fall, gate, assist = LEGGED_ROLLOUT_CASES[index]
+    state, theta = legged_rollout_inputs(index)
+    g = golden("legged_rollout")
+    f32, s32 = g[f"case{index}_f32_fitness"], g[f"case{index}_f32_steps"]
+    f64, s64 = g[f"case{index}_f64_fitness"], g[f"case{index}_f64_steps"]
+    fk, sk = legged_rollout_metal.rollout(torch.from_numpy(state).to(cuda), torch.from_numpy(theta).to(cuda),
+                                          LEGGED_ROLLOUT_HIDDEN, LEGGED_ROLLOUT_HORIZON, c, alive, fall, gate, assist)
+    fk, sk = to_np(fk), to_np(sk)
+
+    def crit(a, b):
+        a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+        return float((np.abs(a - b) <= 1e-2 + 1e-3 * np.maximum(np.abs(b), 1.0)).mean())
+
+    gpu_fit, gpu_steps = crit(fk, f32), float((sk == s32).mean())
+    own_fit, own_steps = crit(f32, f64), float((s32 == s64).mean())
+    record(f"legged{c}_rollout200_case{index}", fitness_agree=gpu_fit, steps_agree=gpu_steps,
+           oracle_f32_vs_f64_fitness_agree=own_fit, oracle_f32_vs_f64_steps_agree=own_steps,
+           gpu_vs_f64_fitness_agree=crit(fk, f64), mean_fitness_gpu=float(fk.mean()), mean_fitness_oracle=float(f32.mean()),
+           members=int(fk.size))
+    assert gpu_fit >= min(0.95, own_fit) - 0.03, (gpu_fit, own_fit)
+    assert gpu_steps >= min(0.95, own_steps) - 0.03, (gpu_steps, own_steps)
+    assert abs(fk.mean() - f32.mean()) <= 0.03 * np.abs(f32).mean() + 0.05
+    assert 5 < s32.mean() < LEGGED_ROLLOUT_HORIZON, "random bodies fall within the horizon"
     if fall:
-        assert fk.min() < 0, "a random biped that falls pays the penalty"
+        assert fk.min() < 0, "a random body that falls pays the penalty"
+
+
+@pytest.mark.parametrize("lanes", [1, 2, 4])
+def test_legged_rollout_lane_groups_give_the_same_bits(cuda, lanes):
+    """Every lane-group width steps the bodies with the same bits (rlenv_legged_rollout_lanes)."""
+    import rlenv_lib as rl
+
+    for index in (1, 5):
+        c, alive, fall, gate, assist = LEGGED_ROLLOUT_CASES[index]
+        state, theta = legged_rollout_inputs(index)
+        st, th = torch.from_numpy(state).to(cuda), torch.from_numpy(theta).to(cuda)
+        p, d = th.shape
+        out = []
+        for g in (1, lanes):
+            f = torch.empty(p, device=cuda)
+            s = torch.empty(p, device=cuda)
+            rl.check(rl.lib().legged_rollout_lanes(g, c, LEGGED_ROLLOUT_HIDDEN, 120, 8, alive, fall, gate, assist,
+                                                   st.data_ptr(), th.data_ptr(), d, p, f.data_ptr(), s.data_ptr(),
+                                                   rl.stream_ptr(cuda)))
+            out.append((f, s))
+        assert torch.equal(out[0][0], out[1][0]) and torch.equal(out[0][1], out[1][1]), (index, lanes)
 
 
 def test_shared_theta_row_equals_broadcast_rows(cuda):

@@ -1,10 +1,12 @@
 """The oracle reproduces the reference's own numpy outputs (tests/golden, made by running the
 reference's *_np.py and es.py). These pins are what lets every GPU test trust the oracle."""
 
+import sys
+
 import numpy as np
 import pytest
 
-from conftest import golden
+from conftest import GOLDEN, golden
 from oracle import classic, es, legged, pendulum
 
 TIGHT = dict(rtol=1e-6, atol=1e-6)
@@ -123,3 +125,17 @@ def test_es_solve_fixture_reproduces():
         r = oes.train(oes.Config(task=task, pop=pop, max_generations=max_gen, time_budget=1e9), 3)
         assert (r.solved, r.generations, r.env_steps) == (bool(g[f"{task}_solved"][3]), int(g[f"{task}_generations"][3]),
                                                           int(g[f"{task}_env_steps"][3]))
+
+
+def test_legged_rollout_fixture_is_the_oracles():
+    """tests/golden/legged_rollout.npz (the GPU rollout test's reference side) is what the oracle
+    computes from parity.legged_rollout_inputs: recomputed here on the first 48 members."""
+    sys.path.insert(0, str(GOLDEN))
+    import make_legged_rollout
+
+    g = golden("legged_rollout")
+    for index, f32 in ((0, True), (0, False), (4, True)):
+        fit, steps = make_legged_rollout.run(index, f32, p=48)
+        tag = "f32" if f32 else "f64"
+        np.testing.assert_array_equal(fit, g[f"case{index}_{tag}_fitness"][:48])
+        np.testing.assert_array_equal(steps, g[f"case{index}_{tag}_steps"][:48])
