@@ -32,6 +32,7 @@ reference bit for bit; parity is the distribution of generations to solve.
 """
 
 import argparse
+import inspect
 import time
 from dataclasses import dataclass
 from typing import Any, Callable
@@ -299,6 +300,20 @@ def loop_fitness(backend, params, horizon, assist=0.0, start_velocity=0.0, state
     return fitness, taken
 
 
+def _reset(backend, n, gen, member_offset):
+    """backend.reset for n members of generation gen from global member member_offset; a subclass
+    that overrides reset with the reference's signature reset(self, n) (as test_es.py:53-56 does)
+    gets just n."""
+    try:
+        params = inspect.signature(backend.reset).parameters.values()
+    except (TypeError, ValueError):
+        params = ()
+    takes = sum(p.kind in (p.POSITIONAL_ONLY, p.POSITIONAL_OR_KEYWORD) for p in params)
+    if takes >= 3 or any(p.kind == p.VAR_POSITIONAL for p in params):
+        return backend.reset(n, gen, member_offset)
+    return backend.reset(n)
+
+
 def _world():
     if dist.is_available() and dist.is_initialized():
         return dist.get_rank(), dist.get_world_size()
@@ -373,7 +388,7 @@ class MetalBackend:
         return out
 
     def rollout(self, theta_pop, hidden, horizon, assist=0.0, start_velocity=0.0, gen=0, member_offset=0):
-        state = push(torch, self.task, self.reset(theta_pop.shape[0], gen, member_offset), start_velocity)
+        state = push(torch, self.task, _reset(self, theta_pop.shape[0], gen, member_offset), start_velocity)
         extra = (assist,) if self.task.assistable else ()
         return self.task.rollout(state, theta_pop, hidden, horizon, *extra)
 
@@ -396,17 +411,44 @@ class MLXBackend(MetalBackend):
     """The step-by-step loop (es.py:230-257): torch policy, CUDA step kernel, per-step launches."""
 
     def rollout(self, theta_pop, hidden, horizon, assist=0.0, start_velocity=0.0, gen=0, member_offset=0):
-        state = self.reset(theta_pop.shape[0], gen, member_offset)
+        state = _reset(self, theta_pop.shape[0], gen, member_offset)
         return loop_fitness(self, unflatten(theta_pop, hidden, self.task), horizon, assist, start_velocity, state)
 
 
 BACKENDS = {"metal": MetalBackend, "cuda": MetalBackend, "mlx": MLXBackend, "loop": MLXBackend}
 
 
+_FUSED = ("shard", "perturb", "update", "centered_ranks")
+
+
+def reference_generation(backend, theta, cfg, hidden, gen=1):
+    """es.py:218-227 as the reference writes it, for a backend that offers only the reference's
+    interface (xp, normal, rollout, sync): half = normal((P/2, D)), eps = [half; -half], fitness
+    of theta + sigma eps, g = sum_i rank_i eps_i / (P sigma), theta + lr g. The ranks come from
+    this module's centred-rank kernel when the arrays are CUDA tensors."""
+    xp = getattr(backend, "xp", torch)
+    half = backend.normal((cfg.pop // 2, theta.shape[0]))
+    eps = xp.concatenate([half, -half], axis=0) if xp is not torch else torch.cat([half, -half], dim=0)
+    assist, start_velocity = curriculum(cfg, gen)
+    fit, steps = backend.rollout(theta[None, :] + cfg.sigma * eps, hidden, cfg.horizon, assist, start_velocity)
+    if isinstance(fit, torch.Tensor) and fit.is_cuda:
+        ranks = centered_ranks(xp, fit)
+    else:  # es.py:214-215 as written, for host arrays
+        ranks = xp.argsort(xp.argsort(fit)).astype(fit.dtype) / (fit.shape[0] - 1) - 0.5
+    grad = (ranks[:, None] * eps).sum(axis=0) / (cfg.pop * cfg.sigma)
+    theta = theta + cfg.lr * grad
+    backend.sync(theta)
+    return theta, fit, steps
+
+
 def generation(backend, theta, cfg, hidden, gen=1):
     """One generation of es.py:218-227 on this rank's shard of the population: perturb, roll
     out, gather every shard's (fitness, steps), rank, update. Returns (theta, fitness, steps)
-    with fitness and steps of the whole population."""
+    with fitness and steps of the whole population. A backend without the fused pieces (shard,
+    perturb, update, centered_ranks), one written against the reference's interface, runs
+    reference_generation instead."""
+    if not all(callable(getattr(backend, m, None)) for m in _FUSED):
+        return reference_generation(backend, theta, cfg, hidden, gen)
     pairs = cfg.pop // 2
     first, count = backend.shard(cfg.pop)
     members = backend.perturb(theta, cfg.sigma, gen, pairs, first, count)

@@ -218,3 +218,68 @@ def test_es_biped_learns_to_stay_up(cuda):
     final = fitness_by_generation[-1]
     record("es_legged2_p1024_60gens", final_fitness=final, generations=len(fitness_by_generation))
     assert final >= 300.0, final  # the biped stands for most of its 500-step episodes
+
+
+def test_generation_runs_a_backend_written_against_the_reference_interface(cuda):
+    """es.generation with a backend that has only the reference's interface (xp, normal,
+    rollout, sync; es.py:218-227) follows the reference's generation: eps = [half; -half],
+    g = sum_i rank_i eps_i / (P sigma), theta + lr g."""
+    import es
+
+    task = es.TASKS["cartpole"]
+    p, hidden = 64, 8
+    state = task.mlx.reset(p)
+    drawn = []
+
+    class Outside:
+        xp = torch
+
+        def __init__(self):
+            self.g = torch.Generator(device=cuda).manual_seed(5)
+
+        def normal(self, shape):
+            drawn.append(torch.randn(shape, device=cuda, generator=self.g))
+            return drawn[-1]
+
+        def rollout(self, theta_pop, hidden, horizon, assist=0.0, start_velocity=0.0):
+            return task.rollout(state, theta_pop, hidden, horizon)
+
+        def sync(self, *arrays):
+            torch.cuda.synchronize()
+
+    cfg = es.Config(pop=p, horizon=50, sigma=0.1, lr=0.1)
+    theta = torch.zeros(es.n_params(hidden, task), device=cuda)
+    new, fit, steps = es.generation(Outside(), theta, cfg, hidden)
+    eps = torch.cat([drawn[0], -drawn[0]])
+    ranks = torch.argsort(torch.argsort(fit, stable=True), stable=True).float() / (p - 1) - 0.5
+    expect = theta + cfg.lr * (ranks[:, None] * eps).sum(0) / (p * cfg.sigma)
+    assert fit.shape == (p,) and steps.shape == (p,)
+    torch.testing.assert_close(new, expect, rtol=1e-5, atol=1e-6)
+
+
+def test_generation_runs_a_subclass_with_the_reference_reset(cuda):
+    """A backend subclass that overrides reset(self, n), as the reference's tests do
+    (test_es.py:53-56), runs inside es.generation and gets its fixed states."""
+    import es
+
+    task = es.TASKS["legged2"]
+    p = 128
+    fixed = task.mlx.reset(p)
+
+    class Fixed(es.MetalBackend):
+        def reset(self, n):
+            return fixed
+
+    class FixedLoop(es.MLXBackend):
+        def reset(self, n):
+            return fixed
+
+    cfg = es.Config(task="legged2", pop=p, horizon=30)
+    theta = torch.from_numpy((np.random.default_rng(1).normal(size=es.n_params(task.hidden, task)) * 0.1)
+                             .astype(np.float32)).to(cuda)
+    outs = [es.generation(b(task, 0), theta, cfg, task.hidden, 1) for b in (Fixed, FixedLoop)]
+    for new, fit, steps in outs:
+        assert fit.shape == (p,) and steps.max().item() <= 30 and not torch.equal(new, theta)
+    # same initial states, same perturbations: the fused rollout and the loop take the same steps
+    # for almost every member (their policies round the MLP differently)
+    assert (outs[0][2] == outs[1][2]).float().mean().item() > 0.95
