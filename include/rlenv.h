@@ -12,7 +12,7 @@
  *  - The caller allocates every buffer. The library never allocates or frees
  *    memory and holds no state between calls; the one exception is
  *    rlenv_es_centered_ranks_static, whose scratch is a fixed array of the
- *    library (its address cached per device).
+ *    library (its address cached per device and context).
  *  - Work is enqueued asynchronously on `stream` (a cudaStream_t; NULL is the
  *    legacy default stream). Calls are reentrant, except that overlapping calls of
  *    rlenv_es_centered_ranks_static on one device share its scratch.
@@ -278,7 +278,9 @@ RLENV_API int rlenv_es_centered_ranks_sorted(const float* fitness, int64_t p, fl
  * held until the process exits), so 2 <= p <= 65,536 and larger p is rejected
  * with RLENV_EINVAL. The first call on each device, with that device current,
  * looks up the array's device address once; make that first call before any
- * stream capture. Nothing in the array needs to start at zero. Calls on one
+ * stream capture. The address is kept with the context it belongs to: after
+ * the device's context is replaced (cudaDeviceReset, then new work), the next
+ * call looks it up again, so again make that call outside a capture. Nothing in the array needs to start at zero. Calls on one
  * device whose executions overlap (different streams or host threads) share
  * the array and race; issue them on one stream. Same ranks, bit for bit, as
  * the other two rank entry points. */

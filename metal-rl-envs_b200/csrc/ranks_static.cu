@@ -7,6 +7,8 @@
 // written earlier in the same call. Every call on a device uses the same
 // array, so calls whose executions overlap (two streams, or two host threads
 // with their own streams) race on it; calls in one stream are ordered and safe.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -23,23 +25,56 @@ constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) uint64_t g_rank_scratch[2 * kStaticRankMembers];
 
+// The array's address is a property of the CUDA context that loaded this module. It is
+// looked up once per device and kept together with that context; when the device's current
+// context is another one (the old one was destroyed, for instance by cudaDeviceReset, and
+// the module loaded again), the address is looked up again.
+struct ScratchAddr {
+  CUcontext ctx;
+  uint64_t* addr;
+};
 std::mutex g_mu;
-uint64_t* g_addr[kMaxDevices] = {};
+ScratchAddr g_addr[kMaxDevices] = {};
 
-// The array's address in the current device's context, looked up once per device.
+using CtxGetCurrent = CUresult (*)(CUcontext*);
+
+// The driver's cuCtxGetCurrent, through the runtime (the library links only cudart).
+CtxGetCurrent ctx_get_current() {
+  static CtxGetCurrent fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<CtxGetCurrent>(nullptr);
+    return reinterpret_cast<CtxGetCurrent>(f);
+  }();
+  return fn;
+}
+
+CUcontext current_ctx() {
+  CUcontext c = nullptr;
+  const CtxGetCurrent f = ctx_get_current();
+  if (!f || f(&c) != CUDA_SUCCESS) return nullptr;
+  return c;
+}
+
+// The array's address in the current device's context.
 int scratch_for_current_device(uint64_t** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return int(e);
   if (dev < 0 || dev >= kMaxDevices) return RLENV_EUNSUPPORTED;
   std::lock_guard<std::mutex> lock(g_mu);
-  if (!g_addr[dev]) {
+  ScratchAddr& slot = g_addr[dev];
+  const CUcontext ctx = current_ctx();
+  if (!slot.addr || !ctx || ctx != slot.ctx) {
     void* a = nullptr;
-    e = cudaGetSymbolAddress(&a, g_rank_scratch);
+    e = cudaGetSymbolAddress(&a, g_rank_scratch);  // makes the device's context current if none is
     if (e != cudaSuccess) return int(e);
-    g_addr[dev] = static_cast<uint64_t*>(a);
+    slot.addr = static_cast<uint64_t*>(a);
+    slot.ctx = current_ctx();
   }
-  *out = g_addr[dev];
+  *out = slot.addr;
   return RLENV_OK;
 }
 

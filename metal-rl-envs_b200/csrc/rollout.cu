@@ -449,23 +449,22 @@ int prepare_smem(const void* fn, size_t smem) {
   return e == cudaSuccess ? RLENV_OK : int(e);
 }
 
-// Lanes per legged member when the caller leaves it open: the widest G (dividing C and H)
-// whose launch keeps every member resident at once. Members run for as long as they stay
-// up, so a launch that needs a second wave runs its longest-lived members one after another.
+// Lanes per legged member when the caller leaves it open. Measured on a B200 (legged4, H = 16,
+// horizon 1,000, an ES population after five generations): a member's time is the latency of
+// its warp's serial chain of steps, and 4 lanes shorten it only while each SM sub-partition
+// holds at most one such warp; 2 lanes never paid.
+//   P = 32:     1 lane 5.18 ms, 2 lanes 5.72, 4 lanes 4.62
+//   P = 2,048:  5.62, 6.27, 5.11          P = 4,096: 5.62, 6.28, 5.13
+//   P = 16,384: 5.71, 8.37, 7.55 (all standing: 5.36, 11.6, 11.7)
+// So 4 lanes when C and H allow it and P * 4 lanes fill at most one warp per sub-partition
+// (P <= 32 x SMs), else one.
 int legged_lanes(int c, int h, int64_t p) {
   int dev = 0, sms = 0;
+  if (c % 4 || h % 4) return 1;
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
     return 1;
-  for (int g = 4; g > 1; g /= 2) {
-    const LeggedLaunch L = pick_legged(c, h, g);
-    if (!L.fn) continue;
-    if (prepare_smem(reinterpret_cast<const void*>(L.fn), L.smem) != RLENV_OK) continue;
-    int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, L.fn, 32, L.smem) != cudaSuccess) continue;
-    if (int64_t(per_sm) * sms * (32 / g) >= p) return g;
-  }
-  return 1;
+  return p <= int64_t(32) * sms ? 4 : 1;
 }
 
 int launch_classic(ClassicRollout fn, int g, const float* state, const float* theta,

@@ -129,6 +129,8 @@ def test_legged_rollout_lane_groups_give_the_same_bits(cuda, lanes):
 
     for index in (1, 5):
         c, alive, fall, gate, assist = LEGGED_ROLLOUT_CASES[index]
+        if c % lanes:
+            continue
         state, theta = legged_rollout_inputs(index)
         st, th = torch.from_numpy(state).to(cuda), torch.from_numpy(theta).to(cuda)
         p, d = th.shape

@@ -9,6 +9,7 @@ import numpy as np
 import pytest
 import torch
 
+from oracle import es as oes
 from parity import to_np
 
 MAX_MEMBERS = 65_536
@@ -53,3 +54,22 @@ def test_static_scratch_equals_caller_scratch_on_two_calls_in_a_row(cuda, p):
     got2 = _with_static_scratch(rl, second)
     np.testing.assert_array_equal(got1, _with_caller_scratch(rl, first))
     np.testing.assert_array_equal(got2, _with_caller_scratch(rl, second))
+    # and the reference's centred ranks (es.py:214-215), ties broken by member index
+    np.testing.assert_allclose(got2, oes.centered_ranks(to_np(second)), rtol=0, atol=1e-7)
+
+
+@pytest.mark.gpu
+def test_a_warm_call_allocates_no_device_memory(cuda):
+    """The point of the entry point: once its first call on the device has set up, a call at the
+    largest size leaves the device's free memory exactly where it was."""
+    import rlenv_lib as rl
+
+    fit = torch.from_numpy(np.random.default_rng(7).normal(size=MAX_MEMBERS).astype(np.float32)).to(cuda)
+    out = torch.empty_like(fit)
+    sp = rl.stream_ptr(cuda)
+    rl.check(rl.lib().es_centered_ranks_static(fit.data_ptr(), MAX_MEMBERS, out.data_ptr(), sp))
+    torch.cuda.synchronize()
+    before = torch.cuda.mem_get_info(cuda)[0]
+    rl.check(rl.lib().es_centered_ranks_static(fit.data_ptr(), MAX_MEMBERS, out.data_ptr(), sp))
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info(cuda)[0] == before
