@@ -1,9 +1,8 @@
 """Generate the golden vectors that pin the oracle to the reference's own numpy code.
 
-Run in a container that has the reference checkout (default /root/reference, or
-$REF_PATH):
+Run where a checkout of the reference exists, with $REF_PATH naming it:
 
-    python tests/golden/make_golden.py
+    REF_PATH=<path of the reference checkout> python tests/golden/make_golden.py
 
 It imports the reference's numpy modules (cartpole_np, acrobot_np, pendulum_np,
 pendulum_aba_np, hopper_np, legged_np, and es.py with a stub `mlx` module so
@@ -22,12 +21,12 @@ from unittest import mock
 import numpy as np
 
 OUT = Path(__file__).resolve().parent
-REF = Path(os.environ.get("REF_PATH", "/root/reference"))
+REF = Path(os.environ["REF_PATH"]) if os.environ.get("REF_PATH") else None
 
 
 def _import_reference():
-    if not REF.exists():
-        raise SystemExit(f"reference checkout not found at {REF} (set REF_PATH)")
+    if REF is None or not REF.exists():
+        raise SystemExit("set REF_PATH to the reference checkout (the directory holding cartpole_np.py)")
     mlx = types.ModuleType("mlx")
     mlx.core = mock.MagicMock()
     sys.modules["mlx"] = mlx
