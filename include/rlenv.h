@@ -61,6 +61,15 @@ RLENV_API const char* rlenv_strerror(int code);
 /* Version of this ABI: bumped whenever a signature below changes. */
 RLENV_API int rlenv_abi_version(void);
 
+/* The check build (librlenv_checks.so, compiled with -DRLENV_CHECKS; no
+ * counterpart in the reference, whose Metal kernels cannot report). Its kernels
+ * record problems in a device word instead of trapping: bit 1 an action outside
+ * its body's range, bit 2 a non-finite value written to an output. This reads
+ * the OR of every kernel's word on the current device into *word and, with
+ * clear, zeroes them. It synchronises the device. In the normal build it
+ * returns RLENV_EUNSUPPORTED and touches no GPU. */
+RLENV_API int rlenv_checks_status(unsigned int* word, int clear);
+
 /* ---- CartPole ------------------------------------------------------------
  * Replaces `cartpole_step` (cartpole_metal.py:69-104, launched at :114-125).
  * state (4, n) rows x, x_dot, theta, theta_dot; action 1 pushes right, anything

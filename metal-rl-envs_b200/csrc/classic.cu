@@ -27,6 +27,7 @@ namespace {
 struct CartPoleEnv {
   using S = CartPole;
   struct Aux {};
+  static constexpr int kActions = 2;
   static constexpr int kVec = 4;
   // 128 threads: 131,072 environments make 1,024 blocks, 6.9 per SM, against 3.5 (so
   // 4 on some SMs, 3 on others) with 256 threads: 145 against 133 B env-steps/s on a B200
@@ -52,6 +53,7 @@ struct CartPoleEnv {
 struct AcrobotEnv {
   using S = Acrobot;
   using Aux = AcrobotTrig;
+  static constexpr int kActions = 3;
   static constexpr int kVec = 1;
   // 8 resident blocks of 256 threads (at most 32 registers): the whole batch of a
   // 262,144-environment launch is resident at once instead of 1.15 waves
@@ -64,8 +66,8 @@ struct AcrobotEnv {
   RLENV_D static Aux aux(const S& s) { return acrobot_trig(s); }
   RLENV_D static bool step(S& s, Aux& t, int a, uint32_t h, float& reward) {
     const S nx = acrobot_physics(s, t, float(a - 1));
-    const Aux tn = acrobot_trig(nx);
-    const bool d = acrobot_terminated(tn);
+    Aux tn;
+    const bool d = acrobot_trig_terminated(nx, tn);
     if (d) {  // rare under random actions: the fresh state's trig only on this branch
       s = S{uniform_pm(pcg_hash(h + classic_row_offset(0)), ac::RESET_BOUND),
             uniform_pm(pcg_hash(h + classic_row_offset(1)), ac::RESET_BOUND),
@@ -191,18 +193,21 @@ step_many_kernel(const float* __restrict__ state_in, const A* __restrict__ actio
   // the next step's actions are loaded one step ahead, so their latency hides behind a step
   int act[V];
   if (T > 0) load_actions<A, V>(actions, i, act);
-  for (int64_t t = 0; t < T; ++t) {
+  int64_t row = i;  // t * n + i, advanced by n per step
+  for (int64_t t = 0; t < T; ++t, row += n) {
     int nxt[V] = {};
-    if (t + 1 < T) load_actions<A, V>(actions, (t + 1) * n + i, nxt);
+    if (t + 1 < T) load_actions<A, V>(actions, row + n, nxt);
     bool d[V];
     float rw[V];
+#pragma unroll
+    for (int u = 0; u < V; ++u) check_flag(act[u] < 0 || act[u] >= Env::kActions, kCheckActionRange);
 #pragma unroll
     for (int u = 0; u < V; ++u)
       d[u] = Env::step(st[u], aux[u], act[u], env_hash(seed0 + uint32_t(t), off + i + u), rw[u]);
 #pragma unroll
     for (int u = 0; u < V; ++u) act[u] = nxt[u];
-    if (SEQ || reward_seq) store_vec<V>(reward_seq, t * n + i, rw);
-    if (SEQ || done_seq) store_flags<V>(done_seq, t * n + i, d);
+    if (SEQ || reward_seq) store_vec<V>(reward_seq, row, rw);
+    if (SEQ || done_seq) store_flags<V>(done_seq, row, d);
     if constexpr (SUMS) {
 #pragma unroll
       for (int u = 0; u < V; ++u) {
@@ -210,6 +215,12 @@ step_many_kernel(const float* __restrict__ state_in, const A* __restrict__ actio
         dcnt[u] += d[u] ? 1.0f : 0.0f;
       }
     }
+  }
+#pragma unroll
+  for (int u = 0; u < V; ++u) {
+    float r[4];
+    Env::to(st[u], r);
+    check_flag(!(isfinite(r[0]) && isfinite(r[1]) && isfinite(r[2]) && isfinite(r[3])), kCheckNonFinite);
   }
   store_states<Env, V>(state_out, n, i, st);
   if constexpr (SUMS) {

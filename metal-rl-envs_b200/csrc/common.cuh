@@ -268,3 +268,40 @@ int with_action_type(int dtype, F&& f) {
 }
 
 }  // namespace rlenv
+
+// ---- the check build -----------------------------------------------------------
+// Compiled with -DRLENV_CHECKS (rlenv_build.build(checks=True), librlenv_checks.so), the
+// kernels record what they find wrong in a device word instead of trapping: an action
+// outside its body's range, a non-finite value in an output. Each translation unit has its
+// own word and registers a host reader for it when the library loads; rlenv_checks_status
+// (checks.cu) reads and clears all of them. In the normal build check_flag is empty.
+namespace rlenv {
+enum CheckBit : unsigned { kCheckActionRange = 1u, kCheckNonFinite = 2u };
+}  // namespace rlenv
+#ifdef RLENV_CHECKS
+namespace rlenv {
+static __device__ unsigned int g_check_word;
+void register_check_reader(int (*reader)(unsigned int*, bool));
+namespace {
+int read_check_word(unsigned int* out, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(out, g_check_word, sizeof(unsigned int));
+  if (e == cudaSuccess && clear && *out) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(g_check_word, &zero, sizeof(unsigned int));
+  }
+  return e == cudaSuccess ? RLENV_OK : int(e);
+}
+struct CheckReaderRegistration {
+  CheckReaderRegistration() { register_check_reader(&read_check_word); }
+};
+CheckReaderRegistration g_check_reader_registration;
+}  // namespace
+RLENV_D void check_flag(bool bad, unsigned int bit) {
+  if (bad) atomicOr(&g_check_word, bit);
+}
+}  // namespace rlenv
+#else
+namespace rlenv {
+RLENV_D void check_flag(bool, unsigned int) {}
+}  // namespace rlenv
+#endif

@@ -17,6 +17,9 @@ RLENV_D int action_at(const void* a, int dtype, int64_t i) {
   }
 }
 
+template <int C>
+constexpr int kActionsOf = C == 1 ? 3 : C == 2 ? 9 : C == 3 ? 27 : 81;  // 3^C
+
 // Per-leg torques from an action index in [0, 3^C): leg k gets
 // ((a / 3^k) % 3 - 1) * TORQUE (legged_np.py:51-54).
 template <int C>
@@ -60,6 +63,7 @@ legged_kernel(const float* __restrict__ state, const void* __restrict__ actions,
   int act = T > 0 ? action_at(actions, dtype, e) : 0;  // loaded one step ahead
   for (int64_t t = 0; t < T; ++t) {
     float tq[C];
+    check_flag(act < 0 || act >= kActionsOf<C>, kCheckActionRange);
     decode_torques<C>(act, tq);
     if (t + 1 < T) act = action_at(actions, dtype, (t + 1) * n + e);
     float imp[2 * C];
@@ -70,7 +74,10 @@ legged_kernel(const float* __restrict__ state, const void* __restrict__ actions,
       legged_substep<C, 1, BRANCHY, IMPULSES>(qt, vt, ql, vl, tq, k_assist, iters, nullptr, 0, true, imp);
     if constexpr (IMPULSES) {
 #pragma unroll
-      for (int k = 0; k < 2 * C; ++k) impulse_seq[(t * 2 * C + k) * n + e] = imp[k];
+      for (int k = 0; k < 2 * C; ++k) {
+        check_flag(!isfinite(imp[k]), kCheckNonFinite);
+        impulse_seq[(t * 2 * C + k) * n + e] = imp[k];
+      }
     }
     const bool d = legged_terminated(qt);
     const float rw = d ? 0.0f : vt[0] + 1.0f;
@@ -90,6 +97,7 @@ legged_kernel(const float* __restrict__ state, const void* __restrict__ actions,
   }
 #pragma unroll
   for (int i = 0; i < nq; ++i) {
+    check_flag(!(isfinite(i < 3 ? qt[i] : ql[i - 3]) && isfinite(i < 3 ? vt[i] : vl[i - 3])), kCheckNonFinite);
     next[i * n + e] = i < 3 ? qt[i] : ql[i - 3];
     next[(nq + i) * n + e] = i < 3 ? vt[i] : vl[i - 3];
   }

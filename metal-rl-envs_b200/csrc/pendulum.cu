@@ -88,6 +88,9 @@ int rlenv_pendulum_aba_step(int k, const float* state, const void* action, int a
   using namespace rlenv::pend;
   if (n > 0 && (!reward || !done)) return RLENV_EINVAL;
   if (int rc = check_args(state, action, action_dtype, 1, n, next_state)) return rc;
+  if (k > rlenv::kUnrollLinks)
+    return launch_aba_long(k, state, action, action_dtype, seed, 1, n, index_offset, next_state,
+                           reward, done, stream);
   StepFn fn = pick_aba(k);
   if (!fn) return RLENV_EUNSUPPORTED;
   return launch(fn, n, 128, state, action, action_dtype, seed, 1, n, index_offset, next_state,
@@ -100,6 +103,9 @@ int rlenv_pendulum_aba_step_many(int k, const float* state, const void* actions,
                                  void* stream) {
   using namespace rlenv::pend;
   if (int rc = check_args(state, actions, action_dtype, steps, n, state_out)) return rc;
+  if (k > rlenv::kUnrollLinks)
+    return launch_aba_long(k, state, actions, action_dtype, seed0, steps, n, index_offset, state_out,
+                           reward_seq, done_seq, stream);
   StepFn fn = pick_aba(k);
   if (!fn) return RLENV_EUNSUPPORTED;
   return launch(fn, n, 128, state, actions, action_dtype, seed0, steps, n, index_offset, state_out,

@@ -1,4 +1,5 @@
-// Articulated-body pendulum kernels, one thread per environment.
+// Articulated-body pendulum kernels for K <= 16, one thread per environment with every
+// per-link array in registers (longer chains: pendulum_long.cu).
 #include "pendulum_kernels.cuh"
 
 namespace rlenv {
@@ -10,7 +11,6 @@ StepFn pick_aba(int k) {
   case KK: return &pendulum_kernel<KK, ARTICULATED>;
     RLENV_K(1) RLENV_K(2) RLENV_K(3) RLENV_K(4) RLENV_K(5) RLENV_K(6) RLENV_K(7) RLENV_K(8)
     RLENV_K(9) RLENV_K(10) RLENV_K(11) RLENV_K(12) RLENV_K(13) RLENV_K(14) RLENV_K(15) RLENV_K(16)
-    RLENV_K(24) RLENV_K(32) RLENV_K(48) RLENV_K(64)
 #undef RLENV_K
     default: return nullptr;
   }

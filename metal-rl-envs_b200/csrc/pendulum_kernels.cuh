@@ -44,6 +44,7 @@ pendulum_kernel(const float* __restrict__ state, const void* __restrict__ action
   // each step's action is loaded one step ahead, off the step's dependency chain
   int act = T > 0 ? action_at(actions, dtype, e) : 0;
   for (int64_t t = 0; t < T; ++t) {
+    check_flag(act < 0 || act > 2, kCheckActionRange);
     const float torque = float(act - 1) * pd::TORQUE;
     if (t + 1 < T) act = action_at(actions, dtype, (t + 1) * n + e);
     if constexpr (FORM == ARTICULATED) {
@@ -68,6 +69,7 @@ pendulum_kernel(const float* __restrict__ state, const void* __restrict__ action
     if (done_seq) done_seq[t * n + e] = d;
   }
   for_range<K, U>([&](int j) {
+    check_flag(!(isfinite(th[j]) && isfinite(om[j])), kCheckNonFinite);
     next[j * n + e] = th[j];
     next[(K + j) * n + e] = om[j];
   });
@@ -188,7 +190,11 @@ using StepFn = void (*)(const float*, const void*, int, uint32_t, int64_t, int64
 // Per-translation-unit pickers: nullptr when the unit does not build this K.
 StepFn pick_mm_lo(int k, bool pairwise);    // k in 1..8
 StepFn pick_mm_hi(int k, bool pairwise);    // k in 9..16
-StepFn pick_aba(int k);                     // k in 1..16, 24, 32, 48, 64
+StepFn pick_aba(int k);                     // k in 1..16
+// The articulated body for 2 <= k <= 192 with its per-link arrays in shared memory (pendulum_long.cu).
+int launch_aba_long(int k, const float* state, const void* actions, int dtype, uint32_t seed0,
+                    int64_t T, int64_t n, int64_t off, float* next, float* reward_seq,
+                    uint8_t* done_seq, void* stream);
 StepFn pick_coop(int k);                    // k in 2, 4, 8, 16, 32
 
 }  // namespace pend

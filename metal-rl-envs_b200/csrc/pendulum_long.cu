@@ -1,0 +1,252 @@
+// Articulated-body pendulum for long chains (pendulum_aba_np.py:30-132): one thread per
+// environment, any K from 2 to kMaxLongLinks chosen at run time, every per-link array in
+// shared memory.
+//
+// A thread keeps nine arrays of K floats: the state (theta, omega), the RK4 stage state,
+// the RK4 sums, and the three values the articulated-body inward pass hands to the last
+// pass (u / D, U1 / D, U2 / D; U0 / D is 1). Kept in local memory, as the register form does
+// for short chains, 4 KB per environment at K = 64 missed L1 and L2 and the kernel waited on
+// memory. Two things keep the count at nine:
+// - link velocities are not stored: the outward pass keeps only the last link's, the inward
+//   pass walks them back link by link through the inverse joint transform (a rotation and a
+//   shift), and the last pass recomputes them forward;
+// - each joint's sine and cosine come from the special function unit in every pass
+//   (sincos_sfu) instead of being stored.
+// The last pass also applies the RK4 stage update to each link as soon as its acceleration is
+// known, so no acceleration array is kept. Arrays are laid out (array, link, thread), so the
+// 32 threads of a block touch 32 consecutive words: no bank conflicts.
+#include "pendulum_kernels.cuh"
+
+namespace rlenv {
+namespace pend {
+
+constexpr int kLongBlock = 32;
+constexpr int kLongArrays = 9;
+constexpr int kMaxLongLinks = 192;  // 9 K floats x 32 threads within 227 KB of shared memory
+enum LongArray { kTh = 0, kOm, kTs, kOs, kDth, kDom, kGu, kU1, kU2 };
+
+size_t long_smem_bytes(int k) { return size_t(kLongArrays) * k * kLongBlock * sizeof(float); }
+
+// The hardware reciprocal (within one ulp): on the inward pass's serial chain, where the
+// correctly rounded division would add its slow-path sequence to every link.
+RLENV_D float rcp_approx(float a) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
+  return r;
+}
+
+struct LongLinks {
+  float* base;  // array 0, link 0 of this thread
+  int k;
+  RLENV_D float& at(int a, int i) const { return base[(a * k + i) * kLongBlock]; }
+};
+
+// Accelerations of the stage whose angles and velocities are arrays (ia, io), applied at once as
+// RK4 stage `stage` (0..3): pendulum_rk4's update for link i, written into the stage, sum and
+// state arrays (pendulum_np.py:60-66).
+RLENV_D void aba_stage(const LongLinks& L, int ia, int io, float torque, int stage) {
+  const int k = L.k;
+  // ---- outward: link velocities v_i = X_i v_{i-1} + S qd_i; only the last is kept
+  float vw = L.at(io, 0), vx = 0.0f, vy = 0.0f;
+  {
+    float pth = L.at(ia, 0), pom = vw;
+#pragma unroll 4
+    for (int i = 1; i < k; ++i) {
+      const float th = L.at(ia, i), om = L.at(io, i);
+      float s, c;
+      sincos_sfu(th - pth, &s, &c);
+      const float xy = vy + vw;  // joint at (1, 0) of the parent
+      const float nx = c * vx + s * xy, ny = -s * vx + c * xy;
+      vw = vw + (om - pom);
+      vx = nx;
+      vy = ny;
+      pth = th;
+      pom = om;
+    }
+  }
+  // ---- inward: articulated inertia and bias of each subtree, carried to the parent; the link
+  // velocities walked back from the last (x_{i-1} = c x_i - s y_i, y_{i-1} = s x_i + c y_i - w_{i-1})
+  float cI00 = 0.0f, cI01 = 0.0f, cI02 = 0.0f, cI11 = 0.0f, cI12 = 0.0f, cI22 = 0.0f;
+  float cp0 = 0.0f, cp1 = 0.0f, cp2 = 0.0f;
+  {
+    float th = L.at(ia, k - 1), om = L.at(io, k - 1);
+#pragma unroll 2
+    for (int i = k - 1; i >= 1; --i) {
+      const float pth = L.at(ia, i - 1), pom = L.at(io, i - 1);
+      const float qd = om - pom;
+      float s, c;
+      sincos_sfu(th - pth, &s, &c);
+      const float w = vw, x = vx, y = vy;
+      // own bias p = v x* (I v), I of a unit mass at (1, 0) = [[1,0,1],[0,1,0],[1,0,1]]
+      const float fy = w + y;
+      const float p0 = (x * fy - y * x) + cp0, p1 = (-w * fy) + cp1, p2 = (w * x) + cp2;
+      const float a00 = 1.0f + cI00, a01 = cI01, a02 = 1.0f + cI02;
+      const float a11 = 1.0f + cI11, a12 = cI12, a22 = 1.0f + cI22;
+      const float r = rcp_approx(a00);
+      const float Ia00 = a00 - a00 * a00 * r, Ia01 = a01 - a00 * a01 * r, Ia02 = a02 - a00 * a02 * r;
+      const float Ia11 = a11 - a01 * a01 * r, Ia12 = a12 - a01 * a02 * r, Ia22 = a22 - a02 * a02 * r;
+      const float c1 = qd * y, c2 = -qd * x;
+      const float g = -p0 * r;
+      L.at(kGu, i) = g;
+      L.at(kU1, i) = a01 * r;
+      L.at(kU2, i) = a02 * r;
+      const float pa0 = p0 + (Ia01 * c1 + Ia02 * c2) + a00 * g;
+      const float pa1 = p1 + (Ia11 * c1 + Ia12 * c2) + a01 * g;
+      const float pa2 = p2 + (Ia12 * c1 + Ia22 * c2) + a02 * g;
+      const float B00 = Ia00 + Ia01 * s + Ia02 * c, B01 = Ia01 * c - Ia02 * s, B02 = Ia01 * s + Ia02 * c;
+      const float B10 = Ia01 + Ia11 * s + Ia12 * c, B11 = Ia11 * c - Ia12 * s, B12 = Ia11 * s + Ia12 * c;
+      const float B20 = Ia02 + Ia12 * s + Ia22 * c, B21 = Ia12 * c - Ia22 * s, B22 = Ia12 * s + Ia22 * c;
+      cI00 = B00 + s * B10 + c * B20;
+      cI01 = B01 + s * B11 + c * B21;
+      cI02 = B02 + s * B12 + c * B22;
+      cI11 = c * B11 - s * B21;
+      cI12 = c * B12 - s * B22;
+      cI22 = s * B12 + c * B22;
+      cp0 = pa0 + s * pa1 + c * pa2;
+      cp1 = c * pa1 - s * pa2;
+      cp2 = s * pa1 + c * pa2;
+      // the parent's velocity
+      const float pw = w - qd;
+      vx = c * x - s * y;
+      vy = (s * x + c * y) - pw;
+      vw = pw;
+      th = pth;
+      om = pom;
+    }
+  }
+  // ---- last pass: accelerations outward from the root (gravity as a base acceleration -G),
+  // each link's RK4 stage update applied as soon as its acceleration is known
+  const float th0 = L.at(ia, 0), om0 = L.at(io, 0);
+  float ax, ay, aw, run;
+  {
+    const float U0_0 = 1.0f + cI00, U1_0 = cI01, U2_0 = 1.0f + cI02;
+    const float uu0 = torque - cp0;  // the root's own bias is zero: v_0 = (qd_0, 0, 0)
+    float sn0, cs0;
+    sincos_sfu(th0, &sn0, &cs0);
+    ax = cs0 * -pd::G;
+    ay = -sn0 * -pd::G;
+    const float qdd = (uu0 - (U1_0 * ax + U2_0 * ay)) * rcp_approx(U0_0);
+    aw = qdd;
+    run = qdd;
+  }
+  auto update = [&](int i, float th_in, float om_in, float a) {
+    float& th = L.at(kTh, i);
+    float& om = L.at(kOm, i);
+    switch (stage) {
+      case 0:
+        L.at(kDth, i) = om_in;
+        L.at(kDom, i) = a;
+        L.at(kTs, i) = th + pd::HALF_DT * om_in;
+        L.at(kOs, i) = om + pd::HALF_DT * a;
+        break;
+      case 1:
+      case 2:
+        L.at(kDth, i) += 2.0f * om_in;
+        L.at(kDom, i) += 2.0f * a;
+        L.at(kTs, i) = th + (stage == 1 ? pd::HALF_DT : pd::DT) * om_in;
+        L.at(kOs, i) = om + (stage == 1 ? pd::HALF_DT : pd::DT) * a;
+        break;
+      default:
+        th = pd_wrap(th + pd::SIXTH_DT * (L.at(kDth, i) + om_in));
+        om = fminf(fmaxf(om + pd::SIXTH_DT * (L.at(kDom, i) + a), -pd::MAX_VEL), pd::MAX_VEL);
+        break;
+    }
+    (void)th_in;
+  };
+  update(0, th0, om0, run);
+  {
+    float pth = th0, pom = om0;
+    float w = om0, x = 0.0f, y = 0.0f;  // link velocity, forward again
+#pragma unroll 4
+    for (int i = 1; i < k; ++i) {
+      const float th = L.at(ia, i), om = L.at(io, i);  // read before this link's update rewrites them
+      const float qd = om - pom;
+      float s, c;
+      sincos_sfu(th - pth, &s, &c);
+      const float vxy = y + w;
+      const float nx = c * x + s * vxy, ny = -s * x + c * vxy;
+      w = w + qd;
+      x = nx;
+      y = ny;
+      const float c1 = qd * y, c2 = -qd * x;
+      const float xy = ay + aw;
+      const float ap1 = c * ax + s * xy + c1;
+      const float ap2 = -s * ax + c * xy + c2;
+      const float q2 = L.at(kGu, i) - aw - L.at(kU1, i) * ap1 - L.at(kU2, i) * ap2;
+      aw = aw + q2;
+      ax = ap1;
+      ay = ap2;
+      run += q2;
+      update(i, th, om, run);
+      pth = th;
+      pom = om;
+    }
+  }
+}
+
+// T steps per launch for N environments; step t reads actions[t * n + e], draws its resets
+// from seed0 + t and writes reward_seq / done_seq row t when those are not null.
+__global__ void __launch_bounds__(kLongBlock)
+pendulum_aba_long_kernel(int k, const float* __restrict__ state, const void* __restrict__ actions,
+                         int dtype, uint32_t seed0, int64_t T, int64_t n, int64_t off,
+                         float* __restrict__ next, float* __restrict__ reward_seq,
+                         uint8_t* __restrict__ done_seq) {
+  extern __shared__ float links[];
+  const int64_t e = int64_t(blockIdx.x) * kLongBlock + threadIdx.x;
+  if (e >= n) return;
+  const LongLinks L{links + threadIdx.x, k};
+  for (int j = 0; j < k; ++j) {
+    L.at(kTh, j) = __ldg(state + j * n + e);
+    L.at(kOm, j) = __ldg(state + (k + j) * n + e);
+  }
+  int act = T > 0 ? action_at(actions, dtype, e) : 0;
+  for (int64_t t = 0; t < T; ++t) {
+    check_flag(act < 0 || act > 2, kCheckActionRange);
+    const float torque = float(act - 1) * pd::TORQUE;
+    if (t + 1 < T) act = action_at(actions, dtype, (t + 1) * n + e);
+    aba_stage(L, kTh, kOm, torque, 0);
+    aba_stage(L, kTs, kOs, torque, 1);
+    aba_stage(L, kTs, kOs, torque, 2);
+    aba_stage(L, kTs, kOs, torque, 3);
+    // the tip above half the chain's length: -sum_j cos t_j > K / 2
+    float h = 0.0f;
+    for (int j = 0; j < k; ++j) h += cos_fast(L.at(kTh, j));
+    const bool d = -h > float(k) * 0.5f;
+    if (d) {
+      const uint32_t hs = env_hash(seed0 + uint32_t(t), off + e);
+      for (int j = 0; j < k; ++j) {
+        L.at(kTh, j) = uniform_pm(pcg_hash(hs + uint32_t(j) * kRowStride), pd::RESET_BOUND);
+        L.at(kOm, j) = uniform_pm(pcg_hash(hs + uint32_t(k + j) * kRowStride), pd::RESET_BOUND);
+      }
+    }
+    if (reward_seq) reward_seq[t * n + e] = d ? 0.0f : -1.0f;
+    if (done_seq) done_seq[t * n + e] = d;
+  }
+  for (int j = 0; j < k; ++j) {
+    check_flag(!(isfinite(L.at(kTh, j)) && isfinite(L.at(kOm, j))), kCheckNonFinite);
+    next[j * n + e] = L.at(kTh, j);
+    next[(k + j) * n + e] = L.at(kOm, j);
+  }
+}
+
+int launch_aba_long(int k, const float* state, const void* actions, int dtype, uint32_t seed0,
+                    int64_t T, int64_t n, int64_t off, float* next, float* reward_seq,
+                    uint8_t* done_seq, void* stream) {
+  if (k < 2 || k > kMaxLongLinks) return RLENV_EUNSUPPORTED;
+  if (n == 0) return RLENV_OK;
+  const size_t smem = long_smem_bytes(k);
+  cudaError_t e = cudaFuncSetAttribute(pendulum_aba_long_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(pendulum_aba_long_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             int(cudaSharedmemCarveoutMaxShared));
+  if (e != cudaSuccess) return int(e);
+  const int64_t blocks = (n + kLongBlock - 1) / kLongBlock;
+  if (blocks > int64_t(0x7fffffff)) return RLENV_EINVAL;
+  pendulum_aba_long_kernel<<<int(blocks), kLongBlock, smem, as_stream(stream)>>>(
+      k, state, actions, dtype, seed0, T, n, off, next, reward_seq, done_seq);
+  return launch_status();
+}
+
+}  // namespace pend
+}  // namespace rlenv

@@ -323,6 +323,7 @@ legged_rollout_kernel(const float* __restrict__ state, const float* __restrict__
     }
   }
   if (valid && gl == 0) {
+    check_flag(!isfinite(ret), kCheckNonFinite);
     fitness[m] = ret;
     steps[m] = taken;
   }

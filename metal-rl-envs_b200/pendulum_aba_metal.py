@@ -5,7 +5,8 @@ Drop-in for the reference module of the same name (pendulum_aba_metal.py:1-144):
 state, action, reward and reset conventions as pendulum_metal; the
 accelerations come from three O(K) passes over the links (outward velocities,
 inward articulated inertias and bias forces, outward accelerations) instead of
-a K x K solve. Built for K = 1..16, 24, 32, 48, 64.
+a K x K solve. Built for any K from 1 to 192 (K > 16 with its per-link arrays in
+shared memory).
 """
 
 import rlenv_lib as _rl

@@ -20,6 +20,10 @@ CSRC = HERE / "csrc"
 INCLUDE = HERE.parent / "include"
 OBJ = HERE / "_build"
 LIB = HERE / "librlenv.so"
+# the check build: the same sources with -DRLENV_CHECKS (kernels record bad actions and
+# non-finite outputs in a device word that rlenv_checks_status reads)
+OBJ_CHECKS = HERE / "_build_checks"
+LIB_CHECKS = HERE / "librlenv_checks.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC",
@@ -64,34 +68,35 @@ def _compile(src, obj, extra, verbose):
     return r.stdout + r.stderr
 
 
-def build(verbose=False, ptxas_verbose=False, jobs=None):
-    """Compile every csrc/*.cu for sm_100a and link librlenv.so. Returns its path."""
-    OBJ.mkdir(exist_ok=True)
+def build(verbose=False, ptxas_verbose=False, jobs=None, checks=False):
+    """Compile every csrc/*.cu for sm_100a and link librlenv.so (librlenv_checks.so with
+    checks=True). Returns its path."""
+    obj_dir, lib = (OBJ_CHECKS, LIB_CHECKS) if checks else (OBJ, LIB)
+    obj_dir.mkdir(exist_ok=True)
     sources = sorted(CSRC.glob("*.cu"))
-    extra = ["-Xptxas", "-v"] if ptxas_verbose else []
-    todo = [s for s in sources if ptxas_verbose or _stale(s, OBJ / (s.stem + ".o"))]
+    extra = (["-Xptxas", "-v"] if ptxas_verbose else []) + (["-DRLENV_CHECKS"] if checks else [])
+    todo = [s for s in sources if ptxas_verbose or _stale(s, obj_dir / (s.stem + ".o"))]
     logs = {}
     if todo:
         with concurrent.futures.ThreadPoolExecutor(max_workers=jobs or min(len(todo), os.cpu_count() or 4)) as ex:
-            futs = {ex.submit(_compile, s, OBJ / (s.stem + ".o"), extra, verbose): s for s in todo}
+            futs = {ex.submit(_compile, s, obj_dir / (s.stem + ".o"), extra, verbose): s for s in todo}
             for f in concurrent.futures.as_completed(futs):
                 logs[futs[f].name] = f.result()
-    objs = [OBJ / (s.stem + ".o") for s in sources]
-    if todo or not LIB.exists() or any(o.stat().st_mtime > LIB.stat().st_mtime for o in objs):
-        tmp = LIB.with_suffix(".so.tmp")
+    objs = [obj_dir / (s.stem + ".o") for s in sources]
+    if todo or not lib.exists() or any(o.stat().st_mtime > lib.stat().st_mtime for o in objs):
+        tmp = lib.with_suffix(".so.tmp")
         cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-lcudart"]
         if verbose:
             print(" ".join(cmd), flush=True)
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
-        os.replace(tmp, LIB)
+        os.replace(tmp, lib)
     if ptxas_verbose:
         for name in sorted(logs):
             print(f"==== {name}\n{logs[name]}")
-    return LIB
+    return lib
 
 
 if __name__ == "__main__":
-    build(verbose="-v" in sys.argv, ptxas_verbose="--ptxas" in sys.argv)
-    print(LIB)
+    print(build(verbose="-v" in sys.argv, ptxas_verbose="--ptxas" in sys.argv, checks="--checks" in sys.argv))

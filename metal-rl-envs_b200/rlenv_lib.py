@@ -13,6 +13,7 @@ There is no CPU path: a missing library or a missing CUDA device raises.
 """
 
 import ctypes
+import os
 from ctypes import c_float, c_int, c_int64, c_uint32, c_uint64, c_void_p
 from pathlib import Path
 
@@ -20,6 +21,8 @@ import numpy as np
 import torch
 
 LIB_PATH = Path(__file__).resolve().parent / "librlenv.so"
+# RLENV_LIBRARY=checks loads the check build instead (rlenv_build.build(checks=True))
+CHECKS_LIB_PATH = Path(__file__).resolve().parent / "librlenv_checks.so"
 
 I32, I64, U8 = 0, 1, 2
 _DTYPES = {torch.int32: I32, torch.int64: I64, torch.uint8: U8, torch.bool: U8}
@@ -28,6 +31,7 @@ _DTYPES = {torch.int32: I32, torch.int64: I64, torch.uint8: U8, torch.bool: U8}
 _RESTYPES = {"rlenv_es_ranks_scratch_bytes": c_int64}
 _SIGNATURES = {
     "rlenv_abi_version": [],
+    "rlenv_checks_status": [c_void_p, c_int],
     "rlenv_cartpole_step": [c_void_p, c_void_p, c_int, c_uint32, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p],
     "rlenv_cartpole_step_many": [c_void_p, c_void_p, c_int, c_uint32, c_int64, c_int64, c_int64, c_void_p, c_void_p,
                                  c_void_p, c_void_p, c_void_p, c_void_p],
@@ -90,9 +94,12 @@ class _Lib:
         return self.cdll.rlenv_strerror(code).decode()
 
 
-def load(path=LIB_PATH):
-    """The loaded library. Raises if it has not been built (there is no fallback)."""
+def load(path=None):
+    """The loaded library. Raises if it has not been built (there is no fallback).
+    RLENV_LIBRARY=checks in the environment selects the check build."""
     global _lib
+    if path is None:
+        path = CHECKS_LIB_PATH if os.environ.get("RLENV_LIBRARY") == "checks" else LIB_PATH
     if _lib is None:
         if not Path(path).exists():
             raise RuntimeError(f"{path} is not built; run metal-rl-envs_b200/rlenv_build.py "
@@ -108,6 +115,17 @@ def lib():
 def exported_symbols():
     """Names of every entry point this binding declares (for ABI tests)."""
     return sorted(list(_SIGNATURES) + ["rlenv_strerror"])
+
+
+CHECK_BITS = {1: "an action outside its body's range", 2: "a non-finite value written to an output"}
+
+
+def checks_status(clear=True):
+    """(word, [messages]) from the check build's device words (rlenv_checks_status), cleared
+    with clear. Raises ValueError in the normal build, which records nothing."""
+    word = ctypes.c_uint(0)
+    check(lib().checks_status(ctypes.byref(word), 1 if clear else 0))
+    return word.value, [m for b, m in CHECK_BITS.items() if word.value & b]
 
 
 def check(rc):

@@ -23,7 +23,7 @@ int main(void) {
   expect(rlenv_cartpole_step(NULL, NULL, RLENV_I32, 1, 0, 0, NULL, NULL, NULL, NULL), RLENV_OK, "empty batch");
   expect(rlenv_acrobot_step_many(fake, fake, RLENV_U8, 1, -1, 4, 0, fake, NULL, NULL, NULL, NULL, NULL),
          RLENV_EINVAL, "negative steps");
-  expect(rlenv_pendulum_aba_step(65, fake, fake, RLENV_I32, 1, 4, 0, fake, fake, fake, NULL), RLENV_EUNSUPPORTED,
+  expect(rlenv_pendulum_aba_step(193, fake, fake, RLENV_I32, 1, 4, 0, fake, fake, fake, NULL), RLENV_EUNSUPPORTED,
          "unbuilt K");
   expect(rlenv_legged_step_many(5, 8, fake, fake, RLENV_I32, 1, fake, 0.0f, NULL, 3, 4, 0, fake, NULL, NULL, NULL,
                                 NULL),

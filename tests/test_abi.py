@@ -54,7 +54,7 @@ def test_arguments_rejected_before_launch(lib):
     assert lib.cartpole_step(None, None, 0, 1, 0, 0, None, None, None, None) == 0     # empty batch: nothing to do
     assert lib.pendulum_mm_step(17, 0, fake, fake, 0, 1, 4, 0, fake, fake, fake, None) == -2
     assert lib.pendulum_coop_step(3, fake, fake, 0, 1, 4, 0, fake, fake, fake, None) == -2
-    assert lib.pendulum_aba_step(65, fake, fake, 0, 1, 4, 0, fake, fake, fake, None) == -2
+    assert lib.pendulum_aba_step(193, fake, fake, 0, 1, 4, 0, fake, fake, fake, None) == -2
     assert lib.legged_step(5, 8, fake, fake, 0, 1, fake, 0.0, None, 4, 0, fake, fake, fake, None, None) == -2
     assert lib.legged_step(2, 0, fake, fake, 0, 1, fake, 0.0, None, 4, 0, fake, fake, fake, None, None) == -1  # iters < 1
     assert lib.pendulum_mm_step_many(17, 0, fake, fake, 0, 1, 5, 4, 0, fake, None, None, None) == -2

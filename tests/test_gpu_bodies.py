@@ -82,9 +82,10 @@ def test_articulated_body_matches_reference(cuda, k):
     check_step(f"pendulum_aba_k{k}", out, g[f"aba_stepped_k{k}"], g[f"aba_done_k{k}"], onext, rtol, atol)
 
 
-@pytest.mark.parametrize("k", [24, 48])
+@pytest.mark.parametrize("k", [17, 24, 37, 48, 100, 192])
 def test_articulated_body_long_chains_match_oracle(cuda, k):
-    """K values with no golden vector: the oracle (itself pinned to the reference's numpy at
+    """K values with no golden vector, any K up to 192 as the reference's template accepts any K
+    (pendulum_aba_metal.py:121-144): the oracle (itself pinned to the reference's numpy at
     K = 2..64) on seeded states of the reference test's distribution."""
     import pendulum_aba_metal
 
@@ -105,7 +106,30 @@ def test_unsupported_k_raises(cuda):
     with pytest.raises(ValueError):
         pendulum_metal.Pendulum(17).step(torch.zeros((34, 4), device=cuda), torch.ones(4, dtype=torch.int64, device=cuda))
     with pytest.raises(ValueError):
-        pendulum_aba_metal.Pendulum(65).step(torch.zeros((130, 4), device=cuda), torch.ones(4, dtype=torch.int64, device=cuda))
+        pendulum_aba_metal.Pendulum(193).step(torch.zeros((386, 4), device=cuda), torch.ones(4, dtype=torch.int64, device=cuda))
+
+
+@pytest.mark.parametrize("k", [20, 64])
+def test_articulated_body_long_chain_trajectory(cuda, k):
+    """50 chained steps of a long chain against the oracle's chain with the same resets (the
+    velocities walked back through the inverse joint transforms and the approximate reciprocals
+    must not drift): done flags equal and states within the reference's 1e-3."""
+    import pendulum_aba_metal
+
+    r = np.random.default_rng(100 + k)
+    st = np.concatenate([r.uniform(-0.1, 0.1, (k, 96)), r.uniform(-0.1, 0.1, (k, 96))]).astype(np.float32)
+    p = pendulum_aba_metal.Pendulum(k)
+    p.reseed(70)
+    s_gpu, s_np = torch.from_numpy(st).to(cuda), st
+    worst, flips = 0.0, 0
+    for t in range(50):
+        ac = r.integers(0, 3, 96)
+        s_gpu, _, d_gpu = p.step(s_gpu, torch.from_numpy(ac).to(cuda))
+        s_np, _, d_np, _ = kernels.pendulum_step(s_np, ac, 71 + t, k, form="aba")
+        flips += int((to_np(d_gpu) != d_np).sum())
+        worst = max(worst, float(np.abs(to_np(s_gpu) - s_np).max()))
+    record(f"pendulum_aba_k{k}_traj50", max_abs=worst, done_flips=flips)
+    assert flips == 0 and worst < 1e-3, (worst, flips)
 
 
 @pytest.mark.parametrize("cls_name", ["pendulum_metal", "pendulum_metal_coop", "pendulum_aba_metal"])
