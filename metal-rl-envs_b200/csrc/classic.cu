@@ -63,7 +63,7 @@ struct AcrobotEnv {
   RLENV_D static void to(const S& s, float (&r)[4]) {
     r[0] = s.th1; r[1] = s.th2; r[2] = s.dth1; r[3] = s.dth2;
   }
-  RLENV_D static Aux aux(const S& s) { return acrobot_trig(s); }
+  RLENV_D static Aux aux(const S& s) { return acrobot_stage_trig(s); }
   RLENV_D static bool step(S& s, Aux& t, int a, uint32_t h, float& reward) {
     const S nx = acrobot_physics(s, t, float(a - 1));
     Aux tn;
@@ -73,7 +73,7 @@ struct AcrobotEnv {
             uniform_pm(pcg_hash(h + classic_row_offset(1)), ac::RESET_BOUND),
             uniform_pm(pcg_hash(h + classic_row_offset(2)), ac::RESET_BOUND),
             uniform_pm(pcg_hash(h + classic_row_offset(3)), ac::RESET_BOUND)};
-      t = acrobot_trig(s);
+      t = acrobot_stage_trig(s);
     } else {
       s = nx;
       t = tn;

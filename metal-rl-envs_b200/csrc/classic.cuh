@@ -161,20 +161,18 @@ RLENV_D float acrobot_height(const AcrobotTrig& t) { return -t.c1 - (t.c1 * t.c2
 RLENV_D bool acrobot_terminated(const AcrobotTrig& t) { return acrobot_height(t) > 1.0f; }
 
 // A stepped state's trig and termination for the step kernels. The trig comes from the special
-// function unit; the height it gives is within 2e-6 of the height from sincos_fast's values
-// (three terms, each within 6e-7), so more than 1e-5 from the threshold the decision is the
-// same, and closer than that the trig is taken again from sincos_fast: termination is decided
-// exactly as acrobot_terminated(acrobot_trig(s)) decides it. This trig also starts the next
-// step's RK4 (its first stage, weighted dt / 6), as the stage trig does for the other three.
+// function unit (acrobot_stage_trig); the height it gives is within 2e-6 of the height from
+// sincos_fast's values (three terms, each within 6e-7), so more than 1e-5 from the threshold
+// the decision is the same, and closer than that the decision is taken from sincos_fast's
+// values: termination is decided exactly as acrobot_terminated(acrobot_trig(s)) decides it.
+// The trig returned is always the special function unit's, a function of the state alone, so
+// the first RK4 stage of the next step (weighted dt / 6, as the stage trig of the other three)
+// starts from the same bits whether the state stayed in registers or went through memory.
 // Against sincos_fast for the stepped state it cuts about 40 instructions per environment-step.
 RLENV_D bool acrobot_trig_terminated(const Acrobot& s, AcrobotTrig& t) {
-  sincos_sfu(s.th1, &t.s1, &t.c1);
-  sincos_sfu(s.th2, &t.s2, &t.c2);
+  t = acrobot_stage_trig(s);
   const float h = acrobot_height(t);
-  if (fabsf(h - 1.0f) < 1e-5f) {
-    t = acrobot_trig(s);
-    return acrobot_terminated(t);
-  }
+  if (fabsf(h - 1.0f) < 1e-5f) return acrobot_terminated(acrobot_trig(s));
   return h > 1.0f;
 }
 
