@@ -115,8 +115,9 @@ acrobot_rollout_kernel(const float* __restrict__ state, const float* __restrict_
   float survived = 0.0f;
   bool alive = true;
   // the observation is (cos t1, sin t1, cos t2, sin t2, w1, w2): the state's trig, which the
-  // first RK4 stage and the previous step's termination test use too
-  AcrobotTrig tr = acrobot_trig(s);
+  // first RK4 stage and the previous step's termination test use too; taken as the step kernel
+  // takes it (acrobot_trig_terminated), so a member steps exactly as rlenv_acrobot_step steps it
+  AcrobotTrig tr = acrobot_stage_trig(s);
   for (int step = 0; step < horizon; ++step) {
     if (!__any_sync(kFull, alive)) break;
     float l0 = 0.0f, l1 = 0.0f, l2 = 0.0f;
@@ -133,8 +134,7 @@ acrobot_rollout_kernel(const float* __restrict__ state, const float* __restrict_
     l2 = group_sum<G>(l2) + b2_2;
     if (alive) {
       s = acrobot_physics(s, tr, float(argmax3(l0, l1, l2) - 1));
-      tr = acrobot_trig(s);
-      if (acrobot_terminated(tr)) alive = false;
+      if (acrobot_trig_terminated(s, tr)) alive = false;
       else survived += 1.0f;
     }
   }
