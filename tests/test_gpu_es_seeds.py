@@ -7,8 +7,9 @@ tests/golden/make_es_solve.py). The GPU run draws its noise from a counter-based
 individual seeds differ; the distributions must agree.
 - CartPole and Acrobot at es.py's defaults (lr 0.1) and at BASELINE's settings (P = 4,096,
   lr 0.03): generations to solve.
-- legged4 (P = 256, horizon 100, lr 0.03): the population's mean training fitness over the last
-  five of 30 generations, since the oracle cannot train it to its threshold in reasonable time."""
+- legged4 (P = 256, horizon 100, lr 0.03): the learning curve of the population's mean training
+  fitness over 30 generations (its mean, and the generations it takes to reach 60), since the
+  oracle cannot train legged4 to its threshold in reasonable time."""
 
 import numpy as np
 import pytest
@@ -63,12 +64,19 @@ def test_legged4_learning_curves_match_the_reference_distribution(cuda):
             curve.append(float(fit.mean().item()))
         curves.append(curve)
     curves = np.array(curves)
-    late, ref_late = curves[:, -5:].mean(axis=1), ref[:, -5:].mean(axis=1)
-    p = float(mannwhitneyu(late, ref_late).pvalue)
+
+    def to_60(c):
+        return np.array([int(np.argmax(r >= 60)) + 1 if (r >= 60).any() else gens + 1 for r in c])
+
+    # the area under the learning curve (the late generations sit near the horizon's cap of about
+    # 100 on both sides, so they would not tell distributions apart) and generations to reach 60
+    area, ref_area = curves.mean(axis=1), ref.mean(axis=1)
+    p = float(mannwhitneyu(area, ref_area).pvalue)
+    p60 = float(mannwhitneyu(to_60(curves), to_60(ref)).pvalue)
     record("es_legged4_curves_10_seeds", population=pop, horizon=horizon, generations=gens, lr=lr,
-           gpu_first=curves[:, 0].round(2).tolist(), reference_first=ref[:, 0].round(2).tolist(),
-           gpu_last5=late.round(2).tolist(), reference_last5=ref_late.round(2).tolist(), mann_whitney_p=p)
-    # both sides learn: the last generations beat the first on most seeds
-    assert (late > curves[:, :3].mean(axis=1)).sum() >= 7 and (ref_late > ref[:, :3].mean(axis=1)).sum() >= 7
-    assert p > 0.01, (late, ref_late, p)
-    assert 0.75 <= np.median(late) / np.median(ref_late) <= 1.33, (late, ref_late)
+           gpu_area=area.round(2).tolist(), reference_area=ref_area.round(2).tolist(),
+           gpu_generations_to_60=to_60(curves).tolist(), reference_generations_to_60=to_60(ref).tolist(),
+           mann_whitney_p_area=p, mann_whitney_p_to_60=p60)
+    assert (to_60(curves) <= gens).sum() >= 9 and (to_60(ref) <= gens).sum() >= 9, "both sides learn"
+    assert p > 0.01 and p60 > 0.01, (area, ref_area, p, p60)
+    assert 0.8 <= np.median(area) / np.median(ref_area) <= 1.25, (area, ref_area)
