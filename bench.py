@@ -520,6 +520,33 @@ def north_star_records(torch, dist, world, rank, local, dev, sgemm):
     return out
 
 
+def _cpulist(text):
+    cpus = set()
+    for part in text.strip().split(","):
+        if "-" in part:
+            a, b = part.split("-")
+            cpus.update(range(int(a), int(b) + 1))
+        elif part:
+            cpus.add(int(part))
+    return cpus
+
+
+def pin_to_gpu_numa(torch, dev):
+    """Run this process on the CPUs next to the GPU (its PCI device's local_cpulist), so that the
+    pinned host buffers of the e2e run are allocated on the GPU's NUMA node: host-to-device copies
+    from a remote node ran at half the bandwidth. Returns what was done, for the JSON line."""
+    try:
+        p = torch.cuda.get_device_properties(dev)
+        path = Path(f"/sys/bus/pci/devices/{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0/local_cpulist")
+        cpus = _cpulist(path.read_text()) & set(os.sched_getaffinity(0))
+        if not cpus:
+            return "no local CPUs found; affinity unchanged"
+        os.sched_setaffinity(0, cpus)
+        return f"pinned to the {len(cpus)} CPUs local to the GPU before allocating pinned buffers"
+    except Exception as e:  # no sysfs entry, or affinity not settable
+        return f"affinity unchanged ({type(e).__name__})"
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -584,6 +611,7 @@ def run_ours(args):
     # and done count go back to pinned host memory. Two steps are in flight: the copy stream moves
     # step k+1's inputs while the compute stream runs step k (two device input buffers), which is
     # how a caller streaming batches from the host would drive acrobot_metal.step_many.
+    numa = pin_to_gpu_numa(torch, dev)
     pin_state = state0.cpu().pin_memory()
     pin_actions = actions.cpu().pin_memory()
     outs = [(torch.empty((4, n), pin_memory=True), torch.empty(n, pin_memory=True), torch.empty(n, pin_memory=True))
@@ -675,7 +703,7 @@ def run_ours(args):
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": "env steps/s", "h2d_bytes_per_step": 4 * 4 * n + T * n,
                 "d2h_bytes_per_step": 4 * 4 * n + 8 * n, "api": "acrobot_metal.step_many", "steps": e2e_steps,
-                "pipelined": "copy stream and compute stream, two steps in flight"},
+                "pipelined": "copy stream and compute stream, two steps in flight", "host": numa},
         "gpu_launches": args.steps,
         "clocks": clock_summary,
         "north_star": subs,

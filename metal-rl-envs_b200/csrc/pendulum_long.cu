@@ -13,8 +13,9 @@
 // - each joint's sine and cosine come from the special function unit in every pass
 //   (sincos_sfu) instead of being stored.
 // The last pass also applies the RK4 stage update to each link as soon as its acceleration is
-// known, so no acceleration array is kept. Arrays are laid out (array, link, thread), so the
-// 32 threads of a block touch 32 consecutive words: no bank conflicts.
+// known, so no acceleration array is kept. The arrays are laid out (link, array, thread): the
+// 32 threads of a block touch 32 consecutive words (no bank conflicts), and one pointer per
+// link reaches all nine.
 #include "pendulum_kernels.cuh"
 
 namespace rlenv {
@@ -35,10 +36,12 @@ RLENV_D float rcp_approx(float a) {
   return r;
 }
 
+// Link-major: the nine values of link i sit together, (link, array, thread), so a pass over the
+// links advances one pointer and reaches every array at a fixed offset from it.
 struct LongLinks {
-  float* base;  // array 0, link 0 of this thread
+  float* base;  // link 0, array 0 of this thread
   int k;
-  RLENV_D float& at(int a, int i) const { return base[(a * k + i) * kLongBlock]; }
+  RLENV_D float& at(int a, int i) const { return base[(i * kLongArrays + a) * kLongBlock]; }
 };
 
 // Accelerations of the stage whose angles and velocities are arrays (ia, io), applied at once as
