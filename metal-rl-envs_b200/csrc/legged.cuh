@@ -179,9 +179,6 @@ RLENV_D void contact_impulse(float Att, float Atn, float Ann, const ContactConst
   lt = active ? l_t : 0.0f;
 }
 
-// Whether the rollout's sweeps (SKIP) also stop at an exact fixed point (gauss_seidel's kStop).
-constexpr bool kStopSweeps = false;
-
 // One contact's Gauss-Seidel solve as affine functions of its coupling
 // s = sum_{l != k} G[k][l] P_l (legged_substep): gap = g0 + lca s, and lt_stick,
 // mu ln_stick, slip_p, P_stick, P_plus and P_minus each a + b s.
@@ -237,19 +234,14 @@ RLENV_D float contact_solve(const ContactAffine& a, float s) {
 // visited contact's coupling in the last sweep. A coupling adds the other contacts' terms
 // least recently updated first, so that only its last multiply-add waits for the contact
 // solved just before (legged_np.py:91-94).
-//
-// With kStop (all 32 lanes of the warp call together), the sweeps end as soon as a sweep leaves
-// every contact's P unchanged bit for bit in every lane of the warp: from such a fixed point each
-// later sweep would compute the same couplings and the same P again, so stopping there gives the
-// same bits as running all `sweeps`.
-template <int C, bool kAll, bool kStop = false>
+
+template <int C, bool kAll>
 RLENV_D void gauss_seidel(const ContactAffine (&af)[C], const float (&gkl)[C * (C - 1) / 2 + 1],
                           unsigned act, int sweeps, float (&sk)[C]) {
   float pl[C];
 #pragma unroll
   for (int k = 0; k < C; ++k) pl[k] = 0.0f;
   for (int it = 0; it < sweeps; ++it) {
-    bool same = true;
 #pragma unroll
     for (int k = 0; k < C; ++k) {
       if (!kAll && !(act & (1u << k))) continue;
@@ -260,13 +252,8 @@ RLENV_D void gauss_seidel(const ContactAffine (&af)[C], const float (&gkl)[C * (
         if (!kAll && !(act & (1u << l))) continue;
         s = fmaf(gkl[k > l ? tri(k - 1, l) : tri(l - 1, k)], pl[l], s);
       }
-      const float p = contact_solve(af[k], s);
-      if constexpr (kStop) same = same && __float_as_uint(p) == __float_as_uint(pl[k]);
-      pl[k] = p;
+      pl[k] = contact_solve(af[k], s);
       sk[k] = s;
-    }
-    if constexpr (kStop) {
-      if (it > 0 && __all_sync(lgx::kFull, same)) break;
     }
   }
 }
@@ -465,8 +452,8 @@ RLENV_D void legged_substep(float (&qt)[3], float (&vt)[3], float (&ql)[C / G], 
       for (int k = 0; k < C; ++k)
         if (__any_sync(kFull, alive && af[k].g0 > -INFINITY)) act |= 1u << k;
     }
-    if (act == kAllMask) gauss_seidel<C, true, SKIP && kStopSweeps>(af, gkl, act, iters, sk);
-    else if (act != 0u) gauss_seidel<C, false, SKIP && kStopSweeps>(af, gkl, act, __popc(act) == 1 ? 1 : iters, sk);
+    if (act == kAllMask) gauss_seidel<C, true>(af, gkl, act, iters, sk);
+    else if (act != 0u) gauss_seidel<C, false>(af, gkl, act, __popc(act) == 1 ? 1 : iters, sk);
 #pragma unroll
     for (int c = 0; c < CL; ++c) {
       // the coupling of own contact gl CL + c in the last sweep
