@@ -33,6 +33,7 @@ reference bit for bit; parity is the distribution of generations to solve.
 
 import argparse
 import inspect
+import os
 import time
 from dataclasses import dataclass
 from typing import Any, Callable
@@ -534,10 +535,33 @@ class Result:
     score: float
 
 
-def train(cfg, backend_name, seed, log=lambda *_: None):
+def _seed_counters(task):
+    """Every counter that seeds a later draw of a training run: the library's reset counter (the
+    evaluation's fresh states) and the task's step-kernel call counter (the step loop's resets)."""
+    m = task.metal
+    holder = getattr(m, "body", None) or getattr(m, "_counter", None) or m
+    return {"reset_calls": _rl._reset_calls, "step_calls": getattr(holder, "calls", None)}
+
+
+def _restore_seed_counters(task, counters):
+    _rl._reset_calls = int(counters["reset_calls"])
+    m = task.metal
+    holder = getattr(m, "body", None) or getattr(m, "_counter", None) or m
+    if counters.get("step_calls") is not None and hasattr(holder, "calls"):
+        holder.calls = int(counters["step_calls"])
+
+
+def train(cfg, backend_name, seed, log=lambda *_: None, *, checkpoint=None, checkpoint_every=10):
     """Run generations until the mean policy's score reaches the threshold, the generation cap
     or the time budget (es.py:334-354). log(gen, env_steps, train_seconds, mean fitness,
-    score) is called after every generation."""
+    score) is called after every generation.
+
+    checkpoint: a file path. Every checkpoint_every generations, and when training ends, theta,
+    the generation, the bookkeeping and every seed counter are saved there (written to a
+    temporary file, then renamed over it; rank 0 writes). If the file exists when train starts,
+    the run resumes from it. The noise and the initial states of a generation are functions of
+    (seed, generation, member), so a resumed run continues exactly as the uninterrupted run
+    would have. The reference keeps theta only in memory (es.py:325-354)."""
     if cfg.pop % 2:
         raise ValueError(f"the population must be even (antithetic pairs); got {cfg.pop}")
     if backend_name not in BACKENDS:
@@ -551,6 +575,24 @@ def train(cfg, backend_name, seed, log=lambda *_: None):
     theta = backend.normal((n_params(width, task),)) * 0.1
     backend.sync(theta)
     clock, taken, score, gen = 0.0, 0, 0.0, 0
+    run = {"task": cfg.task, "pop": cfg.pop, "width": width, "seed": int(seed), "backend": backend_name}
+    if checkpoint is not None and os.path.exists(checkpoint):
+        saved = torch.load(checkpoint, map_location="cpu", weights_only=False)
+        if saved["run"] != run:
+            raise ValueError(f"checkpoint {checkpoint} belongs to another run: {saved['run']} != {run}")
+        theta = saved["theta"].to(theta.device)
+        gen, taken, clock, score = saved["gen"], saved["taken"], saved["clock"], saved["score"]
+        backend._normal_calls = saved["normal_calls"]
+        _restore_seed_counters(task, saved["counters"])
+
+    def save():
+        if checkpoint is None or backend.rank != 0:
+            return
+        tmp = f"{checkpoint}.tmp"
+        torch.save({"run": run, "theta": theta.detach().cpu(), "gen": gen, "taken": taken, "clock": clock,
+                    "score": score, "normal_calls": backend._normal_calls, "counters": _seed_counters(task)}, tmp)
+        os.replace(tmp, checkpoint)
+
     while gen < cfg.max_generations:
         gen += 1
         t0 = time.perf_counter()
@@ -562,9 +604,13 @@ def train(cfg, backend_name, seed, log=lambda *_: None):
         score = evaluate_theta(task, theta, width)
         log(gen, taken, clock, float(fit.mean().item()), score)
         if score >= target:
+            save()
             return Result(True, gen, taken, clock, score)
+        if checkpoint_every > 0 and gen % checkpoint_every == 0:
+            save()
         if clock >= cfg.time_budget:
             break
+    save()
     return Result(False, gen, taken, clock, score)
 
 
@@ -581,6 +627,9 @@ _FLAGS = {
     "--assist": (float, 0.0, "curriculum: torso-assist stiffness at generation 1, annealed to zero"),
     "--start-velocity": (float, 0.0, "curriculum: forward push at the start of every episode, annealed to zero"),
     "--anneal": (int, 300, "generation by which both curricula have reached zero"),
+    # this build's own: checkpoint and resume (train's checkpoint arguments)
+    "--checkpoint": (str, None, "file to save the run to every --checkpoint-every generations, and to resume from"),
+    "--checkpoint-every": (int, 10, "generations between checkpoints"),
 }
 
 
@@ -591,13 +640,15 @@ def main(argv=None):
         parser.add_argument(flag, type=kind, default=default, help=text, choices=choices)
     args = parser.parse_args(argv)
     renamed = {"assist": "assist_k0", "anneal": "anneal_gens"}  # flags whose Config field is named otherwise
-    cfg = Config(**{renamed.get(k, k): v for k, v in vars(args).items() if k not in ("backend", "seed")})
+    own = ("backend", "seed", "checkpoint", "checkpoint_every")
+    cfg = Config(**{renamed.get(k, k): v for k, v in vars(args).items() if k not in own})
 
     def report(gen, env_steps, seconds, fitness, score):
         print(f"generation {gen:4d} | {env_steps:>14,} env steps | {seconds:8.2f} s | population fitness "
               f"{fitness:8.1f} | score {score:8.1f}", flush=True)
 
-    print(train(cfg, args.backend, args.seed, log=report))
+    print(train(cfg, args.backend, args.seed, log=report, checkpoint=args.checkpoint,
+                checkpoint_every=args.checkpoint_every))
     return 0
 
 

@@ -283,3 +283,33 @@ def test_generation_runs_a_subclass_with_the_reference_reset(cuda):
     # same initial states, same perturbations: the fused rollout and the loop take the same steps
     # for almost every member (their policies round the MLP differently)
     assert (outs[0][2] == outs[1][2]).float().mean().item() > 0.95
+
+
+def test_train_resumes_from_a_checkpoint_exactly(cuda, tmp_path):
+    """A run stopped after 3 generations and resumed from its checkpoint ends with the same theta,
+    the same per-generation fitness and scores, and the same Result counts as the run that was
+    never stopped (noise and initial states are functions of (seed, generation, member), and the
+    checkpoint carries every seed counter)."""
+    import es
+    import rlenv_lib
+
+    def run(max_gen, path, logs):
+        cfg = es.Config(task="cartpole", pop=256, max_generations=max_gen, time_budget=1e9, solved_at=1e9)
+        return es.train(cfg, "metal", 3, log=lambda *e: logs.append((e[0], e[1], e[3], e[4])),
+                        checkpoint=str(path), checkpoint_every=2)
+
+    rlenv_lib._reset_calls = 0
+    whole_log = []
+    whole = run(6, tmp_path / "whole.pt", whole_log)
+    rlenv_lib._reset_calls = 0
+    part_log = []
+    run(3, tmp_path / "part.pt", part_log)
+    rlenv_lib._reset_calls = 12345  # whatever the process did meanwhile: the checkpoint restores it
+    resumed = run(6, tmp_path / "part.pt", part_log)
+    assert (resumed.generations, resumed.env_steps, resumed.solved) == (whole.generations, whole.env_steps, whole.solved)
+    assert part_log == whole_log
+    a = torch.load(tmp_path / "whole.pt", weights_only=False)
+    b = torch.load(tmp_path / "part.pt", weights_only=False)
+    assert a["gen"] == b["gen"] == 6 and torch.equal(a["theta"], b["theta"])
+    with pytest.raises(ValueError):  # another run's checkpoint is refused
+        es.train(es.Config(task="acrobot", pop=256, max_generations=1), "metal", 3, checkpoint=str(tmp_path / "part.pt"))
