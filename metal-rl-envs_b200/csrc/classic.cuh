@@ -92,17 +92,21 @@ RLENV_D AcrobotTrig acrobot_trig(const Acrobot& s) {
   return t;
 }
 
-// The trig of an RK4 stage state (the second to fourth derivative evaluations) from the
-// special function unit (sincos_sfu, within 2^-21.4 absolute): the stage derivatives enter
-// the step weighted by dt / 3 and dt / 6, so on a B200 the stepped state stays within
-// 1e-6 of the reference's (the gate is 1e-5) for 42% more steps per second. The stepped
-// state's own trig, which decides termination and starts the next step, stays on
-// sincos_fast. The reference's Metal kernel evaluates every sine and cosine with Metal's
-// default fast-math sin and cos (acrobot_metal.py:42-47, 75).
+// The trig of an Acrobot state from the special function unit, with no 2 pi reduction
+// (sincos_sfu_near), for every state a step evaluates: a wrapped stepped state (|angle| <=
+// 3.1415968: within 4.1e-7 of sin and cos, measured on a B200), a fresh one, a state read from
+// memory (a launch's first step), and the second to fourth RK4 stage states, whose angles are a
+// wrapped angle plus dt / 2 or dt times a stage rate, within 8 of zero but for extreme rates
+// (within 1.21e-6). The stage derivatives enter the step weighted by dt / 3 and dt / 6, and the
+// stepped state stays within the 1e-5 single-step gate of the reference's. It is one function
+// of the state alone, so a chain of steps gives the same bits whether the state stays in
+// registers or goes through memory. Against a 2 pi reduction first (sincos_sfu) it saves four
+// instructions per angle, 32 per environment-step. The reference's Metal kernel evaluates
+// every sine and cosine with Metal's default fast-math sin and cos (acrobot_metal.py:42-47, 75).
 RLENV_D AcrobotTrig acrobot_stage_trig(const Acrobot& s) {
   AcrobotTrig t;
-  sincos_sfu(s.th1, &t.s1, &t.c1);
-  sincos_sfu(s.th2, &t.s2, &t.c2);
+  sincos_sfu_near(s.th1, &t.s1, &t.c1);
+  sincos_sfu_near(s.th2, &t.s2, &t.c2);
   return t;
 }
 
@@ -160,15 +164,12 @@ RLENV_D Acrobot acrobot_physics(const Acrobot& s, const AcrobotTrig& t0, float t
 RLENV_D float acrobot_height(const AcrobotTrig& t) { return -t.c1 - (t.c1 * t.c2 - t.s1 * t.s2); }
 RLENV_D bool acrobot_terminated(const AcrobotTrig& t) { return acrobot_height(t) > 1.0f; }
 
-// A stepped state's trig and termination for the step kernels. The trig comes from the special
-// function unit (acrobot_stage_trig); the height it gives is within 2e-6 of the height from
-// sincos_fast's values (three terms, each within 6e-7), so more than 1e-5 from the threshold
-// the decision is the same, and closer than that the decision is taken from sincos_fast's
-// values: termination is decided exactly as acrobot_terminated(acrobot_trig(s)) decides it.
-// The trig returned is always the special function unit's, a function of the state alone, so
-// the first RK4 stage of the next step (weighted dt / 6, as the stage trig of the other three)
-// starts from the same bits whether the state stayed in registers or went through memory.
-// Against sincos_fast for the stepped state it cuts about 40 instructions per environment-step.
+// A stepped state's trig and termination for the step kernels. The trig is acrobot_stage_trig's;
+// the height it gives is within 4e-6 of the height from sincos_fast's values (each sine and
+// cosine within 6e-7 of the other's, two products and a sum), so more than 1e-5 from the
+// threshold the decision is the same, and closer than that the decision is taken from
+// sincos_fast's values: termination is decided exactly as acrobot_terminated(acrobot_trig(s))
+// decides it. The trig returned starts the next step (its first RK4 stage, weighted dt / 6).
 RLENV_D bool acrobot_trig_terminated(const Acrobot& s, AcrobotTrig& t) {
   t = acrobot_stage_trig(s);
   const float h = acrobot_height(t);

@@ -231,6 +231,16 @@ RLENV_D void sincos_sfu(float x, float* s, float* c) {
   *c = __cosf(r);
 }
 
+// Sine and cosine from the special function unit on the argument as given, with no
+// reduction. Beyond pi the unit reduces the argument itself after scaling it to revolutions,
+// and its error grows with |x|: measured on a B200 over every float32 with |x| <= pi, 4, 8, 10
+// and 16, at most 4.1e-7, 6.5e-7, 1.21e-6, 1.27e-6 and 2.27e-6 (sincos_sfu: 4.9e-7 over
+// |x| <= 16).
+RLENV_D void sincos_sfu_near(float x, float* s, float* c) {
+  *s = __sinf(x);
+  *c = __cosf(x);
+}
+
 RLENV_D float cos_fast(float x) {
   float s, c;
   sincos_fast(x, &s, &c);

@@ -31,11 +31,12 @@ def probe(tmp_path_factory):
     lib = ctypes.CDLL(str(so))
     lib.trig_probe.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int64]
     lib.sfu_probe.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int64]
+    lib.near_probe.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int64]
 
-    def run(x, sfu=False):
+    def run(x, sfu=False, near=False):
         xd = torch.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()
-        outs = [torch.empty_like(xd) for _ in range(2 if sfu else 4)]
-        entry = lib.sfu_probe if sfu else lib.trig_probe
+        outs = [torch.empty_like(xd) for _ in range(2 if (sfu or near) else 4)]
+        entry = lib.near_probe if near else lib.sfu_probe if sfu else lib.trig_probe
         assert entry(xd.data_ptr(), *(o.data_ptr() for o in outs), xd.numel()) == 0
         return [o.cpu().numpy() for o in outs]
 
@@ -101,11 +102,41 @@ SFU_ABS_BOUND = 8e-7
 
 
 def test_sincos_sfu_absolute_error(probe):
-    """sincos_sfu (the Acrobot's RK4 stage trig): within the special function unit's bound
-    over the range the stages use, and far beyond it."""
+    """sincos_sfu (the legged bodies' and the ES rollouts' leg trig): within the special function
+    unit's bound over the range the bodies use, and far beyond it."""
     x = _inputs(1024.0, seed=2)
     s, c = probe(x, sfu=True)
     xs = x.astype(np.float64)
     es, ec = np.abs(s - np.sin(xs)).max(), np.abs(c - np.cos(xs)).max()
     print(f"sincos_sfu |x| <= 1024: sin {es:.3g} cos {ec:.3g} absolute (bound {SFU_ABS_BOUND:.3g})")
     assert es <= SFU_ABS_BOUND and ec <= SFU_ABS_BOUND
+
+
+# sincos_sfu_near (the Acrobot's and the long-chain pendulum's trig) has no reduction in front:
+# the unit's own error grows with |x|. Measured over every float32 in each range on a B200:
+# 4.04e-7, 6.5e-7, 1.21e-6 and 2.27e-6; the bounds keep a margin.
+NEAR_ABS_BOUNDS = [(np.pi, 5e-7), (4.0, 8e-7), (8.0, 1.4e-6), (16.0, 2.6e-6)]
+
+
+@pytest.mark.parametrize("limit,bound", NEAR_ABS_BOUNDS)
+def test_sincos_sfu_near_absolute_error(probe, limit, bound):
+    """The unreduced unit within its measured bound on each range the kernels use it for: a
+    wrapped angle (pi), the Acrobot's stage angles and the pendulum's joint angles (8)."""
+    x = _inputs(limit, seed=3)
+    s, c = probe(x, near=True)
+    xs = x.astype(np.float64)
+    es, ec = np.abs(s - np.sin(xs)).max(), np.abs(c - np.cos(xs)).max()
+    print(f"sincos_sfu_near |x| <= {limit:.4g}: sin {es:.3g} cos {ec:.3g} absolute (bound {bound:.3g})")
+    assert es <= bound and ec <= bound
+
+
+def test_sincos_sfu_near_equals_sincos_sfu_within_pi(probe):
+    """For |x| <= float(pi) the reduction's quotient is zero, so both forms give the same bits
+    (zero aside: the reduction turns -0 into +0)."""
+    r = np.random.default_rng(4)
+    x = np.concatenate([r.uniform(-np.pi, np.pi, 2_000_000), np.linspace(-np.pi, np.pi, 100_001)]).astype(np.float32)
+    x = x[(np.abs(x) <= np.float32(np.pi)) & (x != 0)]
+    s1, c1 = probe(x, sfu=True)
+    s2, c2 = probe(x, near=True)
+    np.testing.assert_array_equal(s1.view(np.uint32), s2.view(np.uint32))
+    np.testing.assert_array_equal(c1.view(np.uint32), c2.view(np.uint32))

@@ -29,6 +29,17 @@ extern "C" int sfu_probe(const float* x, float* s, float* c, int64_t n) {
   return int(cudaDeviceSynchronize());
 }
 
+__global__ void near_probe_kernel(const float* x, float* s, float* c, int64_t n) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) rlenv::sincos_sfu_near(x[i], s + i, c + i);
+}
+
+extern "C" int near_probe(const float* x, float* s, float* c, int64_t n) {
+  if (n <= 0) return 0;
+  near_probe_kernel<<<int((n + 255) / 256), 256>>>(x, s, c, n);
+  return int(cudaDeviceSynchronize());
+}
+
 extern "C" int trig_probe(const float* x, float* s, float* c, float* s_lib, float* c_lib,
                           int64_t n) {
   if (n <= 0) return 0;
