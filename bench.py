@@ -857,6 +857,8 @@ def run_workload(args):
                              r.data_ptr(), d.data_ptr(), sp))
             fl = (rlenv_flops.aba_flops(k) if args.workload == "pendulum_aba" else rlenv_flops.mass_matrix_flops(k))["flops"]
             extra = {"links": k}
+            if args.workload == "pendulum_aba":
+                extra["flops_per_env_step_reference_algorithm"] = rlenv_flops.aba_reference_flops(k)["flops"]
         actions = torch.randint(0, n_act, (T, n), device=dev, generator=g).to(torch.uint8 if n_act < 256 else torch.int32)
         state_b = torch.empty_like(state_a)
         rew, dn = torch.empty((T, n), device=dev), torch.empty((T, n), device=dev, dtype=torch.bool)

@@ -33,8 +33,7 @@ RLENV_D void for_range(F&& f) {
     for (int i = 0; i < N; ++i) f(i);
   } else {
     // partly unrolled: the local-memory loads of eight iterations are independent of one another
-    // and issue together, where one at a time each waited for its own round trip (measured on a
-    // B200 at K = 64, N = 65,536, with aba_accel_loops below: 60 -> 105 M env-steps/s)
+    // and issue together, where one at a time each waited for its own round trip
 #pragma unroll 8
     for (int i = 0; i < N; ++i) f(i);
   }
@@ -44,8 +43,10 @@ RLENV_D void for_range(F&& f) {
 constexpr int kUnrollLinks = 16;
 
 // Every acceleration evaluation (the four RK4 stages) takes its sines and cosines from
-// the special function unit (sincos_sfu, within 5.9e-7 absolute); the derivatives enter
-// the step weighted by dt / 6 and dt / 3. Termination, which the done flags must get
+// the special function unit (the mass matrix through sincos_sfu, within 5.9e-7 absolute; the
+// articulated body without the 2 pi reduction, sincos_sfu_near, within 1.21e-6 over the
+// |x| < 8 that a joint angle of two stage angles spans); the derivatives enter the step
+// weighted by dt / 6 and dt / 3. Termination, which the done flags must get
 // exactly right, uses cos_fast (within 1.6 ulp). The reference's Metal kernels call
 // Metal's default fast-math sin and cos (pendulum_metal.py:27, 98-102;
 // pendulum_aba_metal.py:34, 61, 74).
@@ -134,184 +135,82 @@ RLENV_D void for_links(F&& f) {
   for_range<HI - LO, UNROLL>([&](int t) { f(UP ? LO + t : HI - 1 - t); });
 }
 
-// The same three passes as loops over per-link arrays in local memory, for
-// chains too long to unroll fully (K > kUnrollLinks), unrolled by 8 so that the
-// per-link loads of several links are in flight together. It is kept out of line: when
-// nvcc inlined these loops into the RK4 driver, whose stage arrays they index
-// by the loop variable, the optimised device code returned wrong accelerations
-// for K >= 24 although every single evaluation was right; the same source is
-// correct out of line, without NVVM optimisation (-Xcicc -O0), under -G, and
-// compiled for the host.
-template <int K>
-__device__ __noinline__ void aba_accel_loops(const float* th, const float* om, float torque,
-                                             float* acc) {
-  // Seven per-link arrays in local memory. The inward pass overwrites what the last pass no
-  // longer needs: vw becomes u / D, vx and vy the velocity-product terms -qd vx and qd vy,
-  // and U1r, U2r hold U1 / D and U2 / D (U0 / D is 1: D = U0).
-  float vw[K], vx[K], vy[K], sn[K], cs[K], U1r[K], U2r[K];
-  vw[0] = om[0];
-  vx[0] = 0.0f;
-  vy[0] = 0.0f;
-#pragma unroll 8
-  for (int i = 1; i < K; ++i) {
-    const float qd = om[i] - om[i - 1];
-    float s, c;
-    sincos_sfu(th[i] - th[i - 1], &s, &c);
-    sn[i] = s;
-    cs[i] = c;
-    const float pw = vw[i - 1], px = vx[i - 1], xy = vy[i - 1] + pw;
-    vw[i] = pw + qd;
-    vx[i] = c * px + s * xy;
-    vy[i] = -s * px + c * xy;
-  }
-  // Articulated inertia (symmetric 3x3, upper half) and bias force that the child link hands to
-  // its parent in the inward pass; zero below the last link.
-  float carry_I00 = 0.0f, carry_I01 = 0.0f, carry_I02 = 0.0f;
-  float carry_I11 = 0.0f, carry_I12 = 0.0f, carry_I22 = 0.0f;
-  float carry_p0 = 0.0f, carry_p1 = 0.0f, carry_p2 = 0.0f;
-#pragma unroll 8
-  for (int i = K - 1; i >= 1; --i) {
-    const float w = vw[i], x = vx[i], y = vy[i];
-    const float qd = om[i] - om[i - 1];
-    const float fy = w + y;
-    const float p0 = (x * fy - y * x) + carry_p0, p1 = (-w * fy) + carry_p1, p2 = (w * x) + carry_p2;
-    const float a00 = 1.0f + carry_I00, a01 = carry_I01, a02 = 1.0f + carry_I02;
-    const float a11 = 1.0f + carry_I11, a12 = carry_I12, a22 = 1.0f + carry_I22;
-    const float r = 1.0f / a00;
-    const float Ia00 = a00 - a00 * a00 * r, Ia01 = a01 - a00 * a01 * r, Ia02 = a02 - a00 * a02 * r;
-    const float Ia11 = a11 - a01 * a01 * r, Ia12 = a12 - a01 * a02 * r, Ia22 = a22 - a02 * a02 * r;
-    const float c1 = qd * y, c2 = -qd * x;
-    const float g = -p0 * r;
-    vw[i] = g;
-    vx[i] = c2;
-    vy[i] = c1;
-    U1r[i] = a01 * r;
-    U2r[i] = a02 * r;
-    const float pa0 = p0 + (Ia01 * c1 + Ia02 * c2) + a00 * g;
-    const float pa1 = p1 + (Ia11 * c1 + Ia12 * c2) + a01 * g;
-    const float pa2 = p2 + (Ia12 * c1 + Ia22 * c2) + a02 * g;
-    const float s = sn[i], c = cs[i];
-    const float B00 = Ia00 + Ia01 * s + Ia02 * c, B01 = Ia01 * c - Ia02 * s, B02 = Ia01 * s + Ia02 * c;
-    const float B10 = Ia01 + Ia11 * s + Ia12 * c, B11 = Ia11 * c - Ia12 * s, B12 = Ia11 * s + Ia12 * c;
-    const float B20 = Ia02 + Ia12 * s + Ia22 * c, B21 = Ia12 * c - Ia22 * s, B22 = Ia12 * s + Ia22 * c;
-    carry_I00 = B00 + s * B10 + c * B20;
-    carry_I01 = B01 + s * B11 + c * B21;
-    carry_I02 = B02 + s * B12 + c * B22;
-    carry_I11 = c * B11 - s * B21;
-    carry_I12 = c * B12 - s * B22;
-    carry_I22 = s * B12 + c * B22;
-    carry_p0 = pa0 + s * pa1 + c * pa2;
-    carry_p1 = c * pa1 - s * pa2;
-    carry_p2 = s * pa1 + c * pa2;
-  }
-  const float w0 = vw[0], x0 = vx[0], y0 = vy[0], fy0 = w0 + y0;
-  const float U0_0 = 1.0f + carry_I00, U1_0 = carry_I01, U2_0 = 1.0f + carry_I02;
-  const float uu0 = torque - ((x0 * fy0 - y0 * x0) + carry_p0);
-  float sn0, cs0;
-  sincos_sfu(th[0], &sn0, &cs0);
-  float ax = cs0 * -pd::G + om[0] * y0;
-  float ay = -sn0 * -pd::G - om[0] * x0;
-  const float qdd = (uu0 - (U0_0 * 0.0f + U1_0 * ax + U2_0 * ay)) / U0_0;
-  float aw = 0.0f + qdd, run = qdd;
-  acc[0] = run;
-#pragma unroll 8
-  for (int i = 1; i < K; ++i) {
-    const float xy = ay + aw;
-    const float ap1 = cs[i] * ax + sn[i] * xy + vy[i];
-    const float ap2 = -sn[i] * ax + cs[i] * xy + vx[i];
-    const float q2 = vw[i] - aw - U1r[i] * ap1 - U2r[i] * ap2;
-    aw = aw + q2;
-    ax = ap1;
-    ay = ap2;
-    run += q2;
-    acc[i] = run;
-  }
-}
-
 // The three passes fully unrolled, every per-link array in registers (K <= kUnrollLinks).
+//
+// Every link is a unit point mass at (1, 0) of its frame, and every child's joint sits at that
+// point. The articulated-body algebra then collapses, exactly (checked in float64 against the
+// full 3x3 form to 1e-14): a subtree's articulated inertia, seen from its joint, has the
+// pattern I00 = I02 = I22 of a mass at the joint's point, so U2 / D is 1; its projection
+// Ia = I - U U^T / D keeps one nonzero entry, m = Ia11, and so what a subtree hands to its
+// parent is rank one, m (s^2, s c, c^2) in (I00, I01, I11) and pa1 (s, c) in the bias (s, c the
+// joint's sine and cosine), with pa0 = pa2 = 0. An inward step is then about 20 flops where the
+// full 3x3 form takes about 80, and a link keeps u / D and U1 / D only.
 template <int K>
 RLENV_D void aba_accel_unrolled(const float* th, const float* om, float torque, float* acc) {
   // per link: velocity, the joint rotation's sine and cosine (evaluated once, used by all three
   // passes); the inward pass then overwrites the velocity with what the last pass needs
-  // (u / D and the velocity-product terms c2 = -qd vx, c1 = qd vy) and keeps U1 / D, U2 / D
-  // (U0 / D is 1: D = U0)
-  float vw[K], vx[K], vy[K], sn[K], cs[K], U1r[K], U2r[K];
+  // (u / D and the velocity-product terms c2 = -qd vx, c1 = qd vy) and keeps U1 / D
+  float vw[K], vx[K], vy[K], sn[K], cs[K], U1r[K];
   // outward: link velocities v_i = X_i v_{i-1} + S qd_i; the root has v_0 = (qd_0, 0, 0)
   vw[0] = om[0];
   vx[0] = 0.0f;
   vy[0] = 0.0f;
   for_links<1, K, true, true>([&](int i) {
     const float qd = om[i] - om[i - 1];
-    sincos_sfu(th[i] - th[i - 1], &sn[i], &cs[i]);
+    sincos_sfu_near(th[i] - th[i - 1], &sn[i], &cs[i]);
     const float pw = vw[i - 1], px = vx[i - 1], xy = vy[i - 1] + pw;  // joint at (1, 0)
     vw[i] = pw + qd;
     vx[i] = cs[i] * px + sn[i] * xy;
     vy[i] = -sn[i] * px + cs[i] * xy;
   });
-  // inward: articulated inertia (symmetric 3x3, upper half) and bias force of the subtree,
-  // carried to the parent as the child's contribution; zero below the last link
-  float carry_I00 = 0.0f, carry_I01 = 0.0f, carry_I02 = 0.0f;
-  float carry_I11 = 0.0f, carry_I12 = 0.0f, carry_I22 = 0.0f;
-  float carry_p0 = 0.0f, carry_p1 = 0.0f, carry_p2 = 0.0f;
+  // inward: the subtree's articulated inertia (I00, I01, I11) and bias (p0, p1) carried to the
+  // parent as the child's contribution; zero below the last link
+  float cI00 = 0.0f, cI01 = 0.0f, cI11 = 0.0f, cp0 = 0.0f, cp1 = 0.0f;
   for_links<1, K, false, true>([&](int i) {
     const float w = vw[i], x = vx[i], y = vy[i];
     const float qd = om[i] - om[i - 1];
-    // own bias p = v x* (I v), I of a unit mass at (1, 0) = [[1,0,1],[0,1,0],[1,0,1]]
-    const float fy = w + y;
-    const float p0 = (x * fy - y * x) + carry_p0;
-    const float p1 = (-w * fy) + carry_p1;
-    const float p2 = (w * x) + carry_p2;
-    const float a00 = 1.0f + carry_I00, a01 = carry_I01, a02 = 1.0f + carry_I02;
-    const float a11 = 1.0f + carry_I11, a12 = carry_I12, a22 = 1.0f + carry_I22;
+    // own bias v x* (I v) of a unit mass at (1, 0): (x w, -w (w + y), x w)
+    const float p0 = x * w + cp0;
+    const float p1 = -w * (w + y) + cp1;
+    const float a00 = 1.0f + cI00, a01 = cI01, a11 = 1.0f + cI11;
     const float r = 1.0f / a00;  // D = a00
-    const float Ia00 = a00 - a00 * a00 * r, Ia01 = a01 - a00 * a01 * r, Ia02 = a02 - a00 * a02 * r;
-    const float Ia11 = a11 - a01 * a01 * r, Ia12 = a12 - a01 * a02 * r, Ia22 = a22 - a02 * a02 * r;
+    const float g = -p0 * r;     // u / D, u = -p0
+    const float u1 = a01 * r;
+    const float m = a11 - a01 * u1;
     const float c1 = qd * y, c2 = -qd * x;  // c_i = v_i x S qd
-    const float g = -p0 * r;                 // u / D, u = -p0
+    const float pa1 = p1 + m * c1 + a01 * g;
     vw[i] = g;
     vx[i] = c2;
     vy[i] = c1;
-    U1r[i] = a01 * r;
-    U2r[i] = a02 * r;
-    const float pa0 = p0 + (Ia01 * c1 + Ia02 * c2) + a00 * g;
-    const float pa1 = p1 + (Ia11 * c1 + Ia12 * c2) + a01 * g;
-    const float pa2 = p2 + (Ia12 * c1 + Ia22 * c2) + a02 * g;
+    U1r[i] = u1;
     const float s = sn[i], c = cs[i];
-    // B = Ia X with X = [[1,0,0],[s,c,s],[c,-s,c]] (r = 1); parent gets X^T B and X^T pa
-    const float B00 = Ia00 + Ia01 * s + Ia02 * c, B01 = Ia01 * c - Ia02 * s, B02 = Ia01 * s + Ia02 * c;
-    const float B10 = Ia01 + Ia11 * s + Ia12 * c, B11 = Ia11 * c - Ia12 * s, B12 = Ia11 * s + Ia12 * c;
-    const float B20 = Ia02 + Ia12 * s + Ia22 * c, B21 = Ia12 * c - Ia22 * s, B22 = Ia12 * s + Ia22 * c;
-    carry_I00 = B00 + s * B10 + c * B20;
-    carry_I01 = B01 + s * B11 + c * B21;
-    carry_I02 = B02 + s * B12 + c * B22;
-    carry_I11 = c * B11 - s * B21;
-    carry_I12 = c * B12 - s * B22;
-    carry_I22 = s * B12 + c * B22;
-    carry_p0 = pa0 + s * pa1 + c * pa2;
-    carry_p1 = c * pa1 - s * pa2;
-    carry_p2 = s * pa1 + c * pa2;
+    const float ms = m * s;
+    cI00 = ms * s;
+    cI01 = ms * c;
+    cI11 = (m * c) * c;
+    cp0 = s * pa1;
+    cp1 = c * pa1;
   });
-  // root link: its inertia and bias with the whole chain's contribution
-  const float w0 = vw[0], x0 = vx[0], y0 = vy[0], fy0 = w0 + y0;
-  const float U0_0 = 1.0f + carry_I00, U1_0 = carry_I01, U2_0 = 1.0f + carry_I02;
-  const float uu0 = torque - ((x0 * fy0 - y0 * x0) + carry_p0);
+  // root link: its inertia and bias with the whole chain's contribution (U2 = U0; the root's own
+  // bias is zero, v_0 = (qd_0, 0, 0))
+  const float U0_0 = 1.0f + cI00, U1_0 = cI01;
+  const float uu0 = torque - cp0;
   // outward: accelerations, the base accelerating at -G; the absolute angular
   // accelerations are the running sum of the joint accelerations
   float sn0, cs0;
-  sincos_sfu(th[0], &sn0, &cs0);
-  const float qd0 = om[0];
-  // root: X_0 maps the base acceleration (0, -G, 0); r = 0
-  float ax = cs0 * -pd::G + qd0 * y0;
-  float ay = -sn0 * -pd::G - qd0 * x0;
-  const float qdd = (uu0 - (U0_0 * 0.0f + U1_0 * ax + U2_0 * ay)) / U0_0;
-  float aw = 0.0f + qdd;
+  sincos_sfu_near(th[0], &sn0, &cs0);
+  // root: X_0 maps the base acceleration (0, -G, 0)
+  float ax = cs0 * -pd::G;
+  float ay = -sn0 * -pd::G;
+  const float qdd = (uu0 - (U1_0 * ax + U0_0 * ay)) / U0_0;
+  float aw = qdd;
   float run = qdd;
   acc[0] = run;
   for_links<1, K, true, true>([&](int i) {
     const float xy = ay + aw;
     const float ap1 = cs[i] * ax + sn[i] * xy + vy[i];
     const float ap2 = -sn[i] * ax + cs[i] * xy + vx[i];
-    const float q2 = vw[i] - aw - U1r[i] * ap1 - U2r[i] * ap2;
+    const float q2 = vw[i] - aw - U1r[i] * ap1 - ap2;
     aw = aw + q2;
     ax = ap1;
     ay = ap2;
@@ -322,11 +221,8 @@ RLENV_D void aba_accel_unrolled(const float* th, const float* om, float torque, 
 
 template <int K>
 RLENV_D void aba_accel(const float* th, const float* om, float torque, float* acc) {
-  if constexpr (K > kUnrollLinks) {
-    aba_accel_loops<K>(th, om, torque, acc);
-  } else {
-    aba_accel_unrolled<K>(th, om, torque, acc);
-  }
+  static_assert(K <= kUnrollLinks, "longer chains run in pendulum_long.cu");
+  aba_accel_unrolled<K>(th, om, torque, acc);
 }
 
 // ---- RK4 step on (theta, omega) (pendulum_np.py:60-66) -----------------------

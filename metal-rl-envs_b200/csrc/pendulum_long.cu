@@ -2,11 +2,12 @@
 // environment, any K from 2 to kMaxLongLinks chosen at run time, every per-link array in
 // shared memory.
 //
-// A thread keeps nine arrays of K floats: the state (theta, omega), the RK4 stage state,
-// the RK4 sums, and the three values the articulated-body inward pass hands to the last
-// pass (u / D, U1 / D, U2 / D; U0 / D is 1). Kept in local memory, as the register form does
-// for short chains, 4 KB per environment at K = 64 missed L1 and L2 and the kernel waited on
-// memory. Two things keep the count at nine:
+// A thread keeps eight arrays of K floats: the state (theta, omega), the RK4 stage state,
+// the RK4 sums, and the two values the articulated-body inward pass hands to the last pass
+// (u / D, U1 / D; U0 / D and U2 / D are 1: the rank-one form of pendulum.cuh's
+// aba_accel_unrolled, which this kernel follows). Kept in local memory, 4 KB per
+// environment at K = 64 missed L1 and L2 and the kernel waited on memory. Two things keep
+// the count at eight:
 // - link velocities are not stored: the inward pass starts from the last link's velocity and
 //   walks them back link by link through the inverse joint transform (a rotation and a
 //   shift), and the last pass recomputes them forward;
@@ -18,16 +19,16 @@
 // pass starts from, needs no pass of its own except at a launch's first step and after a
 // reset. The last pass of a step's final stage also sums the termination height. The arrays
 // are laid out (link, array, thread): the 32 threads of a block touch 32 consecutive words
-// (no bank conflicts), and one pointer per link reaches all nine.
+// (no bank conflicts), and one pointer per link reaches all eight.
 #include "pendulum_kernels.cuh"
 
 namespace rlenv {
 namespace pend {
 
 constexpr int kLongBlock = 32;
-constexpr int kLongArrays = 9;
-constexpr int kMaxLongLinks = 192;  // 9 K floats x 32 threads within 227 KB of shared memory
-enum LongArray { kTh = 0, kOm, kTs, kOs, kDth, kDom, kGu, kU1, kU2 };
+constexpr int kLongArrays = 8;
+constexpr int kMaxLongLinks = 192;  // 8 K floats x 32 threads within 227 KB of shared memory
+enum LongArray { kTh = 0, kOm, kTs, kOs, kDth, kDom, kGu, kU1 };
 
 size_t long_smem_bytes(int k) { return size_t(kLongArrays) * k * kLongBlock * sizeof(float); }
 
@@ -39,7 +40,7 @@ RLENV_D float rcp_approx(float a) {
   return r;
 }
 
-// Link-major: the nine values of link i sit together, (link, array, thread), so a pass over the
+// Link-major: the eight values of link i sit together, (link, array, thread), so a pass over the
 // links advances one pointer and reaches every array at a fixed offset from it.
 struct LongLinks {
   float* base;  // link 0, array 0 of this thread
@@ -95,10 +96,10 @@ RLENV_D LinkVel last_link_velocity(const LongLinks& L, int ia, int io) {
 RLENV_D LinkVel aba_stage(const LongLinks& L, int ia, int io, float torque, int stage, LinkVel tip,
                           float& height) {
   const int k = L.k;
-  // ---- inward: articulated inertia and bias of each subtree, carried to the parent; the link
-  // velocities walked back from the last (x_{i-1} = c x_i - s y_i, y_{i-1} = s x_i + c y_i - w_{i-1})
-  float cI00 = 0.0f, cI01 = 0.0f, cI02 = 0.0f, cI11 = 0.0f, cI12 = 0.0f, cI22 = 0.0f;
-  float cp0 = 0.0f, cp1 = 0.0f, cp2 = 0.0f;
+  // ---- inward: the subtree's articulated inertia (I00, I01, I11) and bias (p0, p1), carried to
+  // the parent in the rank-one form; the link velocities walked back from the last
+  // (x_{i-1} = c x_i - s y_i, y_{i-1} = s x_i + c y_i - w_{i-1})
+  float cI00 = 0.0f, cI01 = 0.0f, cI11 = 0.0f, cp0 = 0.0f, cp1 = 0.0f;
   {
     float vw = tip.w, vx = tip.x, vy = tip.y;
     float th = L.at(ia, k - 1), om = L.at(io, k - 1);
@@ -109,34 +110,23 @@ RLENV_D LinkVel aba_stage(const LongLinks& L, int ia, int io, float torque, int 
       float s, c;
       joint_sincos(__fsub_rn(th, pth), &s, &c);
       const float w = vw, x = vx, y = vy;
-      // own bias p = v x* (I v), I of a unit mass at (1, 0) = [[1,0,1],[0,1,0],[1,0,1]]
-      const float fy = w + y;
-      const float p0 = (x * fy - y * x) + cp0, p1 = (-w * fy) + cp1, p2 = (w * x) + cp2;
-      const float a00 = 1.0f + cI00, a01 = cI01, a02 = 1.0f + cI02;
-      const float a11 = 1.0f + cI11, a12 = cI12, a22 = 1.0f + cI22;
+      // own bias v x* (I v) of a unit mass at (1, 0): (x w, -w (w + y), x w)
+      const float p0 = x * w + cp0;
+      const float p1 = -w * (w + y) + cp1;
+      const float a00 = 1.0f + cI00, a01 = cI01, a11 = 1.0f + cI11;
       const float r = rcp_approx(a00);
-      const float Ia00 = a00 - a00 * a00 * r, Ia01 = a01 - a00 * a01 * r, Ia02 = a02 - a00 * a02 * r;
-      const float Ia11 = a11 - a01 * a01 * r, Ia12 = a12 - a01 * a02 * r, Ia22 = a22 - a02 * a02 * r;
-      const float c1 = qd * y, c2 = -qd * x;
       const float g = -p0 * r;
+      const float u1 = a01 * r;
+      const float m = a11 - a01 * u1;
       L.at(kGu, i) = g;
-      L.at(kU1, i) = a01 * r;
-      L.at(kU2, i) = a02 * r;
-      const float pa0 = p0 + (Ia01 * c1 + Ia02 * c2) + a00 * g;
-      const float pa1 = p1 + (Ia11 * c1 + Ia12 * c2) + a01 * g;
-      const float pa2 = p2 + (Ia12 * c1 + Ia22 * c2) + a02 * g;
-      const float B00 = Ia00 + Ia01 * s + Ia02 * c, B01 = Ia01 * c - Ia02 * s, B02 = Ia01 * s + Ia02 * c;
-      const float B10 = Ia01 + Ia11 * s + Ia12 * c, B11 = Ia11 * c - Ia12 * s, B12 = Ia11 * s + Ia12 * c;
-      const float B20 = Ia02 + Ia12 * s + Ia22 * c, B21 = Ia12 * c - Ia22 * s, B22 = Ia12 * s + Ia22 * c;
-      cI00 = B00 + s * B10 + c * B20;
-      cI01 = B01 + s * B11 + c * B21;
-      cI02 = B02 + s * B12 + c * B22;
-      cI11 = c * B11 - s * B21;
-      cI12 = c * B12 - s * B22;
-      cI22 = s * B12 + c * B22;
-      cp0 = pa0 + s * pa1 + c * pa2;
-      cp1 = c * pa1 - s * pa2;
-      cp2 = s * pa1 + c * pa2;
+      L.at(kU1, i) = u1;
+      const float pa1 = p1 + m * (qd * y) + a01 * g;
+      const float ms = m * s;
+      cI00 = ms * s;
+      cI01 = ms * c;
+      cI11 = (m * c) * c;
+      cp0 = s * pa1;
+      cp1 = c * pa1;
       // the parent's velocity
       const float pw = w - qd;
       vx = c * x - s * y;
@@ -151,13 +141,13 @@ RLENV_D LinkVel aba_stage(const LongLinks& L, int ia, int io, float torque, int 
   const float th0 = L.at(ia, 0), om0 = L.at(io, 0);
   float ax, ay, aw, run;
   {
-    const float U0_0 = 1.0f + cI00, U1_0 = cI01, U2_0 = 1.0f + cI02;
+    const float U0_0 = 1.0f + cI00, U1_0 = cI01;  // U2 = U0
     const float uu0 = torque - cp0;  // the root's own bias is zero: v_0 = (qd_0, 0, 0)
     float sn0, cs0;
     joint_sincos(th0, &sn0, &cs0);
     ax = cs0 * -pd::G;
     ay = -sn0 * -pd::G;
-    const float qdd = (uu0 - (U1_0 * ax + U2_0 * ay)) * rcp_approx(U0_0);
+    const float qdd = (uu0 - (U1_0 * ax + U0_0 * ay)) * rcp_approx(U0_0);
     aw = qdd;
     run = qdd;
   }
@@ -211,7 +201,7 @@ RLENV_D LinkVel aba_stage(const LongLinks& L, int ia, int io, float torque, int 
       const float xy = ay + aw;
       const float ap1 = c * ax + s * xy + c1;
       const float ap2 = -s * ax + c * xy + c2;
-      const float q2 = L.at(kGu, i) - aw - L.at(kU1, i) * ap1 - L.at(kU2, i) * ap2;
+      const float q2 = L.at(kGu, i) - aw - L.at(kU1, i) * ap1 - ap2;
       aw = aw + q2;
       ax = ap1;
       ay = ap2;

@@ -42,8 +42,19 @@ def mass_matrix_flops(k):
 
 
 def aba_flops(k):
-    """Per step of the articulated-body form: about 140 flops per link per stage over the three
-    passes plus the RK4 combination, as the reference counts (bench_aba.py:53-55)."""
+    """Per step of the articulated-body form as this build computes it (the rank-one form of
+    csrc/pendulum.cuh, aba_accel_unrolled): per link and RK4 stage, the outward velocity 9, the
+    inward step 24 (own bias 5, the joint's D, u / D, U1 / D and the projected inertia 8, its
+    bias 4, the rank-one carry 7), the last pass's acceleration 16; plus the RK4 combination
+    (12 per link). Transcendentals: one sine and cosine per link and stage, and the termination
+    cosines. The long-chain kernel recomputes the link velocities and the joint trig instead of
+    storing them; that recomputation is not counted."""
+    return dict(flops=4 * 49 * k + 12 * k, transcendentals=4 * 2 * k + k)
+
+
+def aba_reference_flops(k):
+    """The same step as the reference counts it (bench_aba.py:53-55): about 140 flops per link
+    and stage over the three passes of the full 3x3 spatial algebra, plus the RK4 combination."""
     return dict(flops=4 * 140 * k + 12 * k, transcendentals=4 * 6 * k + k)
 
 
