@@ -132,6 +132,42 @@ def test_articulated_body_long_chain_trajectory(cuda, k):
     assert flips == 0 and worst < 1e-3, (worst, flips)
 
 
+@pytest.mark.parametrize("k", [32, 48, 64])
+def test_articulated_body_tensor_and_shared_memory_warps_agree(cuda, k):
+    """For 32 <= K <= 64 and a batch that fills the GPU, a block's first four warps keep their
+    environments in tensor memory and the others in shared memory (seven warps here). The same environments rolled by 128 positions, with
+    index_offset moved back by as much so that their resets draw the same numbers, change kind
+    of warp: states, rewards and done flags are the same bits."""
+    import rlenv_lib as rl
+
+    lib = rl.lib()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    n = 32 * sms * 7  # seven warps per SM: four in tensor memory, three in shared memory
+    T, off, roll = 6, 1000, 128
+    r = np.random.default_rng(k)
+    st = r.uniform(-0.1, 0.1, (2 * k, n)).astype(np.float32)
+    st[:k, ::5] = np.pi  # a fifth start upright: resets in the first step
+    act = r.integers(0, 3, (T, n)).astype(np.int32)
+
+    def run(state, actions, index_offset):
+        s, a = torch.from_numpy(state).to(cuda), torch.from_numpy(actions).to(cuda)
+        nxt = torch.empty_like(s)
+        rew = torch.empty((T, n), device=cuda)
+        done = torch.empty((T, n), dtype=torch.bool, device=cuda)
+        rl.check(lib.pendulum_aba_step_many(k, s.data_ptr(), a.data_ptr(), rl.I32, 7, T, n, index_offset,
+                                            nxt.data_ptr(), rew.data_ptr(), done.data_ptr(),
+                                            torch.cuda.current_stream().cuda_stream))
+        return to_np(nxt), to_np(rew), to_np(done)
+
+    first = run(st, act, off)
+    moved = run(np.roll(st, roll, axis=1), np.roll(act, roll, axis=1), off - roll)
+    assert first[2].any(), "the window should include resets"
+    for a, b in zip(first, moved):
+        a = np.ascontiguousarray(a[..., : n - roll])  # the environments that moved without wrapping
+        b = np.ascontiguousarray(b[..., roll:])
+        np.testing.assert_array_equal(a.view(np.uint8), b.view(np.uint8))
+
+
 @pytest.mark.parametrize("cls_name", ["pendulum_metal", "pendulum_metal_coop", "pendulum_aba_metal"])
 def test_pendulum_resets_and_chain(cuda, cls_name):
     mod = __import__(cls_name)
