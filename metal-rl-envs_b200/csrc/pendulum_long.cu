@@ -431,6 +431,7 @@ RLENV_D LinkVel tm_stage(uint32_t tb, int k, float torque, int stage, LinkVel ti
     Pair cur = tm_ld2(tm_link(tb, k - 1) + in);
     tm_wait(cur);
     Pair nxt = tm_ld2(tm_link(tb, k - 2) + in);
+#pragma unroll 2
     for (int i = k - 1; i >= 1; --i) {
       tm_wait(nxt);
       const Pair prev = nxt;
@@ -461,6 +462,7 @@ RLENV_D LinkVel tm_stage(uint32_t tb, int k, float torque, int stage, LinkVel ti
   float pth = th0, pom = om0, pnth = nth, pnom = nom;
   LinkVel v{om0, 0.0f, 0.0f};
   Record nx = tm_ld8(tm_link(tb, 1));
+#pragma unroll 4  // as the shared-memory passes: +4% for the mixed kernel at K = 32 .. 64
   for (int i = 1; i < k; ++i) {
     tm_wait(nx);
     const Record cur = nx;
