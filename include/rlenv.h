@@ -144,7 +144,12 @@ RLENV_API int rlenv_pendulum_coop_step_many(int k, const float* state, const voi
 
 /* Articulated-body (Featherstone) form, O(k) per stage, one thread per
  * environment. Replaces `pendulum{K}_aba_step` (pendulum_aba_metal.py:14-144).
- * Built for k in 1..16, 24, 32, 48, 64. */
+ * Any k from 1 to 192 (k > 192: RLENV_EUNSUPPORTED). For 32 <= k <= 64 and a
+ * batch that fills the GPU the launch runs one block per SM that allocates all
+ * 512 tensor-memory columns of its SM (tcgen05.alloc) and frees them before it
+ * ends; a tensor-memory kernel of the caller's on another stream can delay its
+ * blocks, never deadlock them (each allocation waits only for blocks that run to
+ * completion). Results do not depend on which kernel a batch size selects. */
 RLENV_API int rlenv_pendulum_aba_step(int k, const float* state, const void* action, int action_dtype,
                             uint32_t seed, int64_t n, int64_t index_offset,
                             float* next_state, float* reward, uint8_t* done, void* stream);

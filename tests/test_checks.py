@@ -102,3 +102,40 @@ def test_check_build_flags_bad_actions_and_non_finite_outputs(cuda):
                                      lo.data_ptr(), rew.data_ptr(), dn.data_ptr(), None, sp) == 0
         torch.cuda.synchronize()
         assert _status(lib) == (0, 1)
+
+
+@pytest.mark.gpu
+def test_check_build_flags_in_the_tensor_memory_kernel(cuda):
+    """K = 64 on a batch that fills the GPU runs the long-chain pendulum's mixed kernel (four
+    tensor-memory warps per block beside shared-memory ones): a clean batch leaves the word at
+    zero, a bad action in a tensor-memory warp (the first environment) and one in a
+    shared-memory warp (the 200th) set bit 1, and a non-finite state sets bit 2."""
+    import torch
+
+    lib = _load("librlenv_checks.so")
+    sp = torch.cuda.current_stream(cuda).cuda_stream
+    assert _status(lib)[0] == 0
+    k = 64
+    n = 32 * torch.cuda.get_device_properties(0).multi_processor_count * 7
+    r = np.random.default_rng(64)
+    ps = torch.from_numpy(r.uniform(-0.1, 0.1, (2 * k, n)).astype(np.float32)).to(cuda)
+    po = torch.empty_like(ps)
+    rew = torch.empty(n, device=cuda)
+    dn = torch.empty(n, dtype=torch.uint8, device=cuda)
+
+    def step(state, action):
+        a = torch.from_numpy(np.asarray(action, np.int32)).to(cuda)
+        assert lib.rlenv_pendulum_aba_step(k, state.data_ptr(), a.data_ptr(), 0, 3, n, 0, po.data_ptr(),
+                                           rew.data_ptr(), dn.data_ptr(), sp) == 0
+        torch.cuda.synchronize()
+        return _status(lib)
+
+    ok = r.integers(0, 3, n)
+    assert step(ps, ok) == (0, 0)
+    for where in (0, 200):
+        bad = ok.copy()
+        bad[where] = 5
+        assert step(ps, bad) == (0, 1), where
+    nan = ps.clone()
+    nan[3, 7] = float("nan")
+    assert step(nan, ok)[1] & 2
