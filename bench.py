@@ -51,6 +51,8 @@ T_STEPS = 1000
 METRIC = "env steps/s"
 WORKLOAD = "acrobot_batched_step"
 # workload -> (config it measures, default N, default T)
+NOMINAL_FP32_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12  # 74.4: FMA lanes x 2 flops x max SM clock
+
 WORKLOADS = {
     "acrobot_step": ("BASELINE configs[1]: Acrobot batched step", N_ENVS, T_STEPS),
     "cartpole_step": ("BASELINE configs[0]: CartPole batched step, T-step kernel", 131_072, T_STEPS),
@@ -940,6 +942,13 @@ def run_workload(args):
         gbs, hbm_peak = bytes_launch / per / 1e9, hbm_peak_gbs()[0]
         fp32 = {"bound": "fp32", "achieved": achieved, "peak": sgemm, "unit": "TFLOP/s",
                 "frac": achieved / sgemm if sgemm else None, "flops_per_env_step": flops}
+        ref_flops = extra.get("flops_per_env_step_reference_algorithm")
+        if ref_flops:
+            # the same run in the reference algorithm's count (its dense or full 3x3 form), against the
+            # measured SGEMM rate and the nominal FP32 FMA rate of 148 SMs x 128 lanes at 1,965 MHz
+            ref = ref_flops * units / per / 1e12
+            fp32["reference_algorithm"] = {"achieved": ref, "frac": ref / sgemm if sgemm else None,
+                                           "frac_of_nominal": ref / NOMINAL_FP32_TFLOPS}
         hbm = {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
                "bytes_per_launch": bytes_launch / T, "peak_kind": "measured (MEASURED_PEAKS.json)"}
         roof = {**hbm, "fp32": fp32} if hbm_bound else {**fp32, "hbm": hbm}
