@@ -63,12 +63,8 @@ constexpr float TWO_PI = 6.283185307179586f;
 constexpr float HALF_PI = 1.5707963267948966f;
 constexpr float RESET_BOUND = 0.1f;
 // Products of the unit link constants, as the reference's Python evaluates them.
-constexpr float D1_CONST = 0.25f;   // m1 lc1^2
-constexpr float D1_INNER = 1.25f;   // l1^2 + lc2^2
-constexpr float D2_CONST = 0.25f;   // lc2^2
 constexpr float PHI2_K = 4.9f;      // m2 lc2 g
 constexpr float PHI1_K = 14.700000000000001f;  // (m1 lc1 + m2 l1) g
-constexpr float DENOM_CONST = 1.25f;  // m2 lc2^2 + I2
 }  // namespace ac
 
 struct Acrobot {
@@ -110,25 +106,36 @@ RLENV_D AcrobotTrig acrobot_stage_trig(const Acrobot& s) {
   return t;
 }
 
-// Gym AcrobotEnv._dsdt with the torque passed alongside (acrobot_np.py:64-86),
-// rearranged: dd2 = (torque + d2/d1 phi1 - 0.5 w1^2 s2 - phi2) / (1.25 - d2^2/d1)
-// multiplied through by d1, and both 1/d1 and 1/(1.25 d1 - d2^2) taken from one
-// reciprocal of their product, which lies in [6.4, 12.7] for every angle (d1 in
-// [2.5, 4.5], 1.25 d1 - d2^2 = 2.8125 - c2^2/4). The reciprocal is the hardware
-// approximation (__fdividef, within 2 ulp on that range): on a B200 it saves 5%
-// of the T-step kernel's time, and its one-step error against the reference is
-// the same as with a correctly rounded reciprocal.
+// Gym AcrobotEnv._dsdt with the torque passed alongside (acrobot_np.py:64-86), with the unit
+// link constants folded (m1 = m2 = l1 = I1 = I2 = 1, lc1 = lc2 = 1/2, g = 9.8):
+//   d1 = m1 lc1^2 + m2 (l1^2 + lc2^2 + 2 l1 lc2 c2) + I1 + I2 = 3.5 + c2,
+//   d2 = m2 (lc2^2 + l1 lc2 c2) + I2 = 1.25 + c2 / 2,
+//   phi1 = -(1/2) w2^2 s2 - w2 w1 s2 + 14.7 s1 + phi2 = -(w2 s2)(w2 / 2 + w1) + 14.7 s1 + phi2,
+//   dd2 = (torque + d2/d1 phi1 - (1/2) w1^2 s2 - phi2) / (1.25 - d2^2/d1), multiplied through by
+//   d1: its denominator 1.25 d1 - d2^2 = 2.8125 - c2^2 / 4,
+//   dd1 = -(d2 dd2 + phi1) / d1;
+// both 1/d1 and 1/(2.8125 - c2^2/4) come from one reciprocal of their product, which lies in
+// [6.4, 12.7] for every angle. The same dynamics as the reference term by term; each folded
+// constant is exact, so only the rounding of the sums differs (the single-step gate is 1e-5).
+// The reciprocal is the hardware approximation (rcp.approx, within one ulp): against a
+// correctly rounded division it saves 5% of the T-step kernel's time at the same one-step
+// error against the reference.
+RLENV_D float acrobot_rcp(float a) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
+  return r;
+}
+
 RLENV_D Acrobot acrobot_dsdt(const Acrobot& s, const AcrobotTrig& t, float torque) {
-  const float s12 = t.s1 * t.c2 + t.c1 * t.s2;
-  const float d1 = ac::D1_CONST + (ac::D1_INNER + t.c2) + 1.0f + 1.0f;  // m1 lc1^2 + m2 (l1^2 + lc2^2 + 2 l1 lc2 c2) + I1 + I2
-  const float d2 = (ac::D2_CONST + 0.5f * t.c2) + 1.0f;                 // m2 (lc2^2 + l1 lc2 c2) + I2
-  const float phi2 = ac::PHI2_K * s12;
-  const float phi1 = -0.5f * (s.dth2 * s.dth2) * t.s2 - s.dth2 * s.dth1 * t.s2 + ac::PHI1_K * t.s1 + phi2;
-  const float num = d1 * (torque - 0.5f * (s.dth1 * s.dth1) * t.s2 - phi2) + d2 * phi1;
-  const float den = ac::DENOM_CONST * d1 - d2 * d2;
-  const float r = __fdividef(1.0f, d1 * den);
+  const float d1 = 3.5f + t.c2;
+  const float d2 = fmaf(0.5f, t.c2, 1.25f);
+  const float phi2 = ac::PHI2_K * fmaf(t.s1, t.c2, t.c1 * t.s2);  // 4.9 sin(t1 + t2)
+  const float phi1 = fmaf(-(s.dth2 * t.s2), fmaf(0.5f, s.dth2, s.dth1), fmaf(ac::PHI1_K, t.s1, phi2));
+  const float num = fmaf(d1, fmaf(-0.5f * s.dth1, s.dth1 * t.s2, torque - phi2), d2 * phi1);
+  const float den = fmaf(-0.25f * t.c2, t.c2, 2.8125f);
+  const float r = acrobot_rcp(d1 * den);
   const float dd2 = num * (d1 * r);
-  const float dd1 = -(d2 * dd2 + phi1) * (den * r);
+  const float dd1 = -fmaf(d2, dd2, phi1) * (den * r);
   return Acrobot{s.dth1, s.dth2, dd1, dd2};
 }
 

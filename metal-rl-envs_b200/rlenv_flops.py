@@ -9,8 +9,9 @@ csrc/*.cuh term by term; they are the denominators' numerators, not profiler
 readings.
 """
 
-# Acrobot (classic.cuh): one derivative evaluation is 36 flops, 4 divides included,
-# and 4 transcendentals (sin and cos of theta2, two cosines for the potential terms).
+# Acrobot: Gym's derivative as the reference writes it (acrobot_np.py:64-86) is 36 flops, 4
+# divides included, and 4 transcendentals (sin and cos of theta2, two cosines for the potential
+# terms); classic.cuh evaluates it with the unit constants folded, in 33.
 # RK4: 4 derivatives (144) + three stage states (4 x 2 x 3 = 24) + the weighted sum and
 # update (4 x 7 = 28) + two wraps (2 x 5) + two clips (2 x 2) + termination (3): 213 flops;
 # transcendentals 4 x 4 + 2 (termination) = 18.
@@ -42,20 +43,21 @@ def mass_matrix_flops(k):
 
 
 def aba_flops(k):
-    """Per step of the articulated-body form as this build computes it (the rank-one form of
-    csrc/pendulum.cuh, aba_accel_unrolled): per link and RK4 stage, the outward velocity 9, the
-    inward step 24 (own bias 5, the joint's D, u / D, U1 / D and the projected inertia 8, its
-    bias 4, the rank-one carry 7), the last pass's acceleration 16; plus the RK4 combination
-    (12 per link). Transcendentals: one sine and cosine per link and stage, and the termination
-    cosines. The long-chain kernel recomputes the link velocities and the joint trig instead of
-    storing them; that recomputation is not counted."""
-    return dict(flops=4 * 49 * k + 12 * k, transcendentals=4 * 2 * k + k)
-
-
-def aba_reference_flops(k):
-    """The same step as the reference counts it (bench_aba.py:53-55): about 140 flops per link
-    and stage over the three passes of the full 3x3 spatial algebra, plus the RK4 combination."""
+    """Per step of the articulated-body form as the reference counts it (bench_aba.py:53-55) and
+    the survey's measurement table fixes it: about 140 flops per link and stage over the three
+    passes of the full 3x3 spatial algebra, plus the RK4 combination. The roofline uses it."""
     return dict(flops=4 * 140 * k + 12 * k, transcendentals=4 * 6 * k + k)
+
+
+def aba_rank_one_flops(k):
+    """The same step as this build computes it (the rank-one form of csrc/pendulum.cuh,
+    aba_accel_unrolled): per link and RK4 stage, the outward velocity 9, the inward step 24 (own
+    bias 5, the joint's D, u / D, U1 / D and the projected inertia 8, its bias 4, the rank-one
+    carry 7), the last pass's acceleration 16; plus the RK4 combination (12 per link).
+    Transcendentals: one sine and cosine per link and stage, and the termination cosines. The
+    long-chain kernel recomputes the link velocities and the joint trig instead of storing them;
+    that recomputation is not counted."""
+    return dict(flops=4 * 49 * k + 12 * k, transcendentals=4 * 2 * k + k)
 
 
 def legged_flops(c, iters=8):
