@@ -28,14 +28,34 @@ struct CartPole {
   float x, xd, th, thd;
 };
 
-// One Euler step for a push of `force` (cartpole_np.py:58-77).
+// The hardware reciprocal (rcp.approx, within one ulp) for denominators known to be normal.
+RLENV_D float rcp_hw(float a) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
+  return r;
+}
+
+// One Euler step for a push of `force` (cartpole_np.py:58-77), with the divisions by the
+// total mass M folded into constants (m l / M and 1 / M, each the float32 of the exact
+// quotient):
+//   temp = force / M + (m l / M) thd^2 sin,
+//   th_acc = (G sin - cos temp) / (l (4/3 - m cos^2 / M)) = (G sin - cos temp) / (2/3 - (m l / M) cos^2),
+//   x_acc = temp - (m l / M) th_acc cos,
+// the pole's denominator, in [0.62, 0.67], through the hardware reciprocal. The sine and cosine
+// come from the special function unit on the angle as given (sincos_sfu_near): a live pole is
+// within 12 degrees of upright and a fresh one within 0.05 rad, where the unit is within
+// 4.1e-7. The step's done flag depends on the state stepped from only (explicit Euler moves x
+// and theta by the old rates), so the flags are the reference's whatever the rounding here;
+// the rates move by a few 1e-8 against the reference's step.
 RLENV_D CartPole cartpole_physics(CartPole s, float force) {
+  constexpr float kInvM = float(1.0 / 1.1);
+  constexpr float kMlOverM = float(0.05 / 1.1);
+  constexpr float kTwoThirds = float(2.0 / 3.0);
   float sn, c;
-  sincos_fast(s.th, &sn, &c);
-  float temp = (force + cp::POLE_MASS_LENGTH * (s.thd * s.thd) * sn) / cp::TOTAL_MASS;
-  float th_acc = (cp::G * sn - c * temp) /
-                 (cp::HALF_POLE * (cp::FOUR_THIRDS - cp::POLE_MASS * (c * c) / cp::TOTAL_MASS));
-  float x_acc = temp - cp::POLE_MASS_LENGTH * th_acc * c / cp::TOTAL_MASS;
+  sincos_sfu_near(s.th, &sn, &c);
+  const float temp = fmaf(kMlOverM * (s.thd * s.thd), sn, force * kInvM);
+  const float th_acc = (cp::G * sn - c * temp) * rcp_hw(fmaf(-kMlOverM * c, c, kTwoThirds));
+  const float x_acc = fmaf(-kMlOverM * th_acc, c, temp);
   CartPole n;
   n.x = s.x + cp::TAU * s.xd;
   n.xd = s.xd + cp::TAU * x_acc;
@@ -120,12 +140,6 @@ RLENV_D AcrobotTrig acrobot_stage_trig(const Acrobot& s) {
 // The reciprocal is the hardware approximation (rcp.approx, within one ulp): against a
 // correctly rounded division it saves 5% of the T-step kernel's time at the same one-step
 // error against the reference.
-RLENV_D float acrobot_rcp(float a) {
-  float r;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
-  return r;
-}
-
 RLENV_D Acrobot acrobot_dsdt(const Acrobot& s, const AcrobotTrig& t, float torque) {
   const float d1 = 3.5f + t.c2;
   const float d2 = fmaf(0.5f, t.c2, 1.25f);
@@ -133,7 +147,7 @@ RLENV_D Acrobot acrobot_dsdt(const Acrobot& s, const AcrobotTrig& t, float torqu
   const float phi1 = fmaf(-(s.dth2 * t.s2), fmaf(0.5f, s.dth2, s.dth1), fmaf(ac::PHI1_K, t.s1, phi2));
   const float num = fmaf(d1, fmaf(-0.5f * s.dth1, s.dth1 * t.s2, torque - phi2), d2 * phi1);
   const float den = fmaf(-0.25f * t.c2, t.c2, 2.8125f);
-  const float r = acrobot_rcp(d1 * den);
+  const float r = rcp_hw(d1 * den);
   const float dd2 = num * (d1 * r);
   const float dd1 = -fmaf(d2, dd2, phi1) * (den * r);
   return Acrobot{s.dth1, s.dth2, dd1, dd2};

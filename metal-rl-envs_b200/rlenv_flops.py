@@ -17,8 +17,9 @@ readings.
 # transcendentals 4 x 4 + 2 (termination) = 18.
 ACROBOT = dict(flops=213, transcendentals=18)
 
-# CartPole (classic.cuh): temp 5, theta_acc 9 (one divide each side), x_acc 5, four Euler
-# updates as FMAs (8), termination 2 compares: 29 flops; sin and cos: 2.
+# CartPole as the reference writes it (cartpole_np.py:58-77): temp 5, theta_acc 9 (one divide
+# each side), x_acc 5, four Euler updates as FMAs (8), termination 2 compares: 29 flops; sin and
+# cos: 2. classic.cuh folds the divisions by the total mass into constants.
 CARTPOLE = dict(flops=29, transcendentals=2)
 
 # Bytes moved per environment step by the single-step kernel: state in and out
