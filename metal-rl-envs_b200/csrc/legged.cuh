@@ -42,6 +42,17 @@ constexpr float INV_I_T = 1.0f / I_T;
 namespace lgx {
 constexpr unsigned kFull = 0xffffffffu;
 RLENV_D float mul(float a, float b) { return __fmul_rn(a, b); }
+// Products with the leg length L and with 1 / L^2 (both 1 in the reference's model,
+// legged_np.py:26): an explicit multiply by one is still an instruction, and a substep has
+// about fifty of them at C = 4. Skipping them changes no bit.
+RLENV_D float times_l(float x) {
+  if constexpr (lg::L == 1.0f) return x;
+  else return __fmul_rn(lg::L, x);
+}
+RLENV_D float times_inv_l2(float x) {
+  if constexpr (lg::INV_L2 == 1.0f) return x;
+  else return __fmul_rn(x, lg::INV_L2);
+}
 RLENV_D float add(float a, float b) { return __fadd_rn(a, b); }
 RLENV_D float sub(float a, float b) { return __fsub_rn(a, b); }
 
@@ -286,8 +297,8 @@ RLENV_D void legged_substep(float (&qt)[3], float (&vt)[3], float (&ql)[C / G], 
     sincos_sfu(add(qt[2], ql[c]), &sa, &ca);
     const float ad = add(vt[2], vl[c]);
     const float ad2 = mul(ad, ad);
-    lca[c] = mul(lg::L, ca);
-    lsa[c] = mul(lg::L, sa);
+    lca[c] = times_l(ca);
+    lsa[c] = times_l(sa);
     const float dx = -mul(lsa[c], ad2);  // foot acceleration at zero joint acceleration
     const float dy = mul(lca[c], ad2);
     depth[c] = sub(lca[c], qt[1]);
@@ -301,8 +312,8 @@ RLENV_D void legged_substep(float (&qt)[3], float (&vt)[3], float (&ql)[C / G], 
     e1[4][c] = dy;
     e1[5][c] = t_dr;
     e1[6][c] = lsa[c];
-    e1[7][c] = mul(mul(lca[c], lg::INV_L2), fl[c]);
-    e1[8][c] = mul(mul(lsa[c], lg::INV_L2), fl[c]);
+    e1[7][c] = mul(times_inv_l2(lca[c]), fl[c]);
+    e1[8][c] = mul(times_inv_l2(lsa[c]), fl[c]);
     e1[9][c] = fl[c];
     e1[10][c] = lca[c];
   }
@@ -342,7 +353,7 @@ RLENV_D void legged_substep(float (&qt)[3], float (&vt)[3], float (&ql)[C / G], 
     const float x2 = mul(r2, lg::INV_I_T);
 #pragma unroll
     for (int c = 0; c < CL; ++c)
-      bl[c] = sub(sub(mul(bl[c], lg::INV_D), mul(fmaf(lca[c], x0, mul(lsa[c], x1)), lg::INV_L2)), x2);
+      bl[c] = sub(sub(mul(bl[c], lg::INV_D), times_inv_l2(fmaf(lca[c], x0, mul(lsa[c], x1)))), x2);
     b0 = x0;
     b1 = x1;
     b2 = x2;
@@ -368,8 +379,8 @@ RLENV_D void legged_substep(float (&qt)[3], float (&vt)[3], float (&ql)[C / G], 
   // P_l = lsa_l lt_l - lca_l ln_l. So the sweeps keep G below the diagonal (packed,
   // G[k][l] at tri(k - 1, l)), the running P_l and the diagonal blocks.
   auto g_of = [](float la, float ls, float& g0, float& g1) {
-    g0 = mul(ls, lg::INV_L2);
-    g1 = -mul(la, lg::INV_L2);
+    g0 = times_inv_l2(ls);
+    g1 = -times_inv_l2(la);
   };
   auto h_of = [&](float g0, float g1, float& h0, float& h1) {
     h0 = fmaf(s00, g0, mul(s01, g1));
@@ -477,8 +488,8 @@ RLENV_D void legged_substep(float (&qt)[3], float (&vt)[3], float (&ql)[C / G], 
       e3[0][c] = lt[c];
       e3[1][c] = ln[c];
       e3[2][c] = rl[c];
-      e3[3][c] = mul(mul(lca[c], lg::INV_L2), rl[c]);
-      e3[4][c] = mul(mul(lsa[c], lg::INV_L2), rl[c]);
+      e3[3][c] = mul(times_inv_l2(lca[c]), rl[c]);
+      e3[4][c] = mul(times_inv_l2(lsa[c]), rl[c]);
     }
     contact_exchange<C, G, kXch3Fields>(e3, a3, xch + kXch3 * C, gl);
   }
