@@ -37,7 +37,7 @@ RLENV_D void decode_torques(int a, float (&tq)[C]) {
 // null) and, with IMPULSES, rows [t * 2C, t * 2C + 2C) of impulse_seq. One step is
 // the launch with T = 1, so a chain of single steps and one T-step launch agree bit
 // for bit.
-template <int C, bool BRANCHY, bool IMPULSES>
+template <int C, bool BRANCHY, bool IMPULSES, int kIters>
 __global__ void __launch_bounds__(128)
 legged_kernel(const float* __restrict__ state, const void* __restrict__ actions, int dtype,
               uint32_t seed0, const float* __restrict__ stand, float assist,
@@ -71,7 +71,8 @@ legged_kernel(const float* __restrict__ state, const void* __restrict__ actions,
     for (int k = 0; k < 2 * C; ++k) imp[k] = 0.0f;
 #pragma unroll 1
     for (int ss = 0; ss < lg::SUBSTEPS; ++ss)
-      legged_substep<C, 1, BRANCHY, IMPULSES>(qt, vt, ql, vl, tq, k_assist, iters, nullptr, 0, true, imp);
+      legged_substep<C, 1, BRANCHY, IMPULSES, false, kIters>(qt, vt, ql, vl, tq, k_assist, iters, nullptr, 0,
+                                                           true, imp);
     if constexpr (IMPULSES) {
 #pragma unroll
       for (int k = 0; k < 2 * C; ++k) {
@@ -107,20 +108,23 @@ using LeggedFn = void (*)(const float*, const void*, int, uint32_t, const float*
                           const float*, int, int64_t, int64_t, int64_t, float*, float*, uint8_t*,
                           float*);
 
-template <bool IMPULSES>
+// kIters = 8 (the reference's ITERS, legged_np.py:27, and the legged tasks' sweeps) has its own
+// instances with the sweeps unrolled; any other count runs the loop.
+template <bool IMPULSES, int kIters>
 LeggedFn pick_c(int c, bool branchy) {
-  if (branchy) return c == 1 ? &legged_kernel<1, true, IMPULSES> : nullptr;
+  if (branchy) return c == 1 ? &legged_kernel<1, true, IMPULSES, kIters> : nullptr;
   switch (c) {
-    case 1: return &legged_kernel<1, false, IMPULSES>;
-    case 2: return &legged_kernel<2, false, IMPULSES>;
-    case 3: return &legged_kernel<3, false, IMPULSES>;
-    case 4: return &legged_kernel<4, false, IMPULSES>;
+    case 1: return &legged_kernel<1, false, IMPULSES, kIters>;
+    case 2: return &legged_kernel<2, false, IMPULSES, kIters>;
+    case 3: return &legged_kernel<3, false, IMPULSES, kIters>;
+    case 4: return &legged_kernel<4, false, IMPULSES, kIters>;
     default: return nullptr;
   }
 }
 
-LeggedFn pick(int c, bool branchy, bool impulses) {
-  return impulses ? pick_c<true>(c, branchy) : pick_c<false>(c, branchy);
+LeggedFn pick(int c, bool branchy, bool impulses, int iters) {
+  if (iters == 8) return impulses ? pick_c<true, 8>(c, branchy) : pick_c<false, 8>(c, branchy);
+  return impulses ? pick_c<true, 0>(c, branchy) : pick_c<false, 0>(c, branchy);
 }
 
 int launch_legged(int c, bool branchy, int iters, const float* state, const void* actions,
@@ -128,7 +132,7 @@ int launch_legged(int c, bool branchy, int iters, const float* state, const void
                   const float* assist_ptr, int64_t T, int64_t n, int64_t off, float* next,
                   float* reward_seq, uint8_t* done_seq, float* impulse_seq, void* stream) {
   if (n < 0 || T < 0 || !valid_dtype(dtype) || iters < 1) return RLENV_EINVAL;
-  LeggedFn fn = pick(c, branchy, impulse_seq != nullptr);
+  LeggedFn fn = pick(c, branchy, impulse_seq != nullptr, iters);
   if (!fn) return RLENV_EUNSUPPORTED;
   if (n == 0) return RLENV_OK;
   if (!state || (T > 0 && !actions) || !stand || !next) return RLENV_EINVAL;

@@ -246,13 +246,13 @@ RLENV_D float contact_solve(const ContactAffine& a, float s) {
 // least recently updated first, so that only its last multiply-add waits for the contact
 // solved just before (legged_np.py:91-94).
 
-template <int C, bool kAll>
+template <int C, bool kAll, int kSweeps = 0>
 RLENV_D void gauss_seidel(const ContactAffine (&af)[C], const float (&gkl)[C * (C - 1) / 2 + 1],
                           unsigned act, int sweeps, float (&sk)[C]) {
   float pl[C];
 #pragma unroll
   for (int k = 0; k < C; ++k) pl[k] = 0.0f;
-  for (int it = 0; it < sweeps; ++it) {
+  auto sweep = [&]() {
 #pragma unroll
     for (int k = 0; k < C; ++k) {
       if (!kAll && !(act & (1u << k))) continue;
@@ -266,6 +266,14 @@ RLENV_D void gauss_seidel(const ContactAffine (&af)[C], const float (&gkl)[C * (
       pl[k] = contact_solve(af[k], s);
       sk[k] = s;
     }
+  };
+  if constexpr (kSweeps > 0) {
+    // a sweep count known at compile time: the sweeps unrolled, the same operations in the same
+    // order as the loop below
+#pragma unroll
+    for (int it = 0; it < kSweeps; ++it) sweep();
+  } else {
+    for (int it = 0; it < sweeps; ++it) sweep();
   }
 }
 
@@ -278,7 +286,7 @@ RLENV_D void gauss_seidel(const ContactAffine (&af)[C], const float (&gkl)[C * (
 // with `alive` set touches are left out of the sweeps: their impulse is zero in every
 // sweep, and a zero term changes no sum, so the results are the same; with one contact
 // left, one sweep already gives the result of all of them.
-template <int C, int G, bool BRANCHY, bool IMPULSES = false, bool SKIP = false>
+template <int C, int G, bool BRANCHY, bool IMPULSES = false, bool SKIP = false, int kIters = 0>
 RLENV_D void legged_substep(float (&qt)[3], float (&vt)[3], float (&ql)[C / G], float (&vl)[C / G],
                             const float (&tq)[C / G], float assist, int iters, float* xch = nullptr,
                             int gl = 0, bool alive = true, float* imp = nullptr) {
@@ -463,7 +471,7 @@ RLENV_D void legged_substep(float (&qt)[3], float (&vt)[3], float (&ql)[C / G], 
       for (int k = 0; k < C; ++k)
         if (__any_sync(kFull, alive && af[k].g0 > -INFINITY)) act |= 1u << k;
     }
-    if (act == kAllMask) gauss_seidel<C, true>(af, gkl, act, iters, sk);
+    if (act == kAllMask) gauss_seidel<C, true, kIters>(af, gkl, act, iters, sk);
     else if (act != 0u) gauss_seidel<C, false>(af, gkl, act, __popc(act) == 1 ? 1 : iters, sk);
 #pragma unroll
     for (int c = 0; c < CL; ++c) {
