@@ -176,7 +176,7 @@ struct LeggedSlice {
 // (legged_rollout_metal.py:52-55). Every lane stays in the loop until the last member of its
 // warp has fallen (finished members keep stepping, unrecorded), so the exchanges and the
 // warp-wide votes of the substep's contact skipping always see 32 lanes.
-template <int C, int H, int G>
+template <int C, int H, int G, int kIters>
 __global__ void __launch_bounds__(32)
 legged_rollout_kernel(const float* __restrict__ state, const float* __restrict__ theta,
                       int64_t stride, int64_t p, int horizon, int iters, float alive_bonus,
@@ -311,7 +311,7 @@ legged_rollout_kernel(const float* __restrict__ state, const float* __restrict__
     }
 #pragma unroll 1
     for (int ss = 0; ss < lg::SUBSTEPS; ++ss)
-      legged_substep<C, G, false, false, true>(qt, vt, ql, vl, tq, assist, iters, xch, gl, alive);
+      legged_substep<C, G, false, false, true, kIters>(qt, vt, ql, vl, tq, assist, iters, xch, gl, alive);
     if (alive) {
       taken += 1.0f;
       if (legged_terminated(qt)) {
@@ -398,43 +398,46 @@ struct LeggedLaunch {
   int lanes;
 };
 
-template <int C, int H, int G>
+// kIters = 8 (legged_rollout_metal.py's ITERS, the sweeps of every legged task) has its own
+// instances for the tasks' two and four legs, with the sweeps unrolled; other counts loop.
+template <int C, int H, int G, int kIters>
 LeggedLaunch legged_instance() {
   if constexpr (C % G == 0 && H % G == 0 && (G == 1 || C % 2 == 0))
-    return LeggedLaunch{&legged_rollout_kernel<C, H, G>, LeggedSlice<C, H, G>::kSmem, G};
+    return LeggedLaunch{&legged_rollout_kernel<C, H, G, kIters>, LeggedSlice<C, H, G>::kSmem, G};
   else
     return LeggedLaunch{nullptr, 0, G};
 }
 
-template <int C, int H>
+template <int C, int H, int kIters>
 LeggedLaunch pick_legged_g(int g) {
   switch (g) {
-    case 1: return legged_instance<C, H, 1>();
-    case 2: return legged_instance<C, H, 2>();
-    case 4: return legged_instance<C, H, 4>();
+    case 1: return legged_instance<C, H, 1, kIters>();
+    case 2: return legged_instance<C, H, 2, kIters>();
+    case 4: return legged_instance<C, H, 4, kIters>();
     default: return LeggedLaunch{nullptr, 0, g};
   }
 }
 
-template <int C>
+template <int C, int kIters = 0>
 LeggedLaunch pick_legged_h(int h, int g) {
   switch (h) {
-    case 1: return pick_legged_g<C, 1>(g);
-    case 2: return pick_legged_g<C, 2>(g);
-    case 4: return pick_legged_g<C, 4>(g);
-    case 8: return pick_legged_g<C, 8>(g);
-    case 16: return pick_legged_g<C, 16>(g);
-    case 32: return pick_legged_g<C, 32>(g);
+    case 1: return pick_legged_g<C, 1, kIters>(g);
+    case 2: return pick_legged_g<C, 2, kIters>(g);
+    case 4: return pick_legged_g<C, 4, kIters>(g);
+    case 8: return pick_legged_g<C, 8, kIters>(g);
+    case 16: return pick_legged_g<C, 16, kIters>(g);
+    case 32: return pick_legged_g<C, 32, kIters>(g);
     default: return LeggedLaunch{nullptr, 0, g};
   }
 }
 
-LeggedLaunch pick_legged(int c, int h, int g) {
+LeggedLaunch pick_legged(int c, int h, int g, int iters) {
+  const bool eight = iters == 8;
   switch (c) {
     case 1: return pick_legged_h<1>(h, g);
-    case 2: return pick_legged_h<2>(h, g);
+    case 2: return eight ? pick_legged_h<2, 8>(h, g) : pick_legged_h<2>(h, g);
     case 3: return pick_legged_h<3>(h, g);
-    case 4: return pick_legged_h<4>(h, g);
+    case 4: return eight ? pick_legged_h<4, 8>(h, g) : pick_legged_h<4>(h, g);
     default: return LeggedLaunch{nullptr, 0, g};
   }
 }
@@ -506,9 +509,9 @@ int rlenv_legged_rollout_lanes(int lanes, int c, int hidden, int horizon, int it
                                float* steps, void* stream) {
   using namespace rlenv;
   if (p < 0 || horizon < 0 || theta_stride < 0 || iters < 1) return RLENV_EINVAL;
-  if (pick_legged(c, hidden, 1).fn == nullptr) return RLENV_EUNSUPPORTED;
+  if (pick_legged(c, hidden, 1, iters).fn == nullptr) return RLENV_EUNSUPPORTED;
   if (lanes == 0) lanes = legged_lanes(c, hidden, p);
-  const LeggedLaunch L = pick_legged(c, hidden, lanes);
+  const LeggedLaunch L = pick_legged(c, hidden, lanes, iters);
   if (!L.fn) return RLENV_EUNSUPPORTED;
   if (p == 0) return RLENV_OK;
   if (!state || !theta || !fitness || !steps) return RLENV_EINVAL;
