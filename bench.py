@@ -860,7 +860,7 @@ def run_workload(args):
             fl = (rlenv_flops.aba_flops(k) if args.workload == "pendulum_aba" else rlenv_flops.mass_matrix_flops(k))["flops"]
             extra = {"links": k}
             if args.workload == "pendulum_aba":
-                # the roofline counts the reference's (and the survey's) 4 x 140 K + 12 K; this
+                # the roofline counts the reference's 4 x 140 K + 12 K (bench_aba.py:53-55); this
                 # build's rank-one form does fewer
                 extra["flops_per_env_step_this_algorithm"] = rlenv_flops.aba_rank_one_flops(k)["flops"]
         actions = torch.randint(0, n_act, (T, n), device=dev, generator=g).to(torch.uint8 if n_act < 256 else torch.int32)

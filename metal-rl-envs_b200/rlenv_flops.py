@@ -44,9 +44,9 @@ def mass_matrix_flops(k):
 
 
 def aba_flops(k):
-    """Per step of the articulated-body form as the reference counts it (bench_aba.py:53-55) and
-    the survey's measurement table fixes it: about 140 flops per link and stage over the three
-    passes of the full 3x3 spatial algebra, plus the RK4 combination. The roofline uses it."""
+    """Per step of the articulated-body form as the reference counts it (bench_aba.py:53-55):
+    about 140 flops per link and stage over the three passes of the full 3x3 spatial algebra,
+    plus the RK4 combination. The roofline uses it."""
     return dict(flops=4 * 140 * k + 12 * k, transcendentals=4 * 6 * k + k)
 
 
