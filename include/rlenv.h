@@ -28,7 +28,8 @@
  *    environment `index_offset` draws exactly the resets the unsharded batch
  *    would.
  *  - Actions are integer arrays of N elements whose element type is given by
- *    `action_dtype` (RLENV_I32, RLENV_I64 or RLENV_U8).
+ *    `action_dtype` (RLENV_I32, RLENV_I64 or RLENV_U8; the CartPole and Acrobot kernels
+ *    also take RLENV_U2, four steps' actions packed into a byte).
  *  - `done` is one byte per environment, 0 or 1 (torch.bool layout).
  */
 #ifndef RLENV_H
@@ -54,6 +55,12 @@ extern "C" {
 #define RLENV_I32 0
 #define RLENV_I64 1
 #define RLENV_U8 2
+/* Actions packed along time, CartPole and Acrobot step kernels only (the other kernels
+ * answer RLENV_EINVAL): a (ceil(T / 4), N) byte array whose byte (r, i) holds environment i's
+ * actions of steps 4r .. 4r + 3, step 4r + u in bits 2u .. 2u + 1 (a single step reads bits
+ * 0-1 of N bytes). A caller that streams T steps of actions from host memory moves a quarter
+ * of the uint8 bytes. No counterpart in the reference, whose kernels read int32 actions. */
+#define RLENV_U2 3
 
 /* Human-readable message for a status code; the string is static. */
 RLENV_API const char* rlenv_strerror(int code);

@@ -46,7 +46,12 @@ def step(state, action):
     """Advance all N environments by one step in one kernel launch."""
     state = _rl.as_state(state, ROWS)
     n = state.shape[1]
-    action, dt = _rl.as_actions(action, n, state.device)
+    if isinstance(action, _rl.PackedActions):  # rlenv_lib.pack_actions of one step
+        if action.steps != 1:
+            raise ValueError(f"step takes the packed actions of one step; got {action.steps}")
+        action, dt = action.checked(n, state.device), _rl.U2
+    else:
+        action, dt = _rl.as_actions(action, n, state.device)
     nxt, reward, done = _rl.step_outputs(ROWS, n, state.device)
     _rl.check(_rl.lib().cartpole_step(state.data_ptr(), action.data_ptr(), dt, _counter.next(), n, 0,
                                       nxt.data_ptr(), reward.data_ptr(), done.data_ptr(),
@@ -57,5 +62,7 @@ def step(state, action):
 def step_many(state, actions, rewards=True, dones=True, sums=False, out=None):
     """T steps in one launch for actions (T, N). Returns (final_state, rewards (T, N) or None,
     dones (T, N) or None[, reward_sum (N,), done_count (N,)] if sums). `out` may give the
-    final-state tensor (it may be `state` itself)."""
+    final-state tensor (it may be `state` itself). actions may also be rlenv_lib.pack_actions'
+    PackedActions, four steps to a byte: the same results from a quarter of the uint8 bytes (for a
+    caller that streams actions from host memory)."""
     return _rl.run_step_many(_rl.lib().cartpole_step_many, ROWS, _counter, state, actions, rewards, dones, sums, out)

@@ -83,6 +83,25 @@ struct AcrobotEnv {
   }
 };
 
+// RLENV_U2: actions packed along time, four steps to a byte: byte (r, i) of the (ceil(T / 4), n)
+// array holds environment i's actions of steps 4r .. 4r + 3, step 4r + u in bits 2u. Packed2 is
+// its element type in the kernels. A thread reads one byte (four for four environments) per four
+// steps and shifts two bits out per step.
+struct Packed2 {
+  uint8_t bits;
+};
+template <typename A>
+constexpr bool kPacked = std::is_same_v<A, Packed2>;
+
+// The packed bytes of V consecutive environments from byte offset `at` (four bytes in one
+// 32-bit load for V = 4, whose offset is a multiple of four).
+template <int V>
+RLENV_D uint32_t load_packed(const Packed2* __restrict__ a, int64_t at) {
+  const uint8_t* p = reinterpret_cast<const uint8_t*>(a) + at;
+  if constexpr (V == 4) return __ldg(reinterpret_cast<const unsigned int*>(p));
+  else return __ldg(p);
+}
+
 // Load V consecutive actions starting at element `i` (i is a multiple of V).
 template <typename A, int V>
 RLENV_D void load_actions(const A* __restrict__ a, int64_t i, int (&out)[V]) {
@@ -170,10 +189,13 @@ RLENV_D void store_states(float* __restrict__ s, int64_t n, int64_t i, const typ
 }
 
 // SUMS selects the instance that also accumulates per-environment reward sums
-// and termination counts; the plain chain keeps those registers free. SEQ is set
-// when both per-step sequences are written: the loop then has no per-step test
-// of their pointers (3.5% of the Acrobot kernel's time on a B200).
-template <typename Env, typename A, int V, bool SUMS, bool SEQ>
+// and termination counts; the plain chain keeps those registers free. SEQ says which
+// per-step sequences are written: kSeqBoth (the loop then has no per-step test of their
+// pointers: 3.5% of the Acrobot kernel's time on a B200), kSeqNone (no per-step row offset
+// either: the sums-only Acrobot instance then fits 32 registers without spilling), or
+// kSeqEither (either pointer may be null, tested per step).
+constexpr int kSeqEither = 0, kSeqBoth = 1, kSeqNone = 2;
+template <typename Env, typename A, int V, bool SUMS, int SEQ>
 __global__ void __launch_bounds__(Env::kBlock, Env::kMinBlocks)
 step_many_kernel(const float* __restrict__ state_in, const A* __restrict__ actions, uint32_t seed0,
                  int64_t T, int64_t n, int64_t off, float* __restrict__ state_out,
@@ -192,11 +214,32 @@ step_many_kernel(const float* __restrict__ state_in, const A* __restrict__ actio
   }
   // the next step's actions are loaded one step ahead, so their latency hides behind a step
   int act[V];
-  if (T > 0) load_actions<A, V>(actions, i, act);
+  // packed actions: the bytes of the current block of four steps (two bits shifted out per
+  // step) and of the next block, loaded four steps ahead; pat is the offset of the block after
+  [[maybe_unused]] uint32_t pcur = 0, pnxt = 0;
+  [[maybe_unused]] int64_t pat = 0;
+  if constexpr (kPacked<A>) {
+    if (T > 0) pcur = load_packed<V>(actions, i);
+    if (T > 4) pnxt = load_packed<V>(actions, n + i);
+    pat = 2 * n + i;
+  } else {
+    if (T > 0) load_actions<A, V>(actions, i, act);
+  }
   int64_t row = i;  // t * n + i, advanced by n per step
   for (int64_t t = 0; t < T; ++t, row += n) {
     int nxt[V] = {};
-    if (t + 1 < T) load_actions<A, V>(actions, row + n, nxt);
+    if constexpr (kPacked<A>) {
+#pragma unroll
+      for (int u = 0; u < V; ++u) act[u] = int((pcur >> (8 * u)) & 3u);
+      pcur = V == 1 ? pcur >> 2 : (pcur >> 2) & 0x3F3F3F3Fu;
+      if ((t & 3) == 3) {
+        pcur = pnxt;
+        if (t + 5 < T) pnxt = load_packed<V>(actions, pat);
+        pat += n;
+      }
+    } else {
+      if (t + 1 < T) load_actions<A, V>(actions, row + n, nxt);
+    }
     bool d[V];
     float rw[V];
 #pragma unroll
@@ -204,10 +247,17 @@ step_many_kernel(const float* __restrict__ state_in, const A* __restrict__ actio
 #pragma unroll
     for (int u = 0; u < V; ++u)
       d[u] = Env::step(st[u], aux[u], act[u], env_hash(seed0 + uint32_t(t), off + i + u), rw[u]);
+    if constexpr (!kPacked<A>) {
 #pragma unroll
-    for (int u = 0; u < V; ++u) act[u] = nxt[u];
-    if (SEQ || reward_seq) store_vec<V>(reward_seq, row, rw);
-    if (SEQ || done_seq) store_flags<V>(done_seq, row, d);
+      for (int u = 0; u < V; ++u) act[u] = nxt[u];
+    }
+    if constexpr (SEQ == kSeqBoth) {
+      store_vec<V>(reward_seq, row, rw);
+      store_flags<V>(done_seq, row, d);
+    } else if constexpr (SEQ == kSeqEither) {
+      if (reward_seq) store_vec<V>(reward_seq, row, rw);
+      if (done_seq) store_flags<V>(done_seq, row, d);
+    }
     if constexpr (SUMS) {
 #pragma unroll
       for (int u = 0; u < V; ++u) {
@@ -242,7 +292,7 @@ template <typename Env>
 int launch_step_many(const float* state_in, const void* actions, int dtype, uint32_t seed0,
                      int64_t T, int64_t n, int64_t off, float* state_out, float* reward_seq,
                      uint8_t* done_seq, float* reward_sum, float* done_count, void* stream) {
-  if (n < 0 || T < 0 || !valid_dtype(dtype)) return RLENV_EINVAL;
+  if (n < 0 || T < 0 || !(valid_dtype(dtype) || dtype == RLENV_U2)) return RLENV_EINVAL;
   if (n == 0) return RLENV_OK;
   if (!state_in || !state_out || (T > 0 && !actions)) return RLENV_EINVAL;
   const int esz = dtype == RLENV_I64 ? 8 : dtype == RLENV_I32 ? 4 : 1;
@@ -253,11 +303,15 @@ int launch_step_many(const float* state_in, const void* actions, int dtype, uint
                    (!reward_sum || aligned16(reward_sum)) && (!done_count || aligned16(done_count)) &&
                    (dtype == RLENV_I64 || (reinterpret_cast<uintptr_t>(actions) % (4 * esz)) == 0);
   cudaStream_t s = as_stream(stream);
-  return with_action_type(dtype, [&](auto tag) {
+  auto typed = [&](auto&& f) {
+    return dtype == RLENV_U2 ? f(static_cast<const Packed2*>(nullptr)) : with_action_type(dtype, f);
+  };
+  return typed([&](auto tag) {
     using A = std::remove_const_t<std::remove_pointer_t<decltype(tag)>>;
     const A* a = static_cast<const A*>(actions);
     auto go = [&](auto sums, auto seq) {
-      constexpr bool S = decltype(sums)::value, Q = decltype(seq)::value;
+      constexpr bool S = decltype(sums)::value;
+      constexpr int Q = decltype(seq)::value;
       constexpr int B = Env::kBlock;
       if constexpr (Env::kVec == 4) {
         if (vec) {
@@ -270,9 +324,15 @@ int launch_step_many(const float* state_in, const void* actions, int dtype, uint
           state_in, a, seed0, T, n, off, state_out, reward_seq, done_seq, reward_sum, done_count);
       return launch_status();
     };
-    const bool sums = reward_sum || done_count, seq = reward_seq && done_seq;
-    if (sums) return seq ? go(std::true_type{}, std::true_type{}) : go(std::true_type{}, std::false_type{});
-    return seq ? go(std::false_type{}, std::true_type{}) : go(std::false_type{}, std::false_type{});
+    using Both = std::integral_constant<int, kSeqBoth>;
+    using None = std::integral_constant<int, kSeqNone>;
+    using Either = std::integral_constant<int, kSeqEither>;
+    const bool sums = reward_sum || done_count;
+    const int seq = reward_seq && done_seq ? kSeqBoth : !reward_seq && !done_seq ? kSeqNone : kSeqEither;
+    auto with_seq = [&](auto s) {
+      return seq == kSeqBoth ? go(s, Both{}) : seq == kSeqNone ? go(s, None{}) : go(s, Either{});
+    };
+    return sums ? with_seq(std::true_type{}) : with_seq(std::false_type{});
   });
 }
 

@@ -24,7 +24,7 @@ LIB_PATH = Path(__file__).resolve().parent / "librlenv.so"
 # RLENV_LIBRARY=checks loads the check build instead (rlenv_build.build(checks=True))
 CHECKS_LIB_PATH = Path(__file__).resolve().parent / "librlenv_checks.so"
 
-I32, I64, U8 = 0, 1, 2
+I32, I64, U8, U2 = 0, 1, 2, 3
 _DTYPES = {torch.int32: I32, torch.int64: I64, torch.uint8: U8, torch.bool: U8}
 
 # name -> argument types; every function returns int except those in _RESTYPES
@@ -187,6 +187,48 @@ def as_actions(a, n, dev, name="action"):
     return a, _DTYPES[a.dtype]
 
 
+class PackedActions:
+    """Actions packed along time for the CartPole and Acrobot step kernels (RLENV_U2): `bits` is a
+    (ceil(steps / 4), N) uint8 tensor whose byte (r, i) holds environment i's actions of steps
+    4r .. 4r + 3, step 4r + u in bits 2u; `steps` is T. Made by pack_actions; a quarter of the
+    bytes of uint8 actions for a caller that streams them from host memory."""
+
+    def __init__(self, bits, steps):
+        self.bits = bits
+        self.steps = int(steps)
+
+    def checked(self, n, dev):
+        """The bits as a contiguous uint8 tensor on dev, checked against T = steps and n."""
+        b = torch.as_tensor(self.bits)
+        rows = (self.steps + 3) // 4
+        if b.dtype != torch.uint8 or self.steps < 0 or b.numel() != rows * n:
+            raise ValueError(f"packed actions of {self.steps} steps and {n} environments must be uint8 "
+                             f"({rows}, {n}); got {b.dtype} {tuple(b.shape)}")
+        return b.to(dev).contiguous()
+
+
+def pack_actions(a):
+    """Actions (T, N) (or (N,) for one step) with values in 0..3, packed along time into
+    PackedActions: byte (r, i) holds steps 4r .. 4r + 3 of environment i, two bits each, steps
+    past T zero; on a's device."""
+    if isinstance(a, np.ndarray):
+        a = torch.from_numpy(np.ascontiguousarray(a))
+    a = torch.as_tensor(a)
+    if a.dtype.is_floating_point:
+        raise ValueError(f"actions must be an integer array, got {a.dtype}")
+    if a.dim() == 1:
+        a = a[None]
+    if a.dim() != 2:
+        raise ValueError(f"actions must have shape (T, N) or (N,); got {tuple(a.shape)}")
+    steps, n = a.shape
+    b = a.to(torch.uint8) & 3
+    pad = (-steps) % 4
+    if pad:
+        b = torch.cat([b, torch.zeros((pad, n), dtype=torch.uint8, device=b.device)])
+    b = b.reshape(-1, 4, n)
+    return PackedActions((b[:, 0] | (b[:, 1] << 2) | (b[:, 2] << 4) | (b[:, 3] << 6)).contiguous(), steps)
+
+
 def step_outputs(rows, n, dev):
     """Fresh (next_state (rows, N) float32, reward (N,) float32, done (N,) bool), as MLX
     allocates a kernel's outputs per call."""
@@ -246,15 +288,20 @@ def reset_uniform(rows, n, bound, center=None, seed=None, index_offset=0, dev=No
 
 def run_step_many(entry, rows, counter, state, actions, rewards=True, dones=True, sums=False, out=None):
     """Shared body of the `step_many` calls: T steps of one launch of `entry` (an ABI
-    function with the rlenv_*_step_many signature) for actions (T, N)."""
+    function with the rlenv_*_step_many signature) for actions (T, N), or PackedActions
+    (CartPole and Acrobot only)."""
     state = as_state(state, rows)
     n, dev = state.shape[1], state.device
-    if not isinstance(actions, torch.Tensor):
-        actions = torch.as_tensor(np.asarray(actions))
-    if actions.dim() != 2 or actions.shape[1] != n:
-        raise ValueError(f"actions must have shape (T, {n}); got {tuple(actions.shape)}")
-    T = actions.shape[0]
-    actions, dt = as_actions(actions, T * n, dev, "actions")
+    if isinstance(actions, PackedActions):
+        T = actions.steps
+        actions, dt = actions.checked(n, dev), U2
+    else:
+        if not isinstance(actions, torch.Tensor):
+            actions = torch.as_tensor(np.asarray(actions))
+        if actions.dim() != 2 or actions.shape[1] != n:
+            raise ValueError(f"actions must have shape (T, {n}); got {tuple(actions.shape)}")
+        T = actions.shape[0]
+        actions, dt = as_actions(actions, T * n, dev, "actions")
     final = torch.empty_like(state) if out is None else out
     rseq = torch.empty((T, n), dtype=torch.float32, device=dev) if rewards else None
     dseq = torch.empty((T, n), dtype=torch.bool, device=dev) if dones else None

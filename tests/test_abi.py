@@ -52,6 +52,11 @@ def test_arguments_rejected_before_launch(lib):
     assert lib.cartpole_step(fake, fake, 7, 1, 4, 0, fake, fake, fake, None) == -1    # unknown dtype
     assert lib.cartpole_step(None, fake, 0, 1, 4, 0, fake, fake, fake, None) == -1    # null state
     assert lib.cartpole_step(None, None, 0, 1, 0, 0, None, None, None, None) == 0     # empty batch: nothing to do
+    # packed actions (RLENV_U2 = 3) are for the CartPole and Acrobot kernels only
+    assert lib.pendulum_aba_step(8, fake, fake, 3, 1, 4, 0, fake, fake, fake, None) == -1
+    assert lib.pendulum_mm_step(4, 0, fake, fake, 3, 1, 4, 0, fake, fake, fake, None) == -1
+    assert lib.legged_step(2, 8, fake, fake, 3, 1, fake, 0.0, None, 4, 0, fake, fake, fake, None, None) == -1
+    assert lib.acrobot_step(None, None, 3, 1, 0, 0, None, None, None, None) == 0       # accepted there
     assert lib.pendulum_mm_step(17, 0, fake, fake, 0, 1, 4, 0, fake, fake, fake, None) == -2
     assert lib.pendulum_coop_step(3, fake, fake, 0, 1, 4, 0, fake, fake, fake, None) == -2
     assert lib.pendulum_aba_step(193, fake, fake, 0, 1, 4, 0, fake, fake, fake, None) == -2

@@ -136,6 +136,40 @@ def test_cartpole_four_envs_per_thread_path(cuda, dtype):
 
 
 @pytest.mark.parametrize("name", ["cartpole", "acrobot"])
+@pytest.mark.parametrize("n,T", [(1, 1), (5, 3), (1030, 17), (4096, 4), (4099, 8), ((1 << 20) + 4, 6)])
+def test_packed_actions_give_the_same_bits(cuda, name, n, T):
+    """Actions packed along time (RLENV_U2, rlenv_lib.pack_actions: four steps to a byte) step
+    the bodies with the same bits as uint8 actions: single steps and T-step launches with every
+    output, for T a multiple of four and not, at ragged sizes and on CartPole's
+    four-environments-per-thread path (N = 2^20 + 4)."""
+    import rlenv_lib as rl
+
+    mod, _, _, n_act, _ = ENVS[name]
+    m = mod()
+    gen = torch.Generator(device=cuda).manual_seed(n + T)
+    acts = torch.randint(0, n_act, (T, n), device=cuda, generator=gen).to(torch.uint8)
+    packed = rl.pack_actions(acts)
+    assert packed.bits.shape == ((T + 3) // 4, n) and packed.steps == T
+    state0 = m.reset(n)
+    m.reseed(7)
+    want = m.step(state0, acts[0])
+    m.reseed(7)
+    got = m.step(state0, rl.pack_actions(acts[0]))
+    assert all(torch.equal(a, b) for a, b in zip(got, want))
+    m.reseed(70)
+    want = m.step_many(state0, acts, sums=True)
+    m.reseed(70)
+    got = m.step_many(state0, packed, sums=True)
+    assert all(torch.equal(a, b) for a, b in zip(got, want))
+    m.reseed(70)
+    fin, _, _ = m.step_many(state0, packed, rewards=False, dones=False)
+    assert torch.equal(fin, want[0])
+    if T > 1:
+        with pytest.raises(ValueError):
+            m.step(state0, packed)  # the packed actions of more than one step
+
+
+@pytest.mark.parametrize("name", ["cartpole", "acrobot"])
 @pytest.mark.parametrize("dtype", [torch.uint8, torch.int64])
 def test_step_many_equals_chained_steps(cuda, name, dtype):
     """T steps in one launch are bit-identical to T single-step launches with the same seeds."""
