@@ -621,7 +621,7 @@ def run_ours(args):
     packed_bits = rl.pack_actions(actions).bits
     outs = [(torch.empty((4, n), pin_memory=True), torch.empty(n, pin_memory=True), torch.empty(n, pin_memory=True))
             for _ in range(2)]
-    copy_s, comp_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    copy_s, comp_s, back_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     keep = [None, None]
 
     def e2e_time(host_actions, packed):
@@ -630,6 +630,8 @@ def run_ours(args):
         as_input = (lambda bits: rl.PackedActions(bits, T)) if packed else (lambda a: a)
 
         def e2e_run(steps):
+            # three streams: inputs in (copy_s), the T steps (comp_s), results out (back_s), so that
+            # neither copy waits for the other direction or delays the next launch
             h2d_done = [torch.cuda.Event() for _ in range(2)]
             comp_done = [torch.cuda.Event() for _ in range(2)]
             for k in range(steps + 1):
@@ -637,7 +639,7 @@ def run_ours(args):
                 if k < steps:
                     with torch.cuda.stream(copy_s):
                         if k >= 2:
-                            copy_s.wait_event(comp_done[b])  # buffer b is free once step k-2 finished
+                            copy_s.wait_event(comp_done[b])  # input buffer b is free once step k-2 ran
                         dev_in[b][0].copy_(pin_state, non_blocking=True)
                         dev_in[b][1].copy_(pin_actions, non_blocking=True)
                         h2d_done[b].record(copy_s)
@@ -645,14 +647,17 @@ def run_ours(args):
                     pb = (k - 1) % 2
                     with torch.cuda.stream(comp_s):
                         comp_s.wait_event(h2d_done[pb])
-                        fin, _, _, rsum, dcnt = acrobot_metal.step_many(dev_in[pb][0], as_input(dev_in[pb][1]),
-                                                                        rewards=False, dones=False, sums=True)
-                        for t_out, t_dev in zip(outs[pb], (fin, rsum, dcnt)):
-                            t_out.copy_(t_dev, non_blocking=True)
+                        res = acrobot_metal.step_many(dev_in[pb][0], as_input(dev_in[pb][1]), rewards=False,
+                                                      dones=False, sums=True)
                         comp_done[pb].record(comp_s)
-                        keep[pb] = (fin, rsum, dcnt)
+                    with torch.cuda.stream(back_s):
+                        back_s.wait_event(comp_done[pb])
+                        for t_out, t_dev in zip(outs[pb], (res[0], res[3], res[4])):
+                            t_dev.record_stream(back_s)
+                            t_out.copy_(t_dev, non_blocking=True)
+                        keep[pb] = res
 
-        e2e_run(max(2, args.warmup // 2))
+        e2e_run(max(4, args.warmup))
         torch.cuda.synchronize()
         barrier()
         steps = max(20, args.steps // 10)
@@ -660,8 +665,9 @@ def run_ours(args):
         s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s2.record(copy_s)
         e2e_run(steps)
-        comp_s.wait_stream(copy_s)
-        e2.record(comp_s)
+        back_s.wait_stream(copy_s)
+        back_s.wait_stream(comp_s)
+        e2.record(back_s)
         torch.cuda.synchronize()
         barrier()
         t2 = torch.tensor([s2.elapsed_time(e2) / 1e3], device=dev)
@@ -717,7 +723,7 @@ def run_ours(args):
                 "d2h_bytes_per_step": 4 * 4 * n + 8 * n, "api": "acrobot_metal.step_many(state, PackedActions)",
                 "actions": "packed along time, four steps to a byte (rlenv_lib.pack_actions), streamed from pinned "
                            "host memory",
-                "steps": e2e_steps, "pipelined": "copy stream and compute stream, two steps in flight", "host": numa,
+                "steps": e2e_steps, "pipelined": "input, compute and output streams, two steps in flight", "host": numa,
                 "uint8_actions": {"value": e2e_u8_value, "h2d_bytes_per_step": 4 * 4 * n + e2e_u8_action_bytes,
                                   "api": "acrobot_metal.step_many"}},
         "gpu_launches": args.steps,
