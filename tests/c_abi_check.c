@@ -21,6 +21,9 @@ int main(void) {
   expect(strcmp(rlenv_strerror(RLENV_OK), "ok"), 0, "strerror(ok)");
   expect(rlenv_cartpole_step(fake, fake, 7, 1, 4, 0, fake, fake, fake, NULL), RLENV_EINVAL, "unknown dtype");
   expect(rlenv_cartpole_step(NULL, NULL, RLENV_I32, 1, 0, 0, NULL, NULL, NULL, NULL), RLENV_OK, "empty batch");
+  expect(rlenv_acrobot_step(NULL, NULL, RLENV_U2, 1, 0, 0, NULL, NULL, NULL, NULL), RLENV_OK, "packed, empty batch");
+  expect(rlenv_pendulum_aba_step(8, fake, fake, RLENV_U2, 1, 4, 0, fake, fake, fake, NULL), RLENV_EINVAL,
+         "packed actions outside the classic bodies");
   expect(rlenv_acrobot_step_many(fake, fake, RLENV_U8, 1, -1, 4, 0, fake, NULL, NULL, NULL, NULL, NULL),
          RLENV_EINVAL, "negative steps");
   expect(rlenv_pendulum_aba_step(193, fake, fake, RLENV_I32, 1, 4, 0, fake, fake, fake, NULL), RLENV_EUNSUPPORTED,
