@@ -61,6 +61,7 @@ WORKLOADS = {
     "pendulum_aba": ("BASELINE configs[2]: K-link pendulum, articulated body", 65_536, 100),
     "pendulum_mm": ("BASELINE configs[2]: K-link pendulum, mass matrix", 65_536, 100),
     "pendulum_coop": ("BASELINE configs[2]: K-link pendulum, K lanes per env", 65_536, 100),
+    "pendulum_aba_coop": ("BASELINE configs[2]: K-link pendulum, articulated body, one warp per env", 65_536, 100),
     "legged_step": ("BASELINE configs[3]: legged body with C contacts", N_ENVS, 50),
     "es_cartpole": ("BASELINE configs[4]: ES generation, CartPole P=4096 H=32 horizon 500", 4096, 500),
     "es_acrobot": ("BASELINE configs[4]: ES generation, Acrobot P=4096 H=32 horizon 500", 4096, 500),
@@ -193,8 +194,8 @@ def cpu_workload_baseline(workload, args, n, budget_s=10.0):
         make = lambda m: (rng.uniform(-bound, bound, (4, m)).astype(np.float32), lambda t: rng.integers(0, n_act, m))
         return _steps_baseline(lambda s, a, t: fn(s, a, 1 + t)[0], make, min(n, 131_072), budget_s,
                                "cartpole_np.step" if cp else "acrobot_np.step")
-    if workload in ("pendulum_aba", "pendulum_mm", "pendulum_coop"):
-        k, form = args.k, ("aba" if workload == "pendulum_aba" else "mass_matrix")
+    if workload in ("pendulum_aba", "pendulum_aba_coop", "pendulum_mm", "pendulum_coop"):
+        k, form = args.k, ("aba" if workload.startswith("pendulum_aba") else "mass_matrix")
         make = lambda m: (np.concatenate([rng.uniform(-0.1, 0.1, (k, m)), np.zeros((k, m))]).astype(np.float32),
                           lambda t: rng.integers(0, 3, m))
         return _steps_baseline(lambda s, a, t: kernels.pendulum_step(s, a, 1 + t, k, form=form)[0], make,
@@ -846,7 +847,7 @@ def run_workload(args):
         extra = {"action_dtype": "int32", "bytes_per_env_step": rlenv_flops.step_bytes(4, 4),
                  "l2": "state, actions and outputs (688 MB per step at N = 2^24) exceed L2"}
         hbm_bound = True
-    elif args.workload in ("pendulum_aba", "pendulum_mm", "pendulum_coop", "legged_step"):
+    elif args.workload in ("pendulum_aba", "pendulum_aba_coop", "pendulum_mm", "pendulum_coop", "legged_step"):
         if args.workload == "legged_step":
             c = args.c
             rows, n_act = 2 * (3 + c), 3 ** c
@@ -870,16 +871,18 @@ def run_workload(args):
             rows, n_act = 2 * k, 3
             state_a = rl.reset_uniform(rows, n, 0.1, seed=3, index_offset=rank * n, dev=dev)
             fn_name = {"pendulum_aba": "pendulum_aba_step_many", "pendulum_mm": "pendulum_mm_step_many",
-                       "pendulum_coop": "pendulum_coop_step_many"}[args.workload]
+                       "pendulum_coop": "pendulum_coop_step_many",
+                       "pendulum_aba_coop": "pendulum_aba_coop_step_many"}[args.workload]
             head = (k, 0) if args.workload == "pendulum_mm" else (k,)
             abi = getattr(lib, fn_name)
 
             def launch_many(src, dst, r, d):
                 rl.check(abi(*head, src.data_ptr(), actions.data_ptr(), rl.U8, 1, T, n, rank * n, dst.data_ptr(),
                              r.data_ptr(), d.data_ptr(), sp))
-            fl = (rlenv_flops.aba_flops(k) if args.workload == "pendulum_aba" else rlenv_flops.mass_matrix_flops(k))["flops"]
+            aba = args.workload.startswith("pendulum_aba")
+            fl = (rlenv_flops.aba_flops(k) if aba else rlenv_flops.mass_matrix_flops(k))["flops"]
             extra = {"links": k}
-            if args.workload == "pendulum_aba":
+            if aba:
                 # the roofline counts the reference's 4 x 140 K + 12 K (bench_aba.py:53-55); this
                 # build's rank-one form does fewer
                 extra["flops_per_env_step_this_algorithm"] = rlenv_flops.aba_rank_one_flops(k)["flops"]
@@ -974,7 +977,9 @@ def run_workload(args):
         hbm = {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
                "bytes_per_launch": bytes_launch / T, "peak_kind": "measured (MEASURED_PEAKS.json)"}
         roof = {**hbm, "fp32": fp32} if hbm_bound else {**fp32, "hbm": hbm}
-        key = (args.workload, n) + ((args.k,) if args.workload.startswith("pendulum") else ()) + \
+        # the one-warp articulated body computes the reference's articulated-body configuration
+        key = ("pendulum_aba" if args.workload == "pendulum_aba_coop" else args.workload, n) + \
+            ((args.k,) if args.workload.startswith("pendulum") else ()) + \
             ((args.c, args.iters) if args.workload == "legged_step" else ())
         pub, pub_src = published(*key)
         if extra.get("impulses"):

@@ -166,6 +166,17 @@ RLENV_API int rlenv_pendulum_aba_step_many(int k, const float* state, const void
                                  float* state_out, float* reward_seq, uint8_t* done_seq,
                                  void* stream);
 
+/* The articulated body with one warp per environment (no counterpart in the reference, whose
+ * only cooperative pendulum is the mass-matrix form): the recurrences along the chain (link
+ * velocities, articulated masses, bias forces, accelerations) run as scans over the warp's
+ * lanes, so a batch too small to fill the GPU with one thread per environment steps in a few
+ * levels of shuffles instead of K dependent link steps. Same arguments and results as
+ * rlenv_pendulum_aba_step_many, to float rounding (the sums are associated differently);
+ * chained calls and one T-step call agree bit for bit. k in 1..192. */
+RLENV_API int rlenv_pendulum_aba_coop_step_many(int k, const float* state, const void* actions, int action_dtype,
+                                      uint32_t seed0, int64_t steps, int64_t n, int64_t index_offset,
+                                      float* state_out, float* reward_seq, uint8_t* done_seq, void* stream);
+
 /* ---- Hopper and legged bodies ---------------------------------------------
  * Legged body with c legs and c hard contacts (legged_metal.py:13-185):
  * state (2(3+c), n) = q then q_dot with q = (x, y, phi, psi_1..psi_c); action in

@@ -1,6 +1,6 @@
 // C ABI entry points of the K-link pendulum step kernels; the kernels
 // themselves are instantiated in pendulum_mm_lo.cu, pendulum_mm_hi.cu,
-// pendulum_aba.cu and pendulum_coop.cu. Every kernel steps T times per launch;
+// pendulum_aba.cu, pendulum_long.cu, pendulum_aba_coop.cu and pendulum_coop.cu. Every kernel steps T times per launch;
 // the single-step entry points launch it with T = 1.
 #include "pendulum_kernels.cuh"
 
@@ -23,6 +23,13 @@ int launch(StepFn fn, int64_t threads, int block, const float* state, const void
                                                                off, next, reward_seq, done_seq);
   return launch_status();
 }
+
+// Above 64 links the articulated body runs one warp per environment whatever the batch: measured on
+// a B200 (T = 100), the one-warp form steps 1.5-1.7x as many environments per second as the
+// one-thread long-chain kernel at N = 65,536 and 4.8-5.7x at N = 256 (K = 128, 192), while up to
+// K = 64 the one-thread kernels win once the batch fills the GPU. The choice depends on K alone,
+// so a shard of a batch runs the same kernel as the whole batch.
+constexpr int kLongAbaMaxDefault = 64;
 
 StepFn pick_mm(int k, int pairwise_trig) {
   return k <= 8 ? pick_mm_lo(k, pairwise_trig != 0) : pick_mm_hi(k, pairwise_trig != 0);
@@ -88,6 +95,11 @@ int rlenv_pendulum_aba_step(int k, const float* state, const void* action, int a
   using namespace rlenv::pend;
   if (n > 0 && (!reward || !done)) return RLENV_EINVAL;
   if (int rc = check_args(state, action, action_dtype, 1, n, next_state)) return rc;
+  if (k > kLongAbaMaxDefault && k <= kCoopAbaMaxLinks) {
+    if (n == 0) return RLENV_OK;
+    return launch_aba_coop(k, state, action, action_dtype, seed, 1, n, index_offset, next_state, reward, done,
+                           stream);
+  }
   if (k > rlenv::kUnrollLinks)
     return launch_aba_long(k, state, action, action_dtype, seed, 1, n, index_offset, next_state,
                            reward, done, stream);
@@ -103,6 +115,11 @@ int rlenv_pendulum_aba_step_many(int k, const float* state, const void* actions,
                                  void* stream) {
   using namespace rlenv::pend;
   if (int rc = check_args(state, actions, action_dtype, steps, n, state_out)) return rc;
+  if (k > kLongAbaMaxDefault && k <= kCoopAbaMaxLinks) {
+    if (n == 0) return RLENV_OK;
+    return launch_aba_coop(k, state, actions, action_dtype, seed0, steps, n, index_offset, state_out, reward_seq,
+                           done_seq, stream);
+  }
   if (k > rlenv::kUnrollLinks)
     return launch_aba_long(k, state, actions, action_dtype, seed0, steps, n, index_offset, state_out,
                            reward_seq, done_seq, stream);
@@ -110,6 +127,17 @@ int rlenv_pendulum_aba_step_many(int k, const float* state, const void* actions,
   if (!fn) return RLENV_EUNSUPPORTED;
   return launch(fn, n, 128, state, actions, action_dtype, seed0, steps, n, index_offset, state_out,
                 reward_seq, done_seq, stream);
+}
+
+int rlenv_pendulum_aba_coop_step_many(int k, const float* state, const void* actions, int action_dtype,
+                                      uint32_t seed0, int64_t steps, int64_t n, int64_t index_offset,
+                                      float* state_out, float* reward_seq, uint8_t* done_seq, void* stream) {
+  using namespace rlenv::pend;
+  if (int rc = check_args(state, actions, action_dtype, steps, n, state_out)) return rc;
+  if (k < 1 || k > kCoopAbaMaxLinks) return RLENV_EUNSUPPORTED;
+  if (n == 0) return RLENV_OK;
+  return launch_aba_coop(k, state, actions, action_dtype, seed0, steps, n, index_offset, state_out, reward_seq,
+                         done_seq, stream);
 }
 
 }  // extern "C"

@@ -1,0 +1,354 @@
+// The articulated-body pendulum with one warp per environment: the warp-cooperative form for
+// batches too small to fill the GPU with one thread per environment (BASELINE's N = 256
+// configurations). Lane l owns links l L .. l L + L - 1 (L = 1, 2, 4 or 6 for K up to 32, 64,
+// 128, 192). The algorithm is the rank-one articulated body of pendulum.cuh (aba_accel_unrolled;
+// pendulum_aba_np.py:30-99), with every recurrence along the chain written as a scan over the
+// lanes, so a derivative evaluation takes a few levels of shuffles instead of K dependent steps:
+//  - link velocities: in the world frame the velocity of link i's joint is the exclusive prefix
+//    sum of om_j (-sin th_j, cos th_j) over j < i, rotated into link i's frame;
+//  - the articulated mass m_i the subtree at link i hands its parent obeys
+//    m_i = (1 + m_{i+1}) / (1 + s_{i+1}^2 m_{i+1}) (s the joint sine; m = 1 at the last link):
+//    a linear fractional map, so m_i is the ratio of a suffix product of 2 x 2 matrices
+//    [[1, 1], [s^2, 1]] applied to (1, 1);
+//  - the bias the subtree hands its parent obeys pa1_i = alpha_i + beta_i pa1_{i+1}, with
+//    beta_i = c_{i+1} / (1 + m_{i+1} s_{i+1}^2): a suffix scan of affine maps;
+//  - the outward accelerations keep two numbers per link, ax and z = ay + aw, and
+//    (ax, z) -> (c ax + s z + c1, g - U1 (c ax + s z + c1)) is affine: a prefix scan of 2 x 2
+//    affine maps; each link's absolute angular acceleration is z - ay.
+// The scan form equals the sequential recurrences in exact arithmetic (checked in float64
+// against the oracle's articulated body to 1e-13 for K = 1..64); in float32 the sums are
+// associated differently, so it agrees with the one-thread kernels to rounding, not bit for bit.
+#include "pendulum_kernels.cuh"
+
+namespace rlenv {
+namespace pend {
+namespace {
+
+constexpr unsigned kWarp = 0xffffffffu;
+
+// v -> M v + b on (ax, z)
+struct Aff2 {
+  float m00, m01, m10, m11, b0, b1;
+};
+
+RLENV_D Aff2 aff2_identity() { return Aff2{1.0f, 0.0f, 0.0f, 1.0f, 0.0f, 0.0f}; }
+
+// f then g (f applied first)
+RLENV_D Aff2 aff2_then(const Aff2& f, const Aff2& g) {
+  return Aff2{fmaf(g.m00, f.m00, g.m01 * f.m10), fmaf(g.m00, f.m01, g.m01 * f.m11),
+              fmaf(g.m10, f.m00, g.m11 * f.m10), fmaf(g.m10, f.m01, g.m11 * f.m11),
+              fmaf(g.m00, f.b0, fmaf(g.m01, f.b1, g.b0)), fmaf(g.m10, f.b0, fmaf(g.m11, f.b1, g.b1))};
+}
+
+RLENV_D Aff2 aff2_shfl_up(const Aff2& a, int d) {
+  return Aff2{__shfl_up_sync(kWarp, a.m00, d), __shfl_up_sync(kWarp, a.m01, d), __shfl_up_sync(kWarp, a.m10, d),
+              __shfl_up_sync(kWarp, a.m11, d), __shfl_up_sync(kWarp, a.b0, d), __shfl_up_sync(kWarp, a.b1, d)};
+}
+
+// a 2 x 2 matrix with non-negative entries, kept near unit size (its action on a ratio does not
+// depend on the scale, and a product of K factors would otherwise overflow)
+struct Mat2 {
+  float a, b, c, d;
+};
+
+RLENV_D Mat2 mat2_identity() { return Mat2{1.0f, 0.0f, 0.0f, 1.0f}; }
+
+RLENV_D Mat2 mat2_mul(const Mat2& p, const Mat2& q) {
+  const Mat2 r{fmaf(p.a, q.a, p.b * q.c), fmaf(p.a, q.b, p.b * q.d), fmaf(p.c, q.a, p.d * q.c),
+               fmaf(p.c, q.b, p.d * q.d)};
+  const float sc = __frcp_rn(r.a + r.b + r.c + r.d);
+  return Mat2{r.a * sc, r.b * sc, r.c * sc, r.d * sc};
+}
+
+RLENV_D Mat2 mat2_shfl_down(const Mat2& p, int d) {
+  return Mat2{__shfl_down_sync(kWarp, p.a, d), __shfl_down_sync(kWarp, p.b, d), __shfl_down_sync(kWarp, p.c, d),
+              __shfl_down_sync(kWarp, p.d, d)};
+}
+
+// the ratio a subtree's product hands on: P applied to (1, 1)
+RLENV_D float mat2_ratio(const Mat2& p) { return (p.a + p.b) / (p.c + p.d); }
+
+// Absolute angular accelerations of this lane's links j = lane L + t (t < L) of a k-link chain;
+// links past the chain are padding and read as zero angles and rates.
+template <int L>
+RLENV_D void coop_aba_accel(const float (&th)[L], const float (&om)[L], float torque, int k, int lane,
+                            float (&acc)[L]) {
+  const int j0 = lane * L;
+  // joint (relative) trig and rates, absolute trig; the previous link of the lane's first link is
+  // the last link of the lane before
+  const float th_prev = __shfl_up_sync(kWarp, th[L - 1], 1);
+  const float om_prev = __shfl_up_sync(kWarp, om[L - 1], 1);
+  float sn[L], cs[L], sa[L], ca[L], qd[L];
+#pragma unroll
+  for (int t = 0; t < L; ++t) {
+    const int j = j0 + t;
+    const float tp = t == 0 ? (lane == 0 ? 0.0f : th_prev) : th[t - 1];
+    const float op = t == 0 ? (lane == 0 ? 0.0f : om_prev) : om[t - 1];
+    sincos_sfu_near(th[t] - tp, &sn[t], &cs[t]);
+    sincos_sfu_near(th[t], &sa[t], &ca[t]);
+    qd[t] = om[t] - op;
+    if (j >= k) {  // padding: no joint
+      sn[t] = 0.0f;
+      cs[t] = 0.0f;
+    }
+  }
+  // ---- velocities: exclusive prefix sum of om_j (-sin th_j, cos th_j) in the world frame
+  float vx[L], vy[L];
+  {
+    float s0 = 0.0f, s1 = 0.0f;  // this lane's links' sum
+#pragma unroll
+    for (int t = 0; t < L; ++t) {
+      s0 = fmaf(-om[t], sa[t], s0);
+      s1 = fmaf(om[t], ca[t], s1);
+    }
+    float i0 = s0, i1 = s1;  // inclusive over lanes
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const float u0 = __shfl_up_sync(kWarp, i0, d), u1 = __shfl_up_sync(kWarp, i1, d);
+      if (lane >= d) {
+        i0 += u0;
+        i1 += u1;
+      }
+    }
+    float e0 = i0 - s0, e1 = i1 - s1;  // exclusive: the links before this lane
+#pragma unroll
+    for (int t = 0; t < L; ++t) {
+      vx[t] = fmaf(ca[t], e0, sa[t] * e1);
+      vy[t] = fmaf(-sa[t], e0, ca[t] * e1);
+      e0 = fmaf(-om[t], sa[t], e0);
+      e1 = fmaf(om[t], ca[t], e1);
+    }
+  }
+  // ---- articulated masses: m_j = ratio of M_{j+1} ... M_{k-1}, M_j = [[1, 1], [s_j^2, 1]] for
+  // 1 <= j < k and the identity elsewhere
+  float m[L];
+  {
+    Mat2 own = mat2_identity();
+#pragma unroll
+    for (int t = 0; t < L; ++t) {
+      const int j = j0 + t;
+      if (j >= 1 && j < k) own = mat2_mul(own, Mat2{1.0f, 1.0f, sn[t] * sn[t], 1.0f});
+    }
+    Mat2 sfx = own;  // inclusive suffix over lanes: this lane's links and every later one
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const Mat2 later = mat2_shfl_down(sfx, d);
+      if (lane + d < 32) sfx = mat2_mul(sfx, later);
+    }
+    Mat2 after = mat2_shfl_down(sfx, 1);  // the links after this lane
+    if (lane == 31) after = mat2_identity();
+#pragma unroll
+    for (int t = L - 1; t >= 0; --t) {
+      const int j = j0 + t;
+      m[t] = mat2_ratio(after);
+      if (j >= 1 && j < k) after = mat2_mul(Mat2{1.0f, 1.0f, sn[t] * sn[t], 1.0f}, after);
+    }
+  }
+  // the next link's joint trig and mass (zero joint trig past the chain: no child)
+  float sn1[L], cs1[L], m1[L];
+  {
+    const float sn_next = __shfl_down_sync(kWarp, sn[0], 1), cs_next = __shfl_down_sync(kWarp, cs[0], 1);
+    const float m_next = __shfl_down_sync(kWarp, m[0], 1);
+#pragma unroll
+    for (int t = 0; t < L; ++t) {
+      const bool last = t == L - 1;
+      sn1[t] = last ? (lane == 31 ? 0.0f : sn_next) : sn[t + 1];
+      cs1[t] = last ? (lane == 31 ? 0.0f : cs_next) : cs[t + 1];
+      m1[t] = last ? (lane == 31 ? 0.0f : m_next) : m[t + 1];
+    }
+  }
+  // ---- per link: the articulated inertia seen from its joint and the velocity-product terms
+  float r[L], u1[L], c1[L], c2[L], alpha[L], beta[L];
+  float root_a00 = 1.0f, root_a01 = 0.0f;  // link 0's, for the root
+#pragma unroll
+  for (int t = 0; t < L; ++t) {
+    const float a00 = fmaf(m1[t] * sn1[t], sn1[t], 1.0f);
+    const float a01 = (m1[t] * sn1[t]) * cs1[t];
+    if (t == 0) {
+      root_a00 = a00;
+      root_a01 = a01;
+    }
+    r[t] = 1.0f / a00;
+    u1[t] = a01 * r[t];
+    const float w = om[t], x = vx[t], y = vy[t];
+    c1[t] = qd[t] * y;
+    c2[t] = -qd[t] * x;
+    alpha[t] = fmaf(-w, w + y, fmaf(m[t], c1[t], -u1[t] * (x * w)));
+    beta[t] = cs1[t] * r[t];
+  }
+  // ---- bias: pa1_j = alpha_j + beta_j pa1_{j+1} for 1 <= j < k, pa1 past the chain zero; a
+  // lane's links compose to pa1_first = A + B pa1_after
+  float pa1_next[L];  // pa1_{j+1}
+  {
+    float B = 1.0f, A = 0.0f;
+#pragma unroll
+    for (int t = L - 1; t >= 0; --t) {
+      const int j = j0 + t;
+      if (j >= 1 && j < k) {
+        A = fmaf(beta[t], A, alpha[t]);
+        B = beta[t] * B;
+      }
+    }
+    float SB = B, SA = A;  // inclusive suffix over lanes
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const float lb = __shfl_down_sync(kWarp, SB, d), la = __shfl_down_sync(kWarp, SA, d);
+      if (lane + d < 32) {
+        SA = fmaf(SB, la, SA);
+        SB = SB * lb;
+      }
+    }
+    float pa = __shfl_down_sync(kWarp, SA, 1);  // pa1 of the next lane's first link
+    if (lane == 31) pa = 0.0f;
+#pragma unroll
+    for (int t = L - 1; t >= 0; --t) {
+      const int j = j0 + t;
+      pa1_next[t] = pa;
+      if (j >= 1 && j < k) pa = fmaf(beta[t], pa, alpha[t]);
+    }
+  }
+  float g[L];
+#pragma unroll
+  for (int t = 0; t < L; ++t) g[t] = -fmaf(vx[t], om[t], sn1[t] * pa1_next[t]) * r[t];
+  // ---- the root (lane 0's first link), the base accelerating at -G
+  float ax0 = 0.0f, z0 = 0.0f, qdd0 = 0.0f;
+  if (lane == 0) {
+    const float U0 = root_a00, U1_0 = root_a01;
+    const float uu0 = torque - sn1[0] * pa1_next[0];
+    const float ax = ca[0] * -pd::G;
+    const float ay = -sa[0] * -pd::G;
+    qdd0 = (uu0 - fmaf(U1_0, ax, U0 * ay)) / U0;
+    ax0 = ax;
+    z0 = ay + qdd0;
+  }
+  ax0 = __shfl_sync(kWarp, ax0, 0);
+  z0 = __shfl_sync(kWarp, z0, 0);
+  qdd0 = __shfl_sync(kWarp, qdd0, 0);
+  // ---- outward accelerations: (ax, z) through each link's affine map, prefix over the lanes
+  {
+    Aff2 own = aff2_identity();
+#pragma unroll
+    for (int t = 0; t < L; ++t) {
+      const int j = j0 + t;
+      if (j >= 1 && j < k) {
+        const Aff2 f{cs[t], sn[t], -u1[t] * cs[t], -u1[t] * sn[t], c1[t], fmaf(-u1[t], c1[t], g[t])};
+        own = aff2_then(own, f);
+      }
+    }
+    Aff2 pre = own;  // inclusive prefix over lanes
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const Aff2 earlier = aff2_shfl_up(pre, d);
+      if (lane >= d) pre = aff2_then(earlier, pre);
+    }
+    Aff2 before = aff2_shfl_up(pre, 1);  // the links before this lane
+    if (lane == 0) before = aff2_identity();
+    float ax = fmaf(before.m00, ax0, fmaf(before.m01, z0, before.b0));
+    float z = fmaf(before.m10, ax0, fmaf(before.m11, z0, before.b1));
+#pragma unroll
+    for (int t = 0; t < L; ++t) {
+      const int j = j0 + t;
+      if (j == 0) {
+        acc[t] = qdd0;
+      } else if (j >= k) {
+        acc[t] = 0.0f;  // padding stays at rest
+      } else {
+        const float ap1 = fmaf(cs[t], ax, fmaf(sn[t], z, c1[t]));
+        const float ay = fmaf(-sn[t], ax, fmaf(cs[t], z, c2[t]));
+        z = fmaf(-u1[t], ap1, g[t]);
+        ax = ap1;
+        acc[t] = z - ay;
+      }
+    }
+  }
+}
+
+// T steps of N environments, one warp per environment (four per block), the lane's links' state
+// in registers between steps; step t reads actions[t * n + e], draws its resets from seed0 + t
+// and writes reward_seq / done_seq row t when those are not null. One step is the launch with
+// T = 1, so a chain of single steps and one T-step launch agree bit for bit.
+template <int L>
+__global__ void __launch_bounds__(128)
+pendulum_aba_coop_kernel(const float* __restrict__ state, const void* __restrict__ actions, int dtype,
+                         uint32_t seed0, int k, int64_t T, int64_t n, int64_t off, float* __restrict__ next,
+                         float* __restrict__ reward_seq, uint8_t* __restrict__ done_seq) {
+  const int lane = int(threadIdx.x) & 31;
+  const int64_t e_raw = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (e_raw >= n) return;  // whole warps: the environment is per warp
+  const int64_t e = e_raw;
+  float th[L], om[L];
+#pragma unroll
+  for (int t = 0; t < L; ++t) {
+    const int j = lane * L + t;
+    th[t] = j < k ? __ldg(state + int64_t(j) * n + e) : 0.0f;
+    om[t] = j < k ? __ldg(state + int64_t(k + j) * n + e) : 0.0f;
+  }
+  int act = T > 0 ? action_at(actions, dtype, e) : 0;  // loaded one step ahead
+  for (int64_t t = 0; t < T; ++t) {
+    check_flag(act < 0 || act > 2, kCheckActionRange);
+    const float torque = float(act - 1) * pd::TORQUE;
+    if (t + 1 < T) act = action_at(actions, dtype, (t + 1) * n + e);
+    pendulum_rk4<L, true>(th, om, torque, [&](const float (&a_t)[L], const float (&a_o)[L], float tq, float (&a)[L]) {
+      coop_aba_accel<L>(a_t, a_o, tq, k, lane, a);
+    });
+    // the tip above half the chain's length: -sum cos th > k / 2, summed over the warp
+    float h = 0.0f;
+#pragma unroll
+    for (int u = 0; u < L; ++u)
+      if (lane * L + u < k) h += cos_fast(th[u]);
+#pragma unroll
+    for (int d = 16; d >= 1; d >>= 1) h += __shfl_xor_sync(kWarp, h, d);
+    const bool dn = -h > float(k) * 0.5f;
+    if (dn) {
+      const uint32_t hs = env_hash(seed0 + uint32_t(t), off + e);
+#pragma unroll
+      for (int u = 0; u < L; ++u) {
+        const int j = lane * L + u;
+        if (j < k) {
+          th[u] = uniform_pm(pcg_hash(hs + uint32_t(j) * kRowStride), pd::RESET_BOUND);
+          om[u] = uniform_pm(pcg_hash(hs + uint32_t(k + j) * kRowStride), pd::RESET_BOUND);
+        }
+      }
+    }
+    if (lane == 0) {
+      if (reward_seq) reward_seq[t * n + e] = dn ? 0.0f : -1.0f;
+      if (done_seq) done_seq[t * n + e] = dn;
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < L; ++u) {
+    const int j = lane * L + u;
+    if (j < k) {
+      check_flag(!(isfinite(th[u]) && isfinite(om[u])), kCheckNonFinite);
+      next[int64_t(j) * n + e] = th[u];
+      next[int64_t(k + j) * n + e] = om[u];
+    }
+  }
+}
+
+}  // namespace
+
+int launch_aba_coop(int k, const float* state, const void* actions, int dtype, uint32_t seed0, int64_t T,
+                    int64_t n, int64_t off, float* next, float* reward_seq, uint8_t* done_seq, void* stream) {
+  if (k < 1 || k > kCoopAbaMaxLinks) return RLENV_EUNSUPPORTED;
+  const int64_t threads = n * 32;
+  const unsigned blocks = unsigned((threads + 127) / 128);
+  cudaStream_t s = as_stream(stream);
+  if (k <= 32) {
+    pendulum_aba_coop_kernel<1><<<blocks, 128, 0, s>>>(state, actions, dtype, seed0, k, T, n, off, next, reward_seq,
+                                                       done_seq);
+  } else if (k <= 64) {
+    pendulum_aba_coop_kernel<2><<<blocks, 128, 0, s>>>(state, actions, dtype, seed0, k, T, n, off, next, reward_seq,
+                                                       done_seq);
+  } else if (k <= 128) {
+    pendulum_aba_coop_kernel<4><<<blocks, 128, 0, s>>>(state, actions, dtype, seed0, k, T, n, off, next, reward_seq,
+                                                       done_seq);
+  } else {
+    pendulum_aba_coop_kernel<6><<<blocks, 128, 0, s>>>(state, actions, dtype, seed0, k, T, n, off, next, reward_seq,
+                                                       done_seq);
+  }
+  return launch_status();
+}
+
+}  // namespace pend
+}  // namespace rlenv

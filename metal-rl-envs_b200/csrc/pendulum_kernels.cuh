@@ -196,6 +196,11 @@ int launch_aba_long(int k, const float* state, const void* actions, int dtype, u
                     int64_t T, int64_t n, int64_t off, float* next, float* reward_seq,
                     uint8_t* done_seq, void* stream);
 StepFn pick_coop(int k);                    // k in 2, 4, 8, 16, 32
+// The articulated body with one warp per environment, its recurrences along the chain as scans
+// over the lanes, for 1 <= k <= kCoopAbaMaxLinks (pendulum_aba_coop.cu).
+constexpr int kCoopAbaMaxLinks = 192;
+int launch_aba_coop(int k, const float* state, const void* actions, int dtype, uint32_t seed0, int64_t T,
+                    int64_t n, int64_t off, float* next, float* reward_seq, uint8_t* done_seq, void* stream);
 
 }  // namespace pend
 }  // namespace rlenv

@@ -60,6 +60,8 @@ _SIGNATURES = {
                                       c_void_p, c_void_p, c_void_p, c_void_p],
     "rlenv_pendulum_aba_step_many": [c_int, c_void_p, c_void_p, c_int, c_uint32, c_int64, c_int64, c_int64,
                                      c_void_p, c_void_p, c_void_p, c_void_p],
+    "rlenv_pendulum_aba_coop_step_many": [c_int, c_void_p, c_void_p, c_int, c_uint32, c_int64, c_int64, c_int64,
+                                          c_void_p, c_void_p, c_void_p, c_void_p],
     "rlenv_legged_step_many": [c_int, c_int, c_void_p, c_void_p, c_int, c_uint32, c_void_p, c_float, c_void_p,
                                c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
     "rlenv_hopper_step_many": [c_int, c_void_p, c_void_p, c_int, c_uint32, c_void_p, c_int64, c_int64, c_int64,
