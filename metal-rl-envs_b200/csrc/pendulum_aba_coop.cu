@@ -26,6 +26,15 @@ namespace {
 
 constexpr unsigned kWarp = 0xffffffffu;
 
+// The hardware reciprocal (rcp.approx.ftz, within one ulp): every denominator here is at least
+// one (1 + m s^2, and the sums of a product's non-negative entries after rescaling), where the
+// correctly rounded reciprocal and division carry slow-path branches that a lone warp waits on.
+RLENV_D float rcp_fast(float a) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
+  return r;
+}
+
 // v -> M v + b on (ax, z)
 struct Aff2 {
   float m00, m01, m10, m11, b0, b1;
@@ -56,7 +65,7 @@ RLENV_D Mat2 mat2_identity() { return Mat2{1.0f, 0.0f, 0.0f, 1.0f}; }
 RLENV_D Mat2 mat2_mul(const Mat2& p, const Mat2& q) {
   const Mat2 r{fmaf(p.a, q.a, p.b * q.c), fmaf(p.a, q.b, p.b * q.d), fmaf(p.c, q.a, p.d * q.c),
                fmaf(p.c, q.b, p.d * q.d)};
-  const float sc = __frcp_rn(r.a + r.b + r.c + r.d);
+  const float sc = rcp_fast(r.a + r.b + r.c + r.d);
   return Mat2{r.a * sc, r.b * sc, r.c * sc, r.d * sc};
 }
 
@@ -66,7 +75,7 @@ RLENV_D Mat2 mat2_shfl_down(const Mat2& p, int d) {
 }
 
 // the ratio a subtree's product hands on: P applied to (1, 1)
-RLENV_D float mat2_ratio(const Mat2& p) { return (p.a + p.b) / (p.c + p.d); }
+RLENV_D float mat2_ratio(const Mat2& p) { return (p.a + p.b) * rcp_fast(p.c + p.d); }
 
 // Absolute angular accelerations of this lane's links j = lane L + t (t < L) of a k-link chain;
 // links past the chain are padding and read as zero angles and rates.
@@ -168,7 +177,7 @@ RLENV_D void coop_aba_accel(const float (&th)[L], const float (&om)[L], float to
       root_a00 = a00;
       root_a01 = a01;
     }
-    r[t] = 1.0f / a00;
+    r[t] = rcp_fast(a00);
     u1[t] = a01 * r[t];
     const float w = om[t], x = vx[t], y = vy[t];
     c1[t] = qd[t] * y;
