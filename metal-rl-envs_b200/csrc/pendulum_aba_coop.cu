@@ -114,10 +114,9 @@ RLENV_D void coop_aba_accel(const float (&th)[L], const float (&om)[L], float to
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
       const float u0 = __shfl_up_sync(kWarp, i0, d), u1 = __shfl_up_sync(kWarp, i1, d);
-      if (lane >= d) {
-        i0 += u0;
-        i1 += u1;
-      }
+      const bool in = lane >= d;  // every combine below is computed and selected, not branched
+      i0 += in ? u0 : 0.0f;
+      i1 += in ? u1 : 0.0f;
     }
     float e0 = i0 - s0, e1 = i1 - s1;  // exclusive: the links before this lane
 #pragma unroll
@@ -136,13 +135,15 @@ RLENV_D void coop_aba_accel(const float (&th)[L], const float (&om)[L], float to
 #pragma unroll
     for (int t = 0; t < L; ++t) {
       const int j = j0 + t;
-      if (j >= 1 && j < k) own = mat2_mul(own, Mat2{1.0f, 1.0f, sn[t] * sn[t], 1.0f});
+      const Mat2 next = mat2_mul(own, Mat2{1.0f, 1.0f, sn[t] * sn[t], 1.0f});
+      own = j >= 1 && j < k ? next : own;
     }
     Mat2 sfx = own;  // inclusive suffix over lanes: this lane's links and every later one
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
       const Mat2 later = mat2_shfl_down(sfx, d);
-      if (lane + d < 32) sfx = mat2_mul(sfx, later);
+      const Mat2 both = mat2_mul(sfx, later);
+      sfx = lane + d < 32 ? both : sfx;
     }
     Mat2 after = mat2_shfl_down(sfx, 1);  // the links after this lane
     if (lane == 31) after = mat2_identity();
@@ -150,7 +151,8 @@ RLENV_D void coop_aba_accel(const float (&th)[L], const float (&om)[L], float to
     for (int t = L - 1; t >= 0; --t) {
       const int j = j0 + t;
       m[t] = mat2_ratio(after);
-      if (j >= 1 && j < k) after = mat2_mul(Mat2{1.0f, 1.0f, sn[t] * sn[t], 1.0f}, after);
+      const Mat2 next = mat2_mul(Mat2{1.0f, 1.0f, sn[t] * sn[t], 1.0f}, after);
+      after = j >= 1 && j < k ? next : after;
     }
   }
   // the next link's joint trig and mass (zero joint trig past the chain: no child)
@@ -192,28 +194,25 @@ RLENV_D void coop_aba_accel(const float (&th)[L], const float (&om)[L], float to
     float B = 1.0f, A = 0.0f;
 #pragma unroll
     for (int t = L - 1; t >= 0; --t) {
-      const int j = j0 + t;
-      if (j >= 1 && j < k) {
-        A = fmaf(beta[t], A, alpha[t]);
-        B = beta[t] * B;
-      }
+      const bool in = j0 + t >= 1 && j0 + t < k;  // outside the chain: the identity map
+      A = fmaf(in ? beta[t] : 1.0f, A, in ? alpha[t] : 0.0f);
+      B = (in ? beta[t] : 1.0f) * B;
     }
     float SB = B, SA = A;  // inclusive suffix over lanes
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
       const float lb = __shfl_down_sync(kWarp, SB, d), la = __shfl_down_sync(kWarp, SA, d);
-      if (lane + d < 32) {
-        SA = fmaf(SB, la, SA);
-        SB = SB * lb;
-      }
+      const bool in = lane + d < 32;
+      SA = fmaf(SB, in ? la : 0.0f, SA);
+      SB = SB * (in ? lb : 1.0f);
     }
     float pa = __shfl_down_sync(kWarp, SA, 1);  // pa1 of the next lane's first link
     if (lane == 31) pa = 0.0f;
 #pragma unroll
     for (int t = L - 1; t >= 0; --t) {
-      const int j = j0 + t;
+      const bool in = j0 + t >= 1 && j0 + t < k;
       pa1_next[t] = pa;
-      if (j >= 1 && j < k) pa = fmaf(beta[t], pa, alpha[t]);
+      pa = fmaf(in ? beta[t] : 1.0f, pa, in ? alpha[t] : 0.0f);
     }
   }
   float g[L];
@@ -239,16 +238,16 @@ RLENV_D void coop_aba_accel(const float (&th)[L], const float (&om)[L], float to
 #pragma unroll
     for (int t = 0; t < L; ++t) {
       const int j = j0 + t;
-      if (j >= 1 && j < k) {
-        const Aff2 f{cs[t], sn[t], -u1[t] * cs[t], -u1[t] * sn[t], c1[t], fmaf(-u1[t], c1[t], g[t])};
-        own = aff2_then(own, f);
-      }
+      const Aff2 f{cs[t], sn[t], -u1[t] * cs[t], -u1[t] * sn[t], c1[t], fmaf(-u1[t], c1[t], g[t])};
+      const Aff2 next = aff2_then(own, f);
+      own = j >= 1 && j < k ? next : own;
     }
     Aff2 pre = own;  // inclusive prefix over lanes
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
       const Aff2 earlier = aff2_shfl_up(pre, d);
-      if (lane >= d) pre = aff2_then(earlier, pre);
+      const Aff2 both = aff2_then(earlier, pre);
+      pre = lane >= d ? both : pre;
     }
     Aff2 before = aff2_shfl_up(pre, 1);  // the links before this lane
     if (lane == 0) before = aff2_identity();
