@@ -145,8 +145,8 @@ RLENV_D void coop_aba_accel(const float (&th)[L], const float (&om)[L], float to
       const Mat2 both = mat2_mul(sfx, later);
       sfx = lane + d < 32 ? both : sfx;
     }
-    Mat2 after = mat2_shfl_down(sfx, 1);  // the links after this lane
-    if (lane == 31) after = mat2_identity();
+    const Mat2 next_lanes = mat2_shfl_down(sfx, 1);  // the links after this lane
+    Mat2 after = lane == 31 ? mat2_identity() : next_lanes;
 #pragma unroll
     for (int t = L - 1; t >= 0; --t) {
       const int j = j0 + t;
@@ -206,8 +206,8 @@ RLENV_D void coop_aba_accel(const float (&th)[L], const float (&om)[L], float to
       SA = fmaf(SB, in ? la : 0.0f, SA);
       SB = SB * (in ? lb : 1.0f);
     }
-    float pa = __shfl_down_sync(kWarp, SA, 1);  // pa1 of the next lane's first link
-    if (lane == 31) pa = 0.0f;
+    const float pa_next_lane = __shfl_down_sync(kWarp, SA, 1);  // pa1 of the next lane's first link
+    float pa = lane == 31 ? 0.0f : pa_next_lane;
 #pragma unroll
     for (int t = L - 1; t >= 0; --t) {
       const bool in = j0 + t >= 1 && j0 + t < k;
@@ -219,19 +219,18 @@ RLENV_D void coop_aba_accel(const float (&th)[L], const float (&om)[L], float to
 #pragma unroll
   for (int t = 0; t < L; ++t) g[t] = -fmaf(vx[t], om[t], sn1[t] * pa1_next[t]) * r[t];
   // ---- the root (lane 0's first link), the base accelerating at -G
-  float ax0 = 0.0f, z0 = 0.0f, qdd0 = 0.0f;
-  if (lane == 0) {
-    const float U0 = root_a00, U1_0 = root_a01;
+  // every lane evaluates it on its own first link and lane 0's result is broadcast (no branch)
+  float ax0, z0, qdd0;
+  {
+    const float U0 = root_a00, U1_0 = root_a01;  // U0 = 1 + m_1 s_1^2 >= 1
     const float uu0 = torque - sn1[0] * pa1_next[0];
     const float ax = ca[0] * -pd::G;
     const float ay = -sa[0] * -pd::G;
-    qdd0 = (uu0 - fmaf(U1_0, ax, U0 * ay)) / U0;
-    ax0 = ax;
-    z0 = ay + qdd0;
+    const float q = (uu0 - fmaf(U1_0, ax, U0 * ay)) * rcp_fast(U0);
+    ax0 = __shfl_sync(kWarp, ax, 0);
+    z0 = __shfl_sync(kWarp, ay + q, 0);
+    qdd0 = __shfl_sync(kWarp, q, 0);
   }
-  ax0 = __shfl_sync(kWarp, ax0, 0);
-  z0 = __shfl_sync(kWarp, z0, 0);
-  qdd0 = __shfl_sync(kWarp, qdd0, 0);
   // ---- outward accelerations: (ax, z) through each link's affine map, prefix over the lanes
   {
     Aff2 own = aff2_identity();
@@ -249,8 +248,8 @@ RLENV_D void coop_aba_accel(const float (&th)[L], const float (&om)[L], float to
       const Aff2 both = aff2_then(earlier, pre);
       pre = lane >= d ? both : pre;
     }
-    Aff2 before = aff2_shfl_up(pre, 1);  // the links before this lane
-    if (lane == 0) before = aff2_identity();
+    const Aff2 earlier_lanes = aff2_shfl_up(pre, 1);  // the links before this lane
+    const Aff2 before = lane == 0 ? aff2_identity() : earlier_lanes;
     float ax = fmaf(before.m00, ax0, fmaf(before.m01, z0, before.b0));
     float z = fmaf(before.m10, ax0, fmaf(before.m11, z0, before.b1));
 #pragma unroll
@@ -303,7 +302,7 @@ pendulum_aba_coop_kernel(const float* __restrict__ state, const void* __restrict
     float h = 0.0f;
 #pragma unroll
     for (int u = 0; u < L; ++u)
-      if (lane * L + u < k) h += cos_fast(th[u]);
+      h += lane * L + u < k ? cos_fast(th[u]) : 0.0f;
 #pragma unroll
     for (int d = 16; d >= 1; d >>= 1) h += __shfl_xor_sync(kWarp, h, d);
     const bool dn = -h > float(k) * 0.5f;
