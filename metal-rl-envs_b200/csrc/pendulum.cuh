@@ -135,6 +135,15 @@ RLENV_D void for_links(F&& f) {
   for_range<HI - LO, UNROLL>([&](int t) { f(UP ? LO + t : HI - 1 - t); });
 }
 
+// The hardware reciprocal (rcp.approx.ftz, within one ulp) for the articulated inertias' D = a00
+// and the root's U0, both at least one: the correctly rounded division is a multi-instruction
+// sequence with a slow-path branch.
+RLENV_D float aba_rcp(float a) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
+  return r;
+}
+
 // The three passes fully unrolled, every per-link array in registers (K <= kUnrollLinks).
 //
 // Every link is a unit point mass at (1, 0) of its frame, and every child's joint sits at that
@@ -173,7 +182,7 @@ RLENV_D void aba_accel_unrolled(const float* th, const float* om, float torque, 
     const float p0 = x * w + cp0;
     const float p1 = -w * (w + y) + cp1;
     const float a00 = 1.0f + cI00, a01 = cI01, a11 = 1.0f + cI11;
-    const float r = 1.0f / a00;  // D = a00
+    const float r = aba_rcp(a00);  // D = a00 >= 1
     const float g = -p0 * r;     // u / D, u = -p0
     const float u1 = a01 * r;
     const float m = a11 - a01 * u1;
@@ -202,7 +211,7 @@ RLENV_D void aba_accel_unrolled(const float* th, const float* om, float torque, 
   // root: X_0 maps the base acceleration (0, -G, 0)
   float ax = cs0 * -pd::G;
   float ay = -sn0 * -pd::G;
-  const float qdd = (uu0 - (U1_0 * ax + U0_0 * ay)) / U0_0;
+  const float qdd = (uu0 - (U1_0 * ax + U0_0 * ay)) * aba_rcp(U0_0);
   float aw = qdd;
   float run = qdd;
   acc[0] = run;
