@@ -84,8 +84,11 @@ RLENV_D void mm_accel(const float (&th)[K], const float (&om)[K], float torque, 
     rhs[i] = -r - (pd::G * float(K - i)) * s[i];
   }
   rhs[0] += torque;
-  // Cholesky in place with the reciprocals of the diagonal, then forward and
-  // back substitution: K divisions instead of K (K + 3) / 2.
+  // Cholesky in place with the reciprocals of the diagonal, then forward and back
+  // substitution. The diagonal itself is needed only through its reciprocal, which the
+  // hardware's reciprocal square root gives directly from the pivot (rsqrt.approx, within two
+  // ulp; the pivots of this positive definite matrix are far from zero): no square root and no
+  // division, each a multi-instruction sequence with a slow path.
   float inv_d[K];
 #pragma unroll
   for (int i = 0; i < K; ++i) {
@@ -95,8 +98,7 @@ RLENV_D void mm_accel(const float (&th)[K], const float (&om)[K], float torque, 
 #pragma unroll
       for (int p = 0; p < j; ++p) v -= L[tri(i, p)] * L[tri(j, p)];
       if (i == j) {
-        L[tri(i, i)] = sqrtf(v);
-        inv_d[i] = 1.0f / L[tri(i, i)];
+        asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(inv_d[i]) : "f"(v));
       } else {
         L[tri(i, j)] = v * inv_d[j];
       }
