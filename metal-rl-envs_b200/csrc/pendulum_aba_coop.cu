@@ -15,8 +15,8 @@
 //  - the outward accelerations keep two numbers per link, ax and z = ay + aw, and
 //    (ax, z) -> (c ax + s z + c1, g - U1 (c ax + s z + c1)) is affine: a prefix scan of 2 x 2
 //    affine maps; each link's absolute angular acceleration is z - ay.
-// The scan form equals the sequential recurrences in exact arithmetic (checked in float64
-// against the oracle's articulated body to 1e-13 for K = 1..64); in float32 the sums are
+// The scan form equals the sequential recurrences in exact arithmetic (tests/test_aba_scan_form.py
+// restates it in float64 and checks it against the oracle's articulated body); in float32 the sums are
 // associated differently, so it agrees with the one-thread kernels to rounding, not bit for bit.
 #include "pendulum_kernels.cuh"
 
