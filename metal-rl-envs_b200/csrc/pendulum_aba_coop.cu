@@ -1,7 +1,8 @@
-// The articulated-body pendulum with one warp per environment: the warp-cooperative form for
-// batches too small to fill the GPU with one thread per environment (BASELINE's N = 256
-// configurations). Lane l owns links l L .. l L + L - 1 (L = 1, 2, 4 or 6 for K up to 32, 64,
-// 128, 192). The algorithm is the rank-one articulated body of pendulum.cuh (aba_accel_unrolled;
+// The articulated-body pendulum with a warp, or a segment of one, per environment: the
+// warp-cooperative form for batches too small to fill the GPU with one thread per environment
+// (BASELINE's N = 256 configurations). Up to 32 links, an environment takes a segment of the next
+// power of two of lanes, one link each (a warp holds 32 / SEG environments); above, a whole warp,
+// lane l owning links l L .. l L + L - 1 (L = 2, 4 or 6 for K up to 64, 128, 192). The algorithm is the rank-one articulated body of pendulum.cuh (aba_accel_unrolled;
 // pendulum_aba_np.py:30-99), with every recurrence along the chain written as a scan over the
 // lanes, so a derivative evaluation takes a few levels of shuffles instead of K dependent steps:
 //  - link velocities: in the world frame the velocity of link i's joint is the exclusive prefix
@@ -49,9 +50,10 @@ RLENV_D Aff2 aff2_then(const Aff2& f, const Aff2& g) {
               fmaf(g.m00, f.b0, fmaf(g.m01, f.b1, g.b0)), fmaf(g.m10, f.b0, fmaf(g.m11, f.b1, g.b1))};
 }
 
-RLENV_D Aff2 aff2_shfl_up(const Aff2& a, int d) {
-  return Aff2{__shfl_up_sync(kWarp, a.m00, d), __shfl_up_sync(kWarp, a.m01, d), __shfl_up_sync(kWarp, a.m10, d),
-              __shfl_up_sync(kWarp, a.m11, d), __shfl_up_sync(kWarp, a.b0, d), __shfl_up_sync(kWarp, a.b1, d)};
+RLENV_D Aff2 aff2_shfl_up(const Aff2& a, int d, int w) {
+  return Aff2{__shfl_up_sync(kWarp, a.m00, d, w), __shfl_up_sync(kWarp, a.m01, d, w),
+              __shfl_up_sync(kWarp, a.m10, d, w), __shfl_up_sync(kWarp, a.m11, d, w),
+              __shfl_up_sync(kWarp, a.b0, d, w), __shfl_up_sync(kWarp, a.b1, d, w)};
 }
 
 // a 2 x 2 matrix with non-negative entries, kept near unit size (its action on a ratio does not
@@ -69,24 +71,26 @@ RLENV_D Mat2 mat2_mul(const Mat2& p, const Mat2& q) {
   return Mat2{r.a * sc, r.b * sc, r.c * sc, r.d * sc};
 }
 
-RLENV_D Mat2 mat2_shfl_down(const Mat2& p, int d) {
-  return Mat2{__shfl_down_sync(kWarp, p.a, d), __shfl_down_sync(kWarp, p.b, d), __shfl_down_sync(kWarp, p.c, d),
-              __shfl_down_sync(kWarp, p.d, d)};
+RLENV_D Mat2 mat2_shfl_down(const Mat2& p, int d, int w) {
+  return Mat2{__shfl_down_sync(kWarp, p.a, d, w), __shfl_down_sync(kWarp, p.b, d, w),
+              __shfl_down_sync(kWarp, p.c, d, w), __shfl_down_sync(kWarp, p.d, d, w)};
 }
 
 // the ratio a subtree's product hands on: P applied to (1, 1)
 RLENV_D float mat2_ratio(const Mat2& p) { return (p.a + p.b) * rcp_fast(p.c + p.d); }
 
-// Absolute angular accelerations of this lane's links j = lane L + t (t < L) of a k-link chain;
-// links past the chain are padding and read as zero angles and rates.
-template <int L>
+// Absolute angular accelerations of this lane's links j = lane L + t (t < L) of a k-link chain,
+// lane being the lane's place in its environment's segment of SEG lanes (SEG a power of two up to
+// 32: every scan and shuffle stays inside the segment); links past the chain are padding and
+// read as zero angles and rates.
+template <int L, int SEG>
 RLENV_D void coop_aba_accel(const float (&th)[L], const float (&om)[L], float torque, int k, int lane,
                             float (&acc)[L]) {
   const int j0 = lane * L;
   // joint (relative) trig and rates, absolute trig; the previous link of the lane's first link is
   // the last link of the lane before
-  const float th_prev = __shfl_up_sync(kWarp, th[L - 1], 1);
-  const float om_prev = __shfl_up_sync(kWarp, om[L - 1], 1);
+  const float th_prev = __shfl_up_sync(kWarp, th[L - 1], 1, SEG);
+  const float om_prev = __shfl_up_sync(kWarp, om[L - 1], 1, SEG);
   float sn[L], cs[L], sa[L], ca[L], qd[L];
 #pragma unroll
   for (int t = 0; t < L; ++t) {
@@ -112,8 +116,8 @@ RLENV_D void coop_aba_accel(const float (&th)[L], const float (&om)[L], float to
     }
     float i0 = s0, i1 = s1;  // inclusive over lanes
 #pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      const float u0 = __shfl_up_sync(kWarp, i0, d), u1 = __shfl_up_sync(kWarp, i1, d);
+    for (int d = 1; d < SEG; d <<= 1) {
+      const float u0 = __shfl_up_sync(kWarp, i0, d, SEG), u1 = __shfl_up_sync(kWarp, i1, d, SEG);
       const bool in = lane >= d;  // every combine below is computed and selected, not branched
       i0 += in ? u0 : 0.0f;
       i1 += in ? u1 : 0.0f;
@@ -140,13 +144,13 @@ RLENV_D void coop_aba_accel(const float (&th)[L], const float (&om)[L], float to
     }
     Mat2 sfx = own;  // inclusive suffix over lanes: this lane's links and every later one
 #pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      const Mat2 later = mat2_shfl_down(sfx, d);
+    for (int d = 1; d < SEG; d <<= 1) {
+      const Mat2 later = mat2_shfl_down(sfx, d, SEG);
       const Mat2 both = mat2_mul(sfx, later);
-      sfx = lane + d < 32 ? both : sfx;
+      sfx = lane + d < SEG ? both : sfx;
     }
-    const Mat2 next_lanes = mat2_shfl_down(sfx, 1);  // the links after this lane
-    Mat2 after = lane == 31 ? mat2_identity() : next_lanes;
+    const Mat2 next_lanes = mat2_shfl_down(sfx, 1, SEG);  // the links after this lane
+    Mat2 after = lane == SEG - 1 ? mat2_identity() : next_lanes;
 #pragma unroll
     for (int t = L - 1; t >= 0; --t) {
       const int j = j0 + t;
@@ -158,14 +162,14 @@ RLENV_D void coop_aba_accel(const float (&th)[L], const float (&om)[L], float to
   // the next link's joint trig and mass (zero joint trig past the chain: no child)
   float sn1[L], cs1[L], m1[L];
   {
-    const float sn_next = __shfl_down_sync(kWarp, sn[0], 1), cs_next = __shfl_down_sync(kWarp, cs[0], 1);
-    const float m_next = __shfl_down_sync(kWarp, m[0], 1);
+    const float sn_next = __shfl_down_sync(kWarp, sn[0], 1, SEG), cs_next = __shfl_down_sync(kWarp, cs[0], 1, SEG);
+    const float m_next = __shfl_down_sync(kWarp, m[0], 1, SEG);
 #pragma unroll
     for (int t = 0; t < L; ++t) {
       const bool last = t == L - 1;
-      sn1[t] = last ? (lane == 31 ? 0.0f : sn_next) : sn[t + 1];
-      cs1[t] = last ? (lane == 31 ? 0.0f : cs_next) : cs[t + 1];
-      m1[t] = last ? (lane == 31 ? 0.0f : m_next) : m[t + 1];
+      sn1[t] = last ? (lane == SEG - 1 ? 0.0f : sn_next) : sn[t + 1];
+      cs1[t] = last ? (lane == SEG - 1 ? 0.0f : cs_next) : cs[t + 1];
+      m1[t] = last ? (lane == SEG - 1 ? 0.0f : m_next) : m[t + 1];
     }
   }
   // ---- per link: the articulated inertia seen from its joint and the velocity-product terms
@@ -200,14 +204,14 @@ RLENV_D void coop_aba_accel(const float (&th)[L], const float (&om)[L], float to
     }
     float SB = B, SA = A;  // inclusive suffix over lanes
 #pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      const float lb = __shfl_down_sync(kWarp, SB, d), la = __shfl_down_sync(kWarp, SA, d);
-      const bool in = lane + d < 32;
+    for (int d = 1; d < SEG; d <<= 1) {
+      const float lb = __shfl_down_sync(kWarp, SB, d, SEG), la = __shfl_down_sync(kWarp, SA, d, SEG);
+      const bool in = lane + d < SEG;
       SA = fmaf(SB, in ? la : 0.0f, SA);
       SB = SB * (in ? lb : 1.0f);
     }
-    const float pa_next_lane = __shfl_down_sync(kWarp, SA, 1);  // pa1 of the next lane's first link
-    float pa = lane == 31 ? 0.0f : pa_next_lane;
+    const float pa_next_lane = __shfl_down_sync(kWarp, SA, 1, SEG);  // pa1 of the next lane's first link
+    float pa = lane == SEG - 1 ? 0.0f : pa_next_lane;
 #pragma unroll
     for (int t = L - 1; t >= 0; --t) {
       const bool in = j0 + t >= 1 && j0 + t < k;
@@ -227,9 +231,9 @@ RLENV_D void coop_aba_accel(const float (&th)[L], const float (&om)[L], float to
     const float ax = ca[0] * -pd::G;
     const float ay = -sa[0] * -pd::G;
     const float q = (uu0 - fmaf(U1_0, ax, U0 * ay)) * rcp_fast(U0);
-    ax0 = __shfl_sync(kWarp, ax, 0);
-    z0 = __shfl_sync(kWarp, ay + q, 0);
-    qdd0 = __shfl_sync(kWarp, q, 0);
+    ax0 = __shfl_sync(kWarp, ax, 0, SEG);
+    z0 = __shfl_sync(kWarp, ay + q, 0, SEG);
+    qdd0 = __shfl_sync(kWarp, q, 0, SEG);
   }
   // ---- outward accelerations: (ax, z) through each link's affine map, prefix over the lanes
   {
@@ -243,12 +247,12 @@ RLENV_D void coop_aba_accel(const float (&th)[L], const float (&om)[L], float to
     }
     Aff2 pre = own;  // inclusive prefix over lanes
 #pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      const Aff2 earlier = aff2_shfl_up(pre, d);
+    for (int d = 1; d < SEG; d <<= 1) {
+      const Aff2 earlier = aff2_shfl_up(pre, d, SEG);
       const Aff2 both = aff2_then(earlier, pre);
       pre = lane >= d ? both : pre;
     }
-    const Aff2 earlier_lanes = aff2_shfl_up(pre, 1);  // the links before this lane
+    const Aff2 earlier_lanes = aff2_shfl_up(pre, 1, SEG);  // the links before this lane
     const Aff2 before = lane == 0 ? aff2_identity() : earlier_lanes;
     float ax = fmaf(before.m00, ax0, fmaf(before.m01, z0, before.b0));
     float z = fmaf(before.m10, ax0, fmaf(before.m11, z0, before.b1));
@@ -270,19 +274,23 @@ RLENV_D void coop_aba_accel(const float (&th)[L], const float (&om)[L], float to
   }
 }
 
-// T steps of N environments, one warp per environment (four per block), the lane's links' state
-// in registers between steps; step t reads actions[t * n + e], draws its resets from seed0 + t
-// and writes reward_seq / done_seq row t when those are not null. One step is the launch with
-// T = 1, so a chain of single steps and one T-step launch agree bit for bit.
-template <int L>
+// T steps of N environments, a segment of SEG lanes per environment (a warp holds 32 / SEG of
+// them; blocks of 128 threads), the lane's links' state in registers between steps; step t reads
+// actions[t * n + e], draws its resets from seed0 + t and writes reward_seq / done_seq row t when
+// those are not null. One step is the launch with T = 1, so a chain of single steps and one
+// T-step launch agree bit for bit. Segments past the last environment mirror it (every lane of a
+// warp takes part in its shuffles) and store nothing.
+template <int L, int SEG>
 __global__ void __launch_bounds__(128)
 pendulum_aba_coop_kernel(const float* __restrict__ state, const void* __restrict__ actions, int dtype,
                          uint32_t seed0, int k, int64_t T, int64_t n, int64_t off, float* __restrict__ next,
                          float* __restrict__ reward_seq, uint8_t* __restrict__ done_seq) {
-  const int lane = int(threadIdx.x) & 31;
-  const int64_t e_raw = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  if (e_raw >= n) return;  // whole warps: the environment is per warp
-  const int64_t e = e_raw;
+  const int64_t gt = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if ((gt & ~int64_t(31)) / SEG >= n) return;  // a whole warp past the batch
+  const int lane = int(threadIdx.x) & (SEG - 1);
+  const int64_t e_raw = gt / SEG;
+  const bool valid = e_raw < n;
+  const int64_t e = valid ? e_raw : n - 1;
   float th[L], om[L];
 #pragma unroll
   for (int t = 0; t < L; ++t) {
@@ -296,15 +304,15 @@ pendulum_aba_coop_kernel(const float* __restrict__ state, const void* __restrict
     const float torque = float(act - 1) * pd::TORQUE;
     if (t + 1 < T) act = action_at(actions, dtype, (t + 1) * n + e);
     pendulum_rk4<L, true>(th, om, torque, [&](const float (&a_t)[L], const float (&a_o)[L], float tq, float (&a)[L]) {
-      coop_aba_accel<L>(a_t, a_o, tq, k, lane, a);
+      coop_aba_accel<L, SEG>(a_t, a_o, tq, k, lane, a);
     });
-    // the tip above half the chain's length: -sum cos th > k / 2, summed over the warp
+    // the tip above half the chain's length: -sum cos th > k / 2, summed over the segment
     float h = 0.0f;
 #pragma unroll
     for (int u = 0; u < L; ++u)
       h += lane * L + u < k ? cos_fast(th[u]) : 0.0f;
 #pragma unroll
-    for (int d = 16; d >= 1; d >>= 1) h += __shfl_xor_sync(kWarp, h, d);
+    for (int d = SEG / 2; d >= 1; d >>= 1) h += __shfl_xor_sync(kWarp, h, d, SEG);
     const bool dn = -h > float(k) * 0.5f;
     if (dn) {
       const uint32_t hs = env_hash(seed0 + uint32_t(t), off + e);
@@ -317,11 +325,12 @@ pendulum_aba_coop_kernel(const float* __restrict__ state, const void* __restrict
         }
       }
     }
-    if (lane == 0) {
+    if (lane == 0 && valid) {
       if (reward_seq) reward_seq[t * n + e] = dn ? 0.0f : -1.0f;
       if (done_seq) done_seq[t * n + e] = dn;
     }
   }
+  if (!valid) return;
 #pragma unroll
   for (int u = 0; u < L; ++u) {
     const int j = lane * L + u;
@@ -333,28 +342,33 @@ pendulum_aba_coop_kernel(const float* __restrict__ state, const void* __restrict
   }
 }
 
+template <int L, int SEG>
+int launch_seg(int k, const float* state, const void* actions, int dtype, uint32_t seed0, int64_t T, int64_t n,
+               int64_t off, float* next, float* reward_seq, uint8_t* done_seq, cudaStream_t s) {
+  const int64_t threads = n * SEG;
+  const unsigned blocks = unsigned((threads + 127) / 128);
+  pendulum_aba_coop_kernel<L, SEG><<<blocks, 128, 0, s>>>(state, actions, dtype, seed0, k, T, n, off, next,
+                                                          reward_seq, done_seq);
+  return launch_status();
+}
+
 }  // namespace
 
 int launch_aba_coop(int k, const float* state, const void* actions, int dtype, uint32_t seed0, int64_t T,
                     int64_t n, int64_t off, float* next, float* reward_seq, uint8_t* done_seq, void* stream) {
   if (k < 1 || k > kCoopAbaMaxLinks) return RLENV_EUNSUPPORTED;
-  const int64_t threads = n * 32;
-  const unsigned blocks = unsigned((threads + 127) / 128);
   cudaStream_t s = as_stream(stream);
-  if (k <= 32) {
-    pendulum_aba_coop_kernel<1><<<blocks, 128, 0, s>>>(state, actions, dtype, seed0, k, T, n, off, next, reward_seq,
-                                                       done_seq);
-  } else if (k <= 64) {
-    pendulum_aba_coop_kernel<2><<<blocks, 128, 0, s>>>(state, actions, dtype, seed0, k, T, n, off, next, reward_seq,
-                                                       done_seq);
-  } else if (k <= 128) {
-    pendulum_aba_coop_kernel<4><<<blocks, 128, 0, s>>>(state, actions, dtype, seed0, k, T, n, off, next, reward_seq,
-                                                       done_seq);
-  } else {
-    pendulum_aba_coop_kernel<6><<<blocks, 128, 0, s>>>(state, actions, dtype, seed0, k, T, n, off, next, reward_seq,
-                                                       done_seq);
-  }
-  return launch_status();
+  // one link per lane in a segment of the next power of two up to 32 lanes, then a whole warp
+  // with 2, 4 or 6 links per lane
+  if (k <= 1) return launch_seg<1, 1>(k, state, actions, dtype, seed0, T, n, off, next, reward_seq, done_seq, s);
+  if (k <= 2) return launch_seg<1, 2>(k, state, actions, dtype, seed0, T, n, off, next, reward_seq, done_seq, s);
+  if (k <= 4) return launch_seg<1, 4>(k, state, actions, dtype, seed0, T, n, off, next, reward_seq, done_seq, s);
+  if (k <= 8) return launch_seg<1, 8>(k, state, actions, dtype, seed0, T, n, off, next, reward_seq, done_seq, s);
+  if (k <= 16) return launch_seg<1, 16>(k, state, actions, dtype, seed0, T, n, off, next, reward_seq, done_seq, s);
+  if (k <= 32) return launch_seg<1, 32>(k, state, actions, dtype, seed0, T, n, off, next, reward_seq, done_seq, s);
+  if (k <= 64) return launch_seg<2, 32>(k, state, actions, dtype, seed0, T, n, off, next, reward_seq, done_seq, s);
+  if (k <= 128) return launch_seg<4, 32>(k, state, actions, dtype, seed0, T, n, off, next, reward_seq, done_seq, s);
+  return launch_seg<6, 32>(k, state, actions, dtype, seed0, T, n, off, next, reward_seq, done_seq, s);
 }
 
 }  // namespace pend

@@ -63,6 +63,22 @@ def test_cooperative_articulated_body_matches_oracle_at_every_width(cuda, k):
     check_step(f"pendulum_aba_coop_k{k}", (nxt, rew[0], done[0]), stepped, odone, onext, rtol, atol)
 
 
+@pytest.mark.parametrize("k,n", [(1, 5), (2, 17), (3, 13), (5, 11), (16, 7), (16, 1), (31, 3)])
+def test_cooperative_articulated_body_ragged_batches(cuda, k, n):
+    """Up to 32 links an environment takes a segment of the next power of two of lanes, so a warp
+    holds several; batches that leave the last warp part empty (its spare segments mirror the
+    last environment and store nothing) against the oracle, with a shard offset."""
+    r = np.random.default_rng(700 + k + n)
+    st = np.concatenate([r.uniform(-np.pi, np.pi, (k, n)), r.uniform(-1, 1, (k, n))]).astype(np.float32)
+    ac = r.integers(0, 3, n)
+    st_t = torch.from_numpy(st).to(cuda)
+    nxt, rew, done = coop_steps(k, st_t, torch.from_numpy(ac).to(cuda)[None], 52, index_offset=9)
+    onext, _, odone, stepped = kernels.pendulum_step(st, ac, 52, k, form="aba", index_offset=9)
+    rtol, atol = _tol(k)
+    check_step(f"pendulum_aba_coop_ragged_k{k}_n{n}", (nxt, rew[0], done[0]), stepped, odone, onext, rtol, atol)
+    assert torch.equal(st_t, torch.from_numpy(st).to(cuda))  # the input is not written
+
+
 @pytest.mark.parametrize("k", [20, 64, 150])
 def test_cooperative_articulated_body_trajectory(cuda, k):
     """50 chained steps against the oracle's chain with the same resets: done flags equal and
