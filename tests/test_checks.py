@@ -139,3 +139,55 @@ def test_check_build_flags_in_the_tensor_memory_kernel(cuda):
     nan = ps.clone()
     nan[3, 7] = float("nan")
     assert step(nan, ok)[1] & 2
+
+
+@pytest.mark.gpu
+def test_check_build_flags_packed_actions_and_the_one_warp_pendulum(cuda):
+    """Packed actions (RLENV_U2) can hold 3, outside both classic bodies' ranges: the T-step
+    kernels flag it on the step that reads it, at one and at four environments per thread
+    (CartPole from N = 4 x 32 x 32 x SMs). The one-warp articulated body (every K above 64)
+    flags a bad action and a non-finite state as the other forms do."""
+    import torch
+
+    import rlenv_lib
+
+    lib = _load("librlenv_checks.so")
+    sp = torch.cuda.current_stream(cuda).cuda_stream
+    assert _status(lib)[0] == 0
+    r = np.random.default_rng(3)
+    for n in (33, 4 * 32 * 32 * torch.cuda.get_device_properties(0).multi_processor_count):
+        st = torch.from_numpy(r.uniform(-0.05, 0.05, (4, n)).astype(np.float32)).to(cuda)
+        out = torch.empty_like(st)
+        T = 6
+        acts = torch.from_numpy(r.integers(0, 2, (T, n))).to(cuda)
+        for fn in (lib.rlenv_cartpole_step_many, lib.rlenv_acrobot_step_many):
+            for bad in (False, True):
+                a = acts.clone()
+                if bad:
+                    a[5, n - 1] = 3
+                bits = rlenv_lib.pack_actions(a).bits
+                assert fn(st.data_ptr(), bits.data_ptr(), rlenv_lib.U2, 1, T, n, 0, out.data_ptr(), None, None, None,
+                          None, sp) == 0
+                torch.cuda.synchronize()
+                assert _status(lib) == (0, 1 if bad else 0), (n, bad)
+    k, n = 100, 40
+    ps = torch.from_numpy(r.uniform(-0.1, 0.1, (2 * k, n)).astype(np.float32)).to(cuda)
+    po = torch.empty_like(ps)
+    rew = torch.empty(n, device=cuda)
+    dn = torch.empty(n, dtype=torch.uint8, device=cuda)
+
+    def step(state, action):
+        a = torch.from_numpy(np.asarray(action, np.int32)).to(cuda)
+        assert lib.rlenv_pendulum_aba_step(k, state.data_ptr(), a.data_ptr(), 0, 3, n, 0, po.data_ptr(),
+                                           rew.data_ptr(), dn.data_ptr(), sp) == 0
+        torch.cuda.synchronize()
+        return _status(lib)
+
+    ok = r.integers(0, 3, n)
+    assert step(ps, ok) == (0, 0)
+    bad = ok.copy()
+    bad[n - 1] = 4
+    assert step(ps, bad) == (0, 1)
+    nan = ps.clone()
+    nan[k + 50, 3] = float("nan")
+    assert step(nan, ok) == (0, 2)
